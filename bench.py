@@ -1,0 +1,488 @@
+"""Benchmark: paged MLA decode serving step on 1..N GPUs.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...   (one process per GPU)
+
+Workload (config 5): 512 concurrent sequences, lengths log-uniform in
+[128, 65536] (seeded), 8 layers, Q8_0 paged KV with block size 64, 20 heads,
+576-wide latent rows N(0,1) with 1% x20 outliers.  Sequences are sharded
+across ranks by greedy LPT on their token counts; each GPU owns its pool.
+A step appends one token per sequence per layer and runs decode attention on
+every layer.  No collective runs inside the timed region.
+
+Printed JSON (rank 0): value = ctx-tokens/s of the whole job (sum over ranks of
+the context tokens attended, / max-over-ranks device time); `e2e` = the same
+through the host-buffer API (kvcache_append_batch / kvcache_mla_decode with
+pinned host buffers, copies inside); `roofline` for the decode kernel (HBM,
+algorithmic bytes = 612 B per context token + q + out + tables); the CPU
+oracle timed on a bounded sample as `cpu_baseline`.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "mobile-moe.zig_b200"))
+
+R, P, W, H = 512, 64, 576, 20
+N_SEQS, N_LAYERS, BS = 512, 8, 64
+LEN_LO, LEN_HI = 128, 65536
+SEED = 5
+OUTLIER_P = 0.01
+SCALE = float(np.float32(1.0 / math.sqrt(192.0)))
+Q8_ROW_BYTES = 18 * 34  # 612
+METRIC = "paged MLA decode ctx-tokens/s (config 5 serving step, Q8_0 KV)"
+UNIT = "ctx-tokens/s"
+
+
+def config5_lengths(seed=SEED, n=N_SEQS):
+    rng = np.random.default_rng(seed)
+    u = rng.uniform(math.log(LEN_LO), math.log(LEN_HI), n)
+    return np.minimum(np.floor(np.exp(u)).astype(np.int64), LEN_HI)
+
+
+def lpt_partition(lens, n_parts):
+    """Greedy LPT: longest sequence first to the least-loaded part."""
+    order = np.argsort(-lens, kind="stable")
+    loads = [0] * n_parts
+    parts = [[] for _ in range(n_parts)]
+    for s in order:
+        k = min(range(n_parts), key=lambda i: (loads[i], i))
+        parts[k].append(int(s))
+        loads[k] += int(lens[s])
+    return [sorted(p) for p in parts], loads
+
+
+def read_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def read_traffic_profile():
+    """Per-context-token DRAM bytes of the decode kernel from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "decode_config5_ncu.md")
+    try:
+        for line in open(path):
+            if line.startswith("dram_bytes_per_ctx_token:"):
+                return float(line.split(":", 1)[1].split()[0])
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index):
+        self.dev = device_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.dev)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.t.join(timeout=5)
+
+    def summary(self):
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for name, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ CPU baseline (oracle)
+def cpu_sample(n_threads, target_tokens, seed=SEED):
+    """A bounded sample of the config-5 workload for the CPU restatement:
+    sequences drawn from the same length distribution, one layer, Q8_0."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import kvoracle
+
+    lens_all = config5_lengths(seed + 1000, 4096)
+    lens, tot = [], 0
+    for L in lens_all:
+        if tot >= target_tokens:
+            break
+        lens.append(int(L))
+        tot += int(L)
+    nb = sum((L + BS - 1) // BS for L in lens)
+    pool = kvoracle.Pool(1, nb, BS, R, P, True)
+    offs, tabs, k = [0], [], 0
+    for s, L in enumerate(lens):
+        need = (L + BS - 1) // BS
+        tabs.extend(range(k, k + need))
+        k += need
+        offs.append(len(tabs))
+        rows = kvoracle.gen_rows(seed, 0, np.full(L, s, np.uint32), np.arange(L, dtype=np.uint32), W,
+                                 OUTLIER_P, n_threads=n_threads)
+        t = np.arange(L)
+        pool.put_rows(0, np.array(tabs[offs[s]:offs[s + 1]], np.uint32)[t // BS], t % BS, rows)
+    q = np.random.default_rng(seed).standard_normal((len(lens), H, W)).astype(np.float32)
+    return pool, np.array(offs, np.uint32), np.array(tabs, np.uint32), np.array(lens, np.uint32), q
+
+
+def cpu_time(sample, n_threads):
+    pool, offs, tabs, lens, q = sample
+    t0 = time.perf_counter()
+    pool.attention_batch(0, offs, tabs, lens, q, SCALE, n_threads=n_threads)
+    return time.perf_counter() - t0, int(lens.sum())
+
+
+def host_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return 0
+    cores = host_cores()
+    sample = cpu_sample(cores, args.cpu_sample_tokens)
+    for _ in range(args.warmup):
+        cpu_time(sample, cores)
+    dt, toks = 0.0, 0
+    for _ in range(args.steps):
+        d, t = cpu_time(sample, cores)
+        dt += d
+        toks += t
+    value = toks / dt
+    desc = (f"one layer of {len(sample[3])} sequences drawn from the config-5 length distribution "
+            f"({int(sample[3].sum())} ctx tokens, 20 heads, Q8_0), oracle C restatement of "
+            f"src/inference.zig:572-660 on a pthread mutex/cond FIFO pool (src/thread_pool.zig)")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,1), 1% x20 outliers)",
+        "config": {"workload": "config5_sharded_serving_step (bounded CPU sample)",
+                   "sample": desc},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": desc},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the Zig reference cannot be built here (no zig toolchain); its CPU path is timed "
+                "through the C restatement in oracle/",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------ GPU arm
+APPEND_ROWS = 1 << 17
+
+
+def measure_append(kvcu, torch, dev, local_rank, reps=5):
+    """Append GB/s on one prefill-sized batch: APPEND_ROWS f32 rows (302 MB,
+    larger than L2) quantized into a fresh Q8_0 pool through a block table."""
+    nb = APPEND_ROWS // BS
+    pool = kvcu.DevicePool(local_rank, 1, nb, BS, R, P, True)
+    rows = torch.randn((APPEND_ROWS, W), dtype=torch.float32, device=dev)
+    seq = torch.zeros(APPEND_ROWS, dtype=torch.int32, device=dev)
+    pos = torch.arange(APPEND_ROWS, dtype=torch.int32, device=dev)
+    toff = torch.tensor([0, nb], dtype=torch.int32, device=dev)
+    tables = torch.randperm(nb, device=dev).to(torch.int32)
+    st = torch.cuda.current_stream(dev)
+    pool.append(0, rows, seq, pos, toff, tables, stream=st)  # warm-up
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(reps):
+        pool.append(0, rows, seq, pos, toff, tables, stream=st)
+    e1.record(st)
+    torch.cuda.synchronize(dev)
+    dt = e0.elapsed_time(e1) / 1e3 / reps
+    status = pool.status()
+    pool.close()
+    if status:
+        raise RuntimeError(f"append benchmark hit device status {status:#x}")
+    return APPEND_ROWS * (2304 + Q8_ROW_BYTES + 8) / dt / 1e9
+
+
+def physical_gpu(local_rank):
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = [x.strip() for x in vis.split(",") if x.strip()]
+        if local_rank < len(ids):
+            return ids[local_rank]
+    return str(local_rank)
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    import kvcu
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    kvcu.init(local_rank)
+    lens_all = config5_lengths()
+    parts, loads = lpt_partition(lens_all, world)
+    mine = np.array(parts[rank], np.int64)
+    lens0 = lens_all[mine]
+    n = mine.size
+    total_steps = args.warmup + args.steps + args.e2e_warmup + args.e2e_steps
+    nb = int(sum((int(L) + total_steps + BS - 1) // BS for L in lens0)) + 8
+    cache = kvcu.KVCache.with_blocks(N_LAYERS, R, P, nb, BS, quantized=True, device=local_rank)
+    for _ in range(n - 1):
+        cache.seq_create()
+    ids = np.arange(n, dtype=np.uint32)
+    for i in range(n):
+        cache.seq_ensure_capacity(i, int(lens0[i]) + total_steps)
+    # ---- prefill (device generator + batched append); also the large-append measurement
+    t_pre = time.perf_counter()
+    for layer in range(N_LAYERS):
+        cache.prefill_synthetic(layer, ids, lens0, SEED, OUTLIER_P, seq_tags=mine)
+    torch.cuda.synchronize()
+    t_pre = time.perf_counter() - t_pre
+
+    st = torch.cuda.Stream(device=dev)
+    W_steps = args.warmup + args.steps
+    # per-step inputs, resident in HBM before timing
+    with torch.cuda.stream(st):
+        pos_dev = torch.empty((total_steps, n), dtype=torch.int32, device=dev)
+        for k in range(total_steps):
+            pos_dev[k] = torch.from_numpy((lens0 + k).astype(np.int32)).to(dev)
+        ids_dev = torch.from_numpy(ids.astype(np.int32)).to(dev)
+        tags_dev = torch.from_numpy(mine.astype(np.int32)).to(dev)
+        rows = torch.empty((W_steps, N_LAYERS, n, W), dtype=torch.float32, device=dev)
+        for k in range(W_steps):
+            for layer in range(N_LAYERS):
+                kvcu.synth_rows(SEED, layer, tags_dev, pos_dev[k], W, rows[k, layer], OUTLIER_P, st)
+        qs = torch.empty((N_LAYERS, n, H, W), dtype=torch.float32, device=dev)
+        qtag = (mine.astype(np.int64) * 64)[:, None] + np.arange(H)[None, :]
+        qb = torch.from_numpy(qtag.reshape(-1).astype(np.int32)).to(dev)
+        qc = torch.zeros(n * H, dtype=torch.int32, device=dev)
+        for layer in range(N_LAYERS):
+            kvcu.synth_rows(SEED + 1, 100 + layer, qb, qc, W, qs[layer].view(n * H, W), 0.0, st)
+        outs = torch.empty((N_LAYERS, n, H, R), dtype=torch.float32, device=dev)
+    st.synchronize()
+
+    ev = {"dec": [], "launches": 0}
+
+    def step(k, timed):
+        pos_h = (lens0 + k).astype(np.uint32)
+        for layer in range(N_LAYERS):
+            cache.appendBatch_dev(layer, ids, pos_h, ids_dev, pos_dev[k], rows[k, layer], st)
+            ev["launches"] += cache.last_launches
+            if timed:
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record(st)
+            cache.mlaDecode_dev(layer, ids, qs[layer], SCALE, outs[layer], st)
+            ev["launches"] += cache.last_launches
+            if timed:
+                e1.record(st)
+                ev["dec"].append((e0, e1, layer))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for k in range(args.warmup):
+        step(k, False)
+    st.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    ev["launches"] = 0
+    ctx_tokens = 0
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(physical_gpu(local_rank)) as clk:
+        t_start.record(st)
+        for k in range(args.warmup, args.warmup + args.steps):
+            step(k, True)
+            ctx_tokens += int((lens0 + k + 1).sum()) * N_LAYERS
+        t_end.record(st)
+        st.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    elapsed = t_start.elapsed_time(t_end) / 1e3
+    launches = ev["launches"]
+    # decode kernel roofline (per launch = one layer's decode)
+    dec_ms = [e0.elapsed_time(e1) for e0, e1, _ in ev["dec"]]
+    avg_dec = sum(dec_ms) / len(dec_ms) / 1e3
+    avg_ctx_per_launch = ctx_tokens / len(dec_ms)
+    tables_bytes = 4 * sum((int(L) + BS - 1) // BS for L in lens0)
+    dec_bytes = (avg_ctx_per_launch * Q8_ROW_BYTES + n * H * W * 4 + n * H * R * 4 + tables_bytes)
+
+    # ---- cross-rank aggregation (outside the timed region)
+    tot = torch.tensor([float(ctx_tokens), elapsed, dec_bytes / avg_dec], dtype=torch.float64, device=dev)
+    if world > 1:
+        tmax = tot.clone()
+        dist.all_reduce(tot, op=dist.ReduceOp.SUM)
+        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+        job_tokens, job_time = tot[0].item(), tmax[1].item()
+        dec_gbs = tot[2].item() / world
+    else:
+        job_tokens, job_time = ctx_tokens, elapsed
+        dec_gbs = dec_bytes / avg_dec
+    value = job_tokens / job_time
+
+    # ---- e2e through the host-buffer API (pinned host memory, copies inside)
+    q_host = qs.cpu().pin_memory()
+    out_host = torch.empty((N_LAYERS, n, H, R), dtype=torch.float32).pin_memory()
+    rows_host = torch.empty((N_LAYERS, n, W), dtype=torch.float32).pin_memory()
+    rows_host.copy_(rows[0])  # same distribution; content does not change the work
+    base = W_steps
+
+    def e2e_step(k):
+        pos_h = (lens0 + base + k).astype(np.uint32)
+        for layer in range(N_LAYERS):
+            cache.appendBatch(layer, ids, pos_h, rows_host[layer].numpy())
+            cache.mlaDecode_ptr(layer, n, ids, q_host[layer].data_ptr(), H, SCALE, out_host[layer].data_ptr())
+            _ = out_host[layer, 0, 0, 0].item()
+
+    for k in range(args.e2e_warmup):
+        e2e_step(k)
+    barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    e2e_tokens = 0
+    for k in range(args.e2e_warmup, args.e2e_warmup + args.e2e_steps):
+        e2e_step(k)
+        e2e_tokens += int((lens0 + base + k + 1).sum()) * N_LAYERS
+    torch.cuda.synchronize()
+    e2e_time = time.perf_counter() - t0
+    e = torch.tensor([float(e2e_tokens), e2e_time], dtype=torch.float64, device=dev)
+    if world > 1:
+        emax = e.clone()
+        dist.all_reduce(e, op=dist.ReduceOp.SUM)
+        dist.all_reduce(emax, op=dist.ReduceOp.MAX)
+        e2e_value = e[0].item() / emax[1].item()
+    else:
+        e2e_value = e2e_tokens / e2e_time
+    h2d = N_LAYERS * n * (W * 4 + 8 + H * W * 4)
+    d2h = N_LAYERS * n * H * R * 4
+
+    append_gbs = measure_append(kvcu, torch, dev, local_rank)
+    clk_sum = clk.summary()
+
+    peak, peak_kind = read_peaks()
+    traffic_per_tok = read_traffic_profile()
+    if rank == 0:
+        cores = host_cores()
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            sample = cpu_sample(cores, args.cpu_sample_tokens)
+            dt, toks = cpu_time(sample, cores)
+            cpu = {"value": toks / dt, "unit": UNIT, "cores": cores, "kind": "port",
+                   "sample": f"one layer, {len(sample[3])} sequences from the config-5 length "
+                             f"distribution ({toks} ctx tokens, 20 heads, Q8_0); oracle C "
+                             f"restatement on a pthread FIFO pool, {cores} threads"}
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1e3 * job_time / args.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded N(0,1) rows with 1% x20 outliers, random q)",
+            "config": {"workload": "config5_sharded_serving_step", "n_seqs": N_SEQS,
+                       "layers": N_LAYERS, "block_size": BS, "heads": H, "kv_rank": R, "rope_dim": P,
+                       "kv_dtype": "q8_0", "lengths": f"log-uniform[{LEN_LO},{LEN_HI}] seed {SEED}",
+                       "ctx_tokens_per_step": int(job_tokens / args.steps),
+                       "parallelism": f"sequence-sharded x{world} (LPT by tokens), no collective",
+                       "shard_tokens": loads, "l2": "inputs larger than L2 (>=0.4 GB of KV per layer per GPU)"},
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "roofline": {"kernel": "mla_decode (k_decode + k_combine), one layer per launch",
+                         "bound": "hbm", "achieved": dec_gbs, "peak": peak, "unit": "GB/s",
+                         "frac": dec_gbs / peak, "peak_source": peak_kind,
+                         "traffic": (traffic_per_tok * avg_ctx_per_launch if traffic_per_tok else None),
+                         "algorithmic_bytes_per_launch": dec_bytes,
+                         "avg_launch_ms": avg_dec * 1e3},
+            "gpu_launches": launches,
+            "clocks": clk_sum,
+            "append": {"GB/s": append_gbs, "rows": APPEND_ROWS,
+                       "bytes_per_row": 2304 + Q8_ROW_BYTES + 8,
+                       "what": "one batched f32->Q8_0 append through the block table (prefill-sized)"},
+            "prefill_s": t_pre,
+        }
+        if cpu:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    cache.close()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--e2e-warmup", type=int, default=1)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-sample-tokens", type=int, default=400_000)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        return run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    sys.exit(main())

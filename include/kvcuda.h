@@ -1,0 +1,276 @@
+/*
+ * kvcuda.h — C-ABI of libkvcuda.so, the B200 (sm_100a) paged MLA KV-cache
+ * library: Q8_0/f32 token append through a block table, block-table
+ * gather/dequant, paged MLA decode attention, checkpoint I/O.
+ *
+ * It is the drop-in boundary for mobile-moe.zig's KV-cache hot path.  The
+ * reference's host code (Zig) would bind these functions with `extern fn`
+ * declarations exactly as src/metal_backend.zig:7-26 binds src/metal_bridge.c;
+ * INTEGRATION.md shows that binding.  Conventions copied from
+ * src/metal_bridge.c: a process-wide last-error string (:50-52), `int` return
+ * codes (0 = success, negative = error, :54-87), opaque handles with explicit
+ * release (:89-96).  No entry point ever falls back to the CPU: without a
+ * usable CUDA device every call returns an error.
+ *
+ * Two layers:
+ *   kvcu_*     device-level operations on device pointers (what a host
+ *              allocator written in another language drives);
+ *   kvcache_*  a C++ host mirror of src/kv_cache.zig's KVCache (block
+ *              allocator, block_table, put/get, prefix cache, checkpoint)
+ *              extended to many sequences on one pool, taking HOST buffers.
+ *
+ * Device pool layout (per GPU, all layers in one pool):
+ *   f32 pools  : kv [L][NB][BS][kv_rank] f32 and pe [L][NB][BS][rope_dim] f32,
+ *                identical to src/kv_cache.zig:34-37.
+ *   Q8_0 pools : qs [L][NB][BS][nblk*32] int8 and sc [L][NB][BS][nblk] f16 bits,
+ *                nblk = ceil(kv_rank/32) + ceil(rope_dim/32).  Same bytes as
+ *                the reference's BlockQ8_0 pools (src/kv_cache.zig:55-57),
+ *                split into payload and scales; checkpoints convert to the
+ *                reference's 34-byte block order.
+ *
+ * Threading: handles are not re-entrant (as KVCache is not, because of its
+ * shared dequant scratch, src/kv_cache.zig:59-60); use one host thread per GPU.
+ */
+#ifndef KVCUDA_H
+#define KVCUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------- errors */
+/* The first eleven mirror the reference's error set (src/kv_cache.zig). */
+#define KVCU_OK 0
+#define KVCU_ERR_OUT_OF_BLOCKS (-1)        /* error.OutOfKVCacheBlocks   kv_cache.zig:159 */
+#define KVCU_ERR_POSITION_OOB (-2)         /* error.PositionOutOfBounds  kv_cache.zig:221 */
+#define KVCU_ERR_LAYER_OOB (-3)            /* error.LayerOutOfBounds     kv_cache.zig:226 */
+#define KVCU_ERR_POSITION_NOT_WRITTEN (-4) /* error.PositionNotWritten   kv_cache.zig:227 */
+#define KVCU_ERR_PREFIX_MISS (-5)          /* error.PrefixCacheMiss      kv_cache.zig:416 */
+#define KVCU_ERR_BAD_MAGIC (-6)            /* error.InvalidCheckpointMagic kv_cache.zig:509 */
+#define KVCU_ERR_BAD_VERSION (-7)          /* error.UnsupportedCheckpointVersion :510 */
+#define KVCU_ERR_SHAPE_MISMATCH (-8)       /* error.CheckpointShapeMismatch :517 */
+#define KVCU_ERR_EOF (-9)                  /* error.EndOfStream          kv_cache.zig:588 */
+#define KVCU_ERR_IO (-10)                  /* POSIX errors of open/read/write */
+#define KVCU_ERR_INVALID_ARG (-11)
+#define KVCU_ERR_CUDA (-12)                /* a CUDA runtime call failed (see last error) */
+#define KVCU_ERR_DEVICE (-13)              /* a kernel flagged a bad index (status word) */
+#define KVCU_ERR_NO_MEMORY (-14)
+#define KVCU_ERR_BAD_BLOCK_ID (-15)        /* checkpoint names a block id >= num_blocks */
+#define KVCU_ERR_UNSUPPORTED (-16)         /* shape outside what the kernels implement */
+#define KVCU_ERR_NO_DEVICE (-17)
+
+/* Device status-word bits set by kernels instead of trapping. */
+#define KVCU_STATUS_BAD_TABLE 0x1u   /* pos / block_size beyond the sequence's table */
+#define KVCU_STATUS_BAD_BLOCK 0x2u   /* table entry >= num_blocks */
+#define KVCU_STATUS_BAD_SEQ 0x4u     /* sequence id >= n_seqs */
+#define KVCU_STATUS_BAD_LEN 0x8u     /* lens[s] > table length * block_size */
+
+/* metal_get_last_error, src/metal_bridge.c:50-52.  Thread-local. */
+const char* kvcu_get_last_error(void);
+/* metal_init, src/metal_bridge.c:54-87: select a CUDA device, check it is
+ * sm_100 (B200), create its context.  0 on success. */
+int kvcu_init(int device);
+/* Number of visible CUDA devices (0 without a driver/GPU). */
+int kvcu_device_count(void);
+/* Library version, for the binding to check. */
+uint32_t kvcu_version(void);
+
+/* ------------------------------------------------------------ block pool */
+typedef struct kvcu_pool kvcu_pool;
+
+typedef struct {
+  uint32_t n_layers, num_blocks, block_size, kv_rank, rope_dim;
+  uint32_t quantized;       /* 1: Q8_0 pools, 0: f32 pools */
+  uint32_t nblk;            /* Q8_0 blocks per row */
+  int32_t device;
+  void* kv;                 /* f32 kv pool (NULL when quantized) */
+  void* pe;                 /* f32 pe pool (NULL when quantized) */
+  void* qs;                 /* Q8_0 payload pool (NULL when f32) */
+  void* sc;                 /* Q8_0 scale pool (NULL when f32) */
+  uint64_t pool_bytes;      /* device bytes of the data pools */
+  uint64_t checkpoint_bytes;/* bytes of the pool section of a checkpoint */
+} kvcu_pool_desc;
+
+/* The pool half of KVCache.init + enableQuantization (src/kv_cache.zig:64-122,
+ * :142-154): allocate and zero the physical block pool for all layers on
+ * `device`.  block_size must be a multiple of 16 (the reference's 16, or 64
+ * for long contexts).  NULL on failure. */
+kvcu_pool* kvcu_pool_create(int device, uint32_t n_layers, uint32_t num_blocks,
+                            uint32_t block_size, uint32_t kv_rank, uint32_t rope_dim,
+                            int quantized);
+/* metal_release analogue (src/metal_bridge.c:94-96); KVCache.deinit's frees
+ * (src/kv_cache.zig:124-139). */
+int kvcu_pool_destroy(kvcu_pool* pool);
+int kvcu_pool_describe(const kvcu_pool* pool, kvcu_pool_desc* out);
+/* Zero every pool byte (stream-ordered). */
+int kvcu_pool_zero(kvcu_pool* pool, void* stream);
+/* Read and clear the device status word (synchronises `stream`). */
+int kvcu_pool_status(kvcu_pool* pool, uint32_t* status_out, void* stream);
+
+/* ------------------------------------------------------------ append / gather
+ * Sequences are described by device arrays indexed by sequence id s:
+ *   table_offsets[s] .. table_offsets[s+1]  its slice of `tables` (CSR),
+ *   tables[...]                              physical block ids, logical order.
+ */
+
+/* KVCache.put batched (src/kv_cache.zig:279-361; callers inference.zig:516,733):
+ * for every row r < n_rows, quantize (Q8_0 pool) or copy (f32 pool) the row
+ * latent[r*latent_stride .. +kv_rank] ++ rope[r*rope_stride .. +rope_dim] into
+ * (layer, tables[table_offsets[row_seq[r]] + row_pos[r]/BS], row_pos[r]%BS).
+ * Q8_0 bytes equal the reference's bit for bit.  If `lens` is not NULL it is
+ * updated as the reference updates `len` (src/kv_cache.zig:358-360):
+ * lens[s] = max(lens[s], pos + 1).  All pointers are device pointers; bad ids
+ * set the status word and skip the row.  Stream-ordered. */
+int kvcu_append(kvcu_pool* pool, uint32_t layer, uint32_t n_rows, const float* latent,
+                uint64_t latent_stride, const float* rope, uint64_t rope_stride,
+                const uint32_t* row_seq, const uint32_t* row_pos, uint32_t n_seqs,
+                const uint32_t* table_offsets, const uint32_t* tables, uint32_t* lens,
+                void* stream);
+
+/* getKVCompressed + getKPe for every position of a sequence
+ * (src/kv_cache.zig:225-277): out[len][kv_rank + rope_dim] f32, dequantized
+ * exactly as f16ToF32(d) * q.  `table` is a device pointer to `table_len` ids. */
+int kvcu_gather(kvcu_pool* pool, uint32_t layer, const uint32_t* table, uint32_t table_len,
+                uint32_t len, float* out, void* stream);
+
+/* Batched gather: rows r < n_rows, out[r][kv_rank + rope_dim] = row (row_seq[r], row_pos[r]). */
+int kvcu_gather_rows(kvcu_pool* pool, uint32_t layer, uint32_t n_rows, const uint32_t* row_seq,
+                     const uint32_t* row_pos, uint32_t n_seqs, const uint32_t* table_offsets,
+                     const uint32_t* tables, float* out, void* stream);
+
+/* ------------------------------------------------------------ MLA decode
+ * The attention core of InferenceEngine.mlaAttention (src/inference.zig:518-660)
+ * in absorbed form: for batch entry b (sequence s = seq_ids ? seq_ids[b] : b,
+ * length lens[s]) and head h,
+ *   score_p = scale * (q[b][h][0:R] . latent_p + q[b][h][R:R+P] . rope_p)
+ *   out[b][h][0:R] = sum_p softmax(score)_p * latent_p   (0 when lens[s] == 0)
+ * over positions p < lens[s] read through the block table.  R = kv_rank = 512,
+ * P = rope_dim = 64, n_heads <= 32.  q: [n][n_heads][R+P] f32, out: [n][n_heads][R]
+ * f32, device pointers.  Long sequences are split across CTAs (split-KV); the
+ * partial results live in the workspace and are combined by a second kernel. */
+typedef struct kvcu_decode_ws kvcu_decode_ws;
+
+/* Workspace for up to max_batch entries of up to max_heads heads. */
+kvcu_decode_ws* kvcu_decode_ws_create(int device, uint32_t max_batch, uint32_t max_heads);
+int kvcu_decode_ws_destroy(kvcu_decode_ws* ws);
+/* Split the batch into work items from the device lengths (one small kernel,
+ * stream-ordered).  Each sequence's last item is open-ended, so a plan stays
+ * valid while appends grow the sequences (re-plan when the batch changes or
+ * sequences shrink); all layers of a step share it. */
+int kvcu_decode_plan(kvcu_decode_ws* ws, const kvcu_pool* pool, uint32_t n, const uint32_t* seq_ids,
+                     uint32_t n_seqs, const uint32_t* lens, void* stream);
+/* Run decode for one layer with the last plan of `ws`. */
+int kvcu_mla_decode(kvcu_decode_ws* ws, kvcu_pool* pool, uint32_t layer, uint32_t n,
+                    const uint32_t* seq_ids, uint32_t n_seqs, const uint32_t* table_offsets,
+                    const uint32_t* tables, const uint32_t* lens, const float* q,
+                    uint32_t n_heads, float scale, float* out, void* stream);
+/* Kernel launches the last kvcu_mla_decode issued (for launch accounting). */
+uint32_t kvcu_decode_last_launches(const kvcu_decode_ws* ws);
+
+/* ------------------------------------------------------------ checkpoint I/O
+ * Bytes of the pool section of a v1 checkpoint in the reference's order
+ * (src/kv_cache.zig:484-492): Q8_0 -> all [rows][ceil(kv_rank/32)] 34-byte
+ * blocks, then all [rows][ceil(rope_dim/32)]; f32 -> kv pool then pe pool.
+ * Copy out / in the byte range [offset, offset+nbytes) of that section through
+ * a host buffer (synchronous on `stream`). */
+int kvcu_pool_read_checkpoint(kvcu_pool* pool, uint64_t offset, uint64_t nbytes, void* host_dst,
+                              void* stream);
+int kvcu_pool_write_checkpoint(kvcu_pool* pool, uint64_t offset, uint64_t nbytes,
+                               const void* host_src, void* stream);
+
+/* ------------------------------------------------------------ synthetic inputs
+ * Seeded counter-based N(0,1) generator used by the benchmarks and tests:
+ * out[r*width + i] = normal(seed, a, b[r], c[r]*1024 + i), with probability
+ * outlier_p multiplied by 20.  b, c, out are device pointers. */
+int kvcu_synth_rows(uint64_t seed, uint64_t a, uint32_t n_rows, const uint32_t* b,
+                    const uint32_t* c, uint32_t width, float outlier_p, float* out, void* stream);
+
+/* =============================================================== kvcache_*
+ * Host mirror of src/kv_cache.zig's KVCache over one kvcu_pool, extended to
+ * many sequences sharing the pool (sequence 0 is the reference's single
+ * sequence).  Block allocator, refcounts, free list, block tables and the
+ * prefix-cache hash map live on the host exactly as in the reference; data
+ * lives on the device.  Buffers are HOST pointers unless a name ends in _dev.
+ */
+typedef struct kvcache kvcache;
+
+/* KVCache.init (src/kv_cache.zig:64-122): num_blocks = ceil(max_seq_len/BS). */
+kvcache* kvcache_init(int device, uint32_t n_layers, uint32_t kv_rank, uint32_t rope_dim,
+                      uint32_t max_seq_len, uint32_t block_size);
+/* Same with an explicit block count (a pool shared by many sequences). */
+kvcache* kvcache_init_blocks(int device, uint32_t n_layers, uint32_t kv_rank, uint32_t rope_dim,
+                             uint32_t num_blocks, uint32_t block_size, int quantized);
+void kvcache_deinit(kvcache* c);                               /* :124-139 */
+int kvcache_enable_quantization(kvcache* c);                   /* :142-154 */
+int kvcache_ensure_capacity(kvcache* c, uint32_t n_tokens);    /* :188-194 */
+void kvcache_truncate(kvcache* c, uint32_t n_tokens);          /* :197-206 */
+void kvcache_reset(kvcache* c);                                /* :209-215 */
+int kvcache_put(kvcache* c, uint32_t layer, uint32_t pos, const float* kv_comp,
+                const float* k_pe);                            /* :279-361 */
+int kvcache_get_kv_compressed(kvcache* c, uint32_t layer, uint32_t pos, float* out); /* :225-250 */
+int kvcache_get_kpe(kvcache* c, uint32_t layer, uint32_t pos, float* out);           /* :252-277 */
+uint32_t kvcache_len(const kvcache* c);
+uint32_t kvcache_num_blocks(const kvcache* c);
+uint32_t kvcache_block_size(const kvcache* c);
+int kvcache_quantized(const kvcache* c);
+uint32_t kvcache_num_free_blocks(const kvcache* c);            /* :446-448 */
+uint64_t kvcache_memory_usage(const kvcache* c);               /* :439-443 */
+uint32_t kvcache_block_table(const kvcache* c, uint32_t* out, uint32_t cap);
+uint32_t kvcache_refcount(const kvcache* c, uint32_t block_id);
+/* Overwrite the free list (LIFO: the last id is handed out first), e.g. to
+ * shuffle the allocation order. */
+int kvcache_set_free_list(kvcache* c, const uint32_t* ids, uint32_t n);
+kvcu_pool* kvcache_pool(kvcache* c);
+int kvcache_save_to_file(kvcache* c, const char* path);       /* :453-494 */
+int kvcache_load_from_file(kvcache* c, const char* path);     /* :497-546 */
+/* Prefix caching (src/kv_cache.zig:367-436, hash :596-609). */
+void kvcache_cache_block(kvcache* c, uint32_t block_idx, const uint32_t* token_ids,
+                         uint32_t n_tokens, uint64_t prefix_hash);
+uint32_t kvcache_find_prefix_blocks(kvcache* c, const uint32_t* tokens, uint32_t n);
+int kvcache_reuse_prefix_blocks(kvcache* c, const uint32_t* tokens, uint32_t n, uint32_t n_blocks);
+uint64_t kvcache_compute_hash(const uint32_t* token_ids, uint32_t n, uint64_t prefix_hash);
+
+/* ---- many sequences on one pool (sequence 0 always exists) ---- */
+/* New empty sequence; returns its id or a negative error. */
+int64_t kvcache_seq_create(kvcache* c);
+uint32_t kvcache_num_seqs(const kvcache* c);
+int kvcache_seq_ensure_capacity(kvcache* c, uint32_t seq, uint32_t n_tokens);
+int kvcache_seq_truncate(kvcache* c, uint32_t seq, uint32_t n_tokens);
+int kvcache_seq_reset(kvcache* c, uint32_t seq);
+uint32_t kvcache_seq_len(const kvcache* c, uint32_t seq);
+uint32_t kvcache_seq_block_table(const kvcache* c, uint32_t seq, uint32_t* out, uint32_t cap);
+/* appendBatch: rows[r] = latent ++ rope ([n][kv_rank+rope_dim] f32) for
+ * (seq_ids[r], positions[r]); the positions must lie inside each sequence's
+ * capacity.  Sets len = max(len, pos+1).  `rows` is a HOST pointer; the
+ * _dev variant takes device pointers for rows, seq_ids and positions (the
+ * host copies of seq_ids/positions are still needed for the length update). */
+int kvcache_append_batch(kvcache* c, uint32_t layer, uint32_t n, const uint32_t* seq_ids,
+                         const uint32_t* positions, const float* rows);
+int kvcache_append_batch_dev(kvcache* c, uint32_t layer, uint32_t n, const uint32_t* seq_ids,
+                             const uint32_t* positions, const uint32_t* seq_ids_dev,
+                             const uint32_t* positions_dev, const float* rows_dev, void* stream);
+/* gather(layer, seq): out[len][kv_rank + rope_dim] (HOST buffer). */
+int kvcache_gather(kvcache* c, uint32_t layer, uint32_t seq, float* out);
+/* mlaDecode (the call replacing src/inference.zig:518-660): HOST q
+ * [n][n_heads][R+P] and out [n][n_heads][R]; copies in and out inside. */
+int kvcache_mla_decode(kvcache* c, uint32_t layer, uint32_t n, const uint32_t* seq_ids,
+                       const float* q, uint32_t n_heads, float scale, float* out);
+/* Device variant: q/out device pointers, no host copies; plans once per step
+ * (a plan is reused until a sequence length or the batch changes). */
+int kvcache_mla_decode_dev(kvcache* c, uint32_t layer, uint32_t n, const uint32_t* seq_ids,
+                           const float* q_dev, uint32_t n_heads, float scale, float* out_dev,
+                           void* stream);
+/* Launches issued by the last kvcache_* data call (for launch accounting). */
+uint32_t kvcache_last_launches(const kvcache* c);
+/* Multi-sequence checkpoint (v2: header, per-sequence lengths and tables,
+ * pool).  Single-sequence caches use kvcache_save_to_file (v1, byte-exact). */
+int kvcache_save_to_file_v2(kvcache* c, const char* path);
+int kvcache_load_from_file_v2(kvcache* c, const char* path);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* KVCUDA_H */

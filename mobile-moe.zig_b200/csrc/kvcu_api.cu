@@ -1,0 +1,450 @@
+// kvcu_api.cu — the kvcu_* C-ABI (include/kvcuda.h): device selection, pool
+// lifetime, the append / gather / decode entry points and checkpoint
+// repacking.  Modelled on src/metal_bridge.c: a last-error string, integer
+// return codes, opaque handles with explicit release.  There is no CPU path:
+// every entry point either runs CUDA work or returns an error.
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
+#include <new>
+
+#include "kvcu_internal.h"
+
+#define KVCU_VERSION 0x00010000u
+
+static thread_local char g_last_error[512] = {0};
+
+void kvcu_set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+}
+
+int kvcu_check_cuda(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return KVCU_OK;
+  kvcu_set_error("%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+  if (e == cudaErrorMemoryAllocation) return KVCU_ERR_NO_MEMORY;
+  if (e == cudaErrorNoDevice || e == cudaErrorInsufficientDriver) return KVCU_ERR_NO_DEVICE;
+  return KVCU_ERR_CUDA;
+}
+
+namespace {
+
+// Make `device` current for the duration of a call, restoring the caller's.
+struct DeviceGuard {
+  int prev = -1;
+  int rc = KVCU_OK;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    if (prev != dev) rc = kvcu_check_cuda(cudaSetDevice(dev), "cudaSetDevice");
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+bool valid_pool(const kvcu_pool* p) { return p != nullptr && (p->kv || p->qs); }
+
+uint64_t checkpoint_bytes(const kvcu_pool* p) {
+  if (p->quantized) return p->rows() * (uint64_t)(p->nbk + p->nbp) * 34u;
+  return p->rows() * (uint64_t)(p->kv_rank + p->rope_dim) * 4u;
+}
+
+constexpr uint64_t kStagingBytes = 64ull << 20;
+
+}  // namespace
+
+extern "C" {
+
+const char* kvcu_get_last_error(void) { return g_last_error; }
+
+uint32_t kvcu_version(void) { return KVCU_VERSION; }
+
+int kvcu_device_count(void) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
+int kvcu_init(int device) {
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess || n == 0) {
+    cudaGetLastError();
+    kvcu_set_error("kvcu_init: no CUDA device (%s)", cudaGetErrorString(e));
+    return KVCU_ERR_NO_DEVICE;
+  }
+  if (device < 0 || device >= n) {
+    kvcu_set_error("kvcu_init: device %d out of range [0, %d)", device, n);
+    return KVCU_ERR_INVALID_ARG;
+  }
+  cudaDeviceProp prop;
+  KVCU_CUDA(cudaGetDeviceProperties(&prop, device));
+  if (prop.major != 10) {
+    kvcu_set_error("kvcu_init: device %d is sm_%d%d; this library is built for sm_100a (B200)",
+                   device, prop.major, prop.minor);
+    return KVCU_ERR_UNSUPPORTED;
+  }
+  DeviceGuard g(device);
+  if (g.rc) return g.rc;
+  KVCU_CUDA(cudaFree(nullptr));  // create the primary context
+  return KVCU_OK;
+}
+
+kvcu_pool* kvcu_pool_create(int device, uint32_t n_layers, uint32_t num_blocks,
+                            uint32_t block_size, uint32_t kv_rank, uint32_t rope_dim,
+                            int quantized) {
+  if (!n_layers || !num_blocks || !kv_rank || !rope_dim || block_size == 0 || block_size % 16 ||
+      block_size > 1024) {
+    kvcu_set_error("kvcu_pool_create: bad shape L=%u NB=%u BS=%u R=%u P=%u (BS must be a "
+                   "multiple of 16, <= 1024)",
+                   n_layers, num_blocks, block_size, kv_rank, rope_dim);
+    return nullptr;
+  }
+  if (kvcu_init(device) != KVCU_OK) return nullptr;
+  DeviceGuard g(device);
+  if (g.rc) return nullptr;
+  kvcu_pool* p = new (std::nothrow) kvcu_pool();
+  if (!p) return nullptr;
+  memset(p, 0, sizeof(*p));
+  p->device = device;
+  p->n_layers = n_layers;
+  p->num_blocks = num_blocks;
+  p->block_size = block_size;
+  p->kv_rank = kv_rank;
+  p->rope_dim = rope_dim;
+  p->quantized = quantized ? 1u : 0u;
+  p->nbk = (kv_rank + 31) / 32;
+  p->nbp = (rope_dim + 31) / 32;
+  p->nblk = p->nbk + p->nbp;
+  const uint64_t rows = p->rows();
+  int rc = KVCU_OK;
+  if (p->quantized) {
+    rc = kvcu_check_cuda(cudaMalloc(&p->qs, rows * 32ull * p->nblk), "cudaMalloc(qs)");
+    if (!rc) rc = kvcu_check_cuda(cudaMalloc(&p->sc, rows * 2ull * p->nblk), "cudaMalloc(sc)");
+  } else {
+    rc = kvcu_check_cuda(cudaMalloc(&p->kv, rows * 4ull * kv_rank), "cudaMalloc(kv)");
+    if (!rc) rc = kvcu_check_cuda(cudaMalloc(&p->pe, rows * 4ull * rope_dim), "cudaMalloc(pe)");
+  }
+  if (!rc) rc = kvcu_check_cuda(cudaMalloc(&p->status, sizeof(uint32_t)), "cudaMalloc(status)");
+  if (!rc) rc = kvcu_pool_zero(p, nullptr);
+  if (!rc) rc = kvcu_check_cuda(cudaDeviceSynchronize(), "pool zeroing");
+  if (rc) {
+    kvcu_pool_destroy(p);
+    return nullptr;
+  }
+  return p;
+}
+
+int kvcu_pool_destroy(kvcu_pool* p) {
+  if (!p) return KVCU_OK;
+  DeviceGuard g(p->device);
+  cudaFree(p->kv);
+  cudaFree(p->pe);
+  cudaFree(p->qs);
+  cudaFree(p->sc);
+  cudaFree(p->status);
+  cudaFree(p->staging);
+  delete p;
+  return KVCU_OK;
+}
+
+int kvcu_pool_describe(const kvcu_pool* p, kvcu_pool_desc* out) {
+  if (!valid_pool(p) || !out) return KVCU_ERR_INVALID_ARG;
+  out->n_layers = p->n_layers;
+  out->num_blocks = p->num_blocks;
+  out->block_size = p->block_size;
+  out->kv_rank = p->kv_rank;
+  out->rope_dim = p->rope_dim;
+  out->quantized = p->quantized;
+  out->nblk = p->nblk;
+  out->device = p->device;
+  out->kv = p->kv;
+  out->pe = p->pe;
+  out->qs = p->qs;
+  out->sc = p->sc;
+  out->pool_bytes = p->quantized ? p->rows() * 34ull * p->nblk
+                                 : p->rows() * 4ull * (p->kv_rank + p->rope_dim);
+  out->checkpoint_bytes = checkpoint_bytes(p);
+  return KVCU_OK;
+}
+
+int kvcu_pool_zero(kvcu_pool* p, void* stream) {
+  if (!valid_pool(p)) return KVCU_ERR_INVALID_ARG;
+  DeviceGuard g(p->device);
+  if (g.rc) return g.rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  const uint64_t rows = p->rows();
+  if (p->quantized) {
+    KVCU_CUDA(cudaMemsetAsync(p->qs, 0, rows * 32ull * p->nblk, st));
+    KVCU_CUDA(cudaMemsetAsync(p->sc, 0, rows * 2ull * p->nblk, st));
+  } else {
+    KVCU_CUDA(cudaMemsetAsync(p->kv, 0, rows * 4ull * p->kv_rank, st));
+    KVCU_CUDA(cudaMemsetAsync(p->pe, 0, rows * 4ull * p->rope_dim, st));
+  }
+  KVCU_CUDA(cudaMemsetAsync(p->status, 0, sizeof(uint32_t), st));
+  return KVCU_OK;
+}
+
+int kvcu_pool_status(kvcu_pool* p, uint32_t* status_out, void* stream) {
+  if (!valid_pool(p) || !status_out) return KVCU_ERR_INVALID_ARG;
+  DeviceGuard g(p->device);
+  if (g.rc) return g.rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  uint32_t v = 0;
+  KVCU_CUDA(cudaMemcpyAsync(&v, p->status, sizeof(v), cudaMemcpyDeviceToHost, st));
+  KVCU_CUDA(cudaMemsetAsync(p->status, 0, sizeof(uint32_t), st));
+  KVCU_CUDA(cudaStreamSynchronize(st));
+  *status_out = v;
+  return KVCU_OK;
+}
+
+int kvcu_append(kvcu_pool* p, uint32_t layer, uint32_t n_rows, const float* latent,
+                uint64_t latent_stride, const float* rope, uint64_t rope_stride,
+                const uint32_t* row_seq, const uint32_t* row_pos, uint32_t n_seqs,
+                const uint32_t* table_offsets, const uint32_t* tables, uint32_t* lens,
+                void* stream) {
+  if (!valid_pool(p)) return KVCU_ERR_INVALID_ARG;
+  if (layer >= p->n_layers) {
+    kvcu_set_error("kvcu_append: layer %u >= n_layers %u", layer, p->n_layers);
+    return KVCU_ERR_LAYER_OOB;
+  }
+  if (n_rows && (!latent || !rope || !row_seq || !row_pos || !table_offsets || !tables)) {
+    kvcu_set_error("kvcu_append: null pointer argument");
+    return KVCU_ERR_INVALID_ARG;
+  }
+  DeviceGuard g(p->device);
+  if (g.rc) return g.rc;
+  return kvcu_launch_append(p, layer, n_rows, latent, latent_stride, rope, rope_stride, row_seq,
+                            row_pos, n_seqs, table_offsets, tables, lens, (cudaStream_t)stream);
+}
+
+int kvcu_gather(kvcu_pool* p, uint32_t layer, const uint32_t* table, uint32_t table_len,
+                uint32_t len, float* out, void* stream) {
+  if (!valid_pool(p)) return KVCU_ERR_INVALID_ARG;
+  if (layer >= p->n_layers) {
+    kvcu_set_error("kvcu_gather: layer %u >= n_layers %u", layer, p->n_layers);
+    return KVCU_ERR_LAYER_OOB;
+  }
+  if ((uint64_t)len > (uint64_t)table_len * p->block_size) {
+    kvcu_set_error("kvcu_gather: len %u exceeds table capacity %u*%u", len, table_len,
+                   p->block_size);
+    return KVCU_ERR_POSITION_OOB;
+  }
+  if (len && (!table || !out)) return KVCU_ERR_INVALID_ARG;
+  DeviceGuard g(p->device);
+  if (g.rc) return g.rc;
+  return kvcu_launch_gather_rows(p, layer, len, nullptr, nullptr, 0, nullptr, nullptr, table,
+                                 table_len, out, (cudaStream_t)stream);
+}
+
+int kvcu_gather_rows(kvcu_pool* p, uint32_t layer, uint32_t n_rows, const uint32_t* row_seq,
+                     const uint32_t* row_pos, uint32_t n_seqs, const uint32_t* table_offsets,
+                     const uint32_t* tables, float* out, void* stream) {
+  if (!valid_pool(p)) return KVCU_ERR_INVALID_ARG;
+  if (layer >= p->n_layers) return KVCU_ERR_LAYER_OOB;
+  if (n_rows && (!row_seq || !row_pos || !table_offsets || !tables || !out))
+    return KVCU_ERR_INVALID_ARG;
+  DeviceGuard g(p->device);
+  if (g.rc) return g.rc;
+  return kvcu_launch_gather_rows(p, layer, n_rows, row_seq, row_pos, n_seqs, table_offsets,
+                                 tables, nullptr, 0, out, (cudaStream_t)stream);
+}
+
+// ---------------------------------------------------------------- decode
+kvcu_decode_ws* kvcu_decode_ws_create(int device, uint32_t max_batch, uint32_t max_heads) {
+  if (!max_batch || !max_heads || max_heads > 32) {
+    kvcu_set_error("kvcu_decode_ws_create: max_batch=%u max_heads=%u (heads must be 1..32)",
+                   max_batch, max_heads);
+    return nullptr;
+  }
+  if (kvcu_init(device) != KVCU_OK) return nullptr;
+  DeviceGuard g(device);
+  if (g.rc) return nullptr;
+  kvcu_decode_ws* ws = new (std::nothrow) kvcu_decode_ws();
+  if (!ws) return nullptr;
+  memset(ws, 0, sizeof(*ws));
+  ws->device = device;
+  ws->max_batch = max_batch;
+  ws->max_heads = max_heads;
+  int rc = kvcu_decode_setup(ws);
+  // items <= batch + target items (each sequence adds at most one partial item)
+  ws->max_items = max_batch + (uint32_t)ws->decode_ctas * 4u + 1u;
+  const uint64_t mi = ws->max_items;
+  if (!rc) rc = kvcu_check_cuda(cudaMalloc(&ws->items, mi * sizeof(kvcu_item)), "cudaMalloc(items)");
+  if (!rc) rc = kvcu_check_cuda(cudaMalloc(&ws->meta, 4 * sizeof(uint32_t)), "cudaMalloc(meta)");
+  if (!rc) rc = kvcu_check_cuda(cudaMalloc(&ws->seq_first, max_batch * 4ull), "cudaMalloc");
+  if (!rc) rc = kvcu_check_cuda(cudaMalloc(&ws->seq_count, max_batch * 4ull), "cudaMalloc");
+  if (!rc) rc = kvcu_check_cuda(cudaMalloc(&ws->part_o, mi * max_heads * 512ull * 4), "cudaMalloc");
+  if (!rc) rc = kvcu_check_cuda(cudaMalloc(&ws->part_ml, mi * max_heads * 2ull * 4), "cudaMalloc");
+  if (!rc) rc = kvcu_check_cuda(cudaMemset(ws->meta, 0, 4 * sizeof(uint32_t)), "cudaMemset");
+  if (rc) {
+    kvcu_decode_ws_destroy(ws);
+    return nullptr;
+  }
+  return ws;
+}
+
+int kvcu_decode_ws_destroy(kvcu_decode_ws* ws) {
+  if (!ws) return KVCU_OK;
+  DeviceGuard g(ws->device);
+  cudaFree(ws->items);
+  cudaFree(ws->meta);
+  cudaFree(ws->seq_first);
+  cudaFree(ws->seq_count);
+  cudaFree(ws->part_o);
+  cudaFree(ws->part_ml);
+  delete ws;
+  return KVCU_OK;
+}
+
+int kvcu_decode_plan(kvcu_decode_ws* ws, const kvcu_pool* p, uint32_t n, const uint32_t* seq_ids,
+                     uint32_t n_seqs, const uint32_t* lens, void* stream) {
+  if (!ws || !valid_pool(p)) return KVCU_ERR_INVALID_ARG;
+  if (n > ws->max_batch) {
+    kvcu_set_error("kvcu_decode_plan: batch %u exceeds workspace capacity %u", n, ws->max_batch);
+    return KVCU_ERR_INVALID_ARG;
+  }
+  if (ws->device != p->device) return KVCU_ERR_INVALID_ARG;
+  if (n && !lens) return KVCU_ERR_INVALID_ARG;
+  DeviceGuard g(p->device);
+  if (g.rc) return g.rc;
+  return kvcu_launch_plan(ws, p, n, seq_ids, n_seqs, lens, (cudaStream_t)stream);
+}
+
+int kvcu_mla_decode(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint32_t n,
+                    const uint32_t* seq_ids, uint32_t n_seqs, const uint32_t* table_offsets,
+                    const uint32_t* tables, const uint32_t* lens, const float* q,
+                    uint32_t n_heads, float scale, float* out, void* stream) {
+  if (!ws || !valid_pool(p)) return KVCU_ERR_INVALID_ARG;
+  if (ws->device != p->device) return KVCU_ERR_INVALID_ARG;
+  if (layer >= p->n_layers) {
+    kvcu_set_error("kvcu_mla_decode: layer %u >= n_layers %u", layer, p->n_layers);
+    return KVCU_ERR_LAYER_OOB;
+  }
+  if (n && (!table_offsets || !tables || !lens || !q || !out)) return KVCU_ERR_INVALID_ARG;
+  DeviceGuard g(p->device);
+  if (g.rc) return g.rc;
+  return kvcu_launch_decode(ws, p, layer, n, seq_ids, n_seqs, table_offsets, tables, lens, q,
+                            n_heads, scale, out, (cudaStream_t)stream);
+}
+
+uint32_t kvcu_decode_last_launches(const kvcu_decode_ws* ws) { return ws ? ws->last_launches : 0; }
+
+// ---------------------------------------------------------------- checkpoint
+static int ensure_staging(kvcu_pool* p) {
+  if (p->staging) return KVCU_OK;
+  KVCU_CUDA(cudaMalloc(&p->staging, kStagingBytes));
+  p->staging_bytes = kStagingBytes;
+  return KVCU_OK;
+}
+
+// Walk [offset, offset+nbytes) of the checkpoint pool section in chunks.
+// f32: plain copies out of / into the kv and pe pools.  Q8_0: whole 34-byte
+// blocks are (un)packed through the device staging buffer.
+static int checkpoint_io(kvcu_pool* p, uint64_t offset, uint64_t nbytes, uint8_t* host,
+                         bool to_host, cudaStream_t st) {
+  const uint64_t total = checkpoint_bytes(p);
+  if (offset > total || nbytes > total - offset) {
+    kvcu_set_error("checkpoint range [%llu, +%llu) outside the %llu-byte pool section",
+                   (unsigned long long)offset, (unsigned long long)nbytes,
+                   (unsigned long long)total);
+    return KVCU_ERR_INVALID_ARG;
+  }
+  if (!nbytes) return KVCU_OK;
+  if (!p->quantized) {
+    const uint64_t kv_bytes = p->rows() * 4ull * p->kv_rank;
+    uint64_t done = 0;
+    while (done < nbytes) {
+      const uint64_t off = offset + done;
+      uint8_t* dev;
+      uint64_t avail;
+      if (off < kv_bytes) {
+        dev = reinterpret_cast<uint8_t*>(p->kv) + off;
+        avail = kv_bytes - off;
+      } else {
+        dev = reinterpret_cast<uint8_t*>(p->pe) + (off - kv_bytes);
+        avail = total - off;
+      }
+      const uint64_t n = std::min(avail, nbytes - done);
+      if (to_host)
+        KVCU_CUDA(cudaMemcpyAsync(host + done, dev, n, cudaMemcpyDeviceToHost, st));
+      else
+        KVCU_CUDA(cudaMemcpyAsync(dev, host + done, n, cudaMemcpyHostToDevice, st));
+      done += n;
+    }
+    KVCU_CUDA(cudaStreamSynchronize(st));
+    return KVCU_OK;
+  }
+  int rc = ensure_staging(p);
+  if (rc) return rc;
+  const uint64_t part0_blocks = p->rows() * p->nbk;
+  const uint64_t part0_bytes = part0_blocks * 34u;
+  const uint64_t chunk_blocks = p->staging_bytes / 34u;
+  uint64_t done = 0;
+  while (done < nbytes) {
+    const uint64_t off = offset + done;
+    const int part = off < part0_bytes ? 0 : 1;
+    const uint64_t part_off = part == 0 ? off : off - part0_bytes;
+    const uint64_t part_blocks = part == 0 ? part0_blocks : p->rows() * p->nbp;
+    const uint64_t blk0 = part_off / 34u;
+    const uint64_t skip = part_off - blk0 * 34u;  // bytes into the first block
+    const uint64_t part_end = part == 0 ? part0_bytes : total;
+    const uint64_t want = std::min(nbytes - done, part_end - off);
+    uint64_t nblk = std::min((skip + want + 33u) / 34u, chunk_blocks);
+    nblk = std::min(nblk, part_blocks - blk0);
+    const uint64_t n = std::min(want, nblk * 34u - skip);
+    if (to_host) {
+      rc = kvcu_launch_pack_q8(p, part, blk0, nblk, p->staging, st);
+      if (rc) return rc;
+      KVCU_CUDA(cudaMemcpyAsync(host + done, p->staging + skip, n, cudaMemcpyDeviceToHost, st));
+      KVCU_CUDA(cudaStreamSynchronize(st));
+    } else {
+      // partial first/last blocks: read-modify-write through the staging buffer
+      if (skip != 0 || n != nblk * 34u) {
+        rc = kvcu_launch_pack_q8(p, part, blk0, nblk, p->staging, st);
+        if (rc) return rc;
+      }
+      KVCU_CUDA(cudaMemcpyAsync(p->staging + skip, host + done, n, cudaMemcpyHostToDevice, st));
+      rc = kvcu_launch_unpack_q8(p, part, blk0, nblk, p->staging, st);
+      if (rc) return rc;
+      KVCU_CUDA(cudaStreamSynchronize(st));
+    }
+    done += n;
+  }
+  return KVCU_OK;
+}
+
+int kvcu_pool_read_checkpoint(kvcu_pool* p, uint64_t offset, uint64_t nbytes, void* host_dst,
+                              void* stream) {
+  if (!valid_pool(p) || (nbytes && !host_dst)) return KVCU_ERR_INVALID_ARG;
+  DeviceGuard g(p->device);
+  if (g.rc) return g.rc;
+  return checkpoint_io(p, offset, nbytes, static_cast<uint8_t*>(host_dst), true,
+                       (cudaStream_t)stream);
+}
+
+int kvcu_pool_write_checkpoint(kvcu_pool* p, uint64_t offset, uint64_t nbytes,
+                               const void* host_src, void* stream) {
+  if (!valid_pool(p) || (nbytes && !host_src)) return KVCU_ERR_INVALID_ARG;
+  DeviceGuard g(p->device);
+  if (g.rc) return g.rc;
+  return checkpoint_io(p, offset, nbytes, const_cast<uint8_t*>(static_cast<const uint8_t*>(host_src)),
+                       false, (cudaStream_t)stream);
+}
+
+int kvcu_synth_rows(uint64_t seed, uint64_t a, uint32_t n_rows, const uint32_t* b,
+                    const uint32_t* c, uint32_t width, float outlier_p, float* out, void* stream) {
+  if (n_rows && (!b || !c || !out)) return KVCU_ERR_INVALID_ARG;
+  return kvcu_launch_synth(seed, a, n_rows, b, c, width, outlier_p, out, (cudaStream_t)stream);
+}
+
+}  // extern "C"

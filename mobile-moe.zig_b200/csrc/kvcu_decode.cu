@@ -1,0 +1,514 @@
+// kvcu_decode.cu — paged MLA decode attention (split-KV) over the block pool.
+//
+// Restates the attention core of InferenceEngine.mlaAttention
+// (src/inference.zig:518-660) in absorbed form (q is 576 wide, K is the cached
+// latent ++ rope row, V is the latent): online softmax over the sequence's
+// cached positions read through its block table, Q8_0 rows dequantized on the
+// fly exactly as getKVCompressed/getKPe do (src/kv_cache.zig:232-246).
+//
+// Structure (one decode = three stream-ordered launches, or two when the plan
+// is reused across layers):
+//   k_plan      one CTA: splits every sequence into work items of at most C
+//               tokens, C chosen so the item count is ~4 waves of the GPU;
+//   k_decode    persistent CTAs (one per SM) stride over the items; each
+//               streams its KV tile-by-tile through shared memory and keeps
+//               (m, l, o[512]) per head; single-item sequences write the final
+//               output, the others write partials to the workspace;
+//   k_combine   merges the partials of split sequences (log-sum-exp rescale).
+#include <cuda_runtime.h>
+#include <math.h>
+
+#include "kvcu_internal.h"
+#include "kvcu_numeric.cuh"
+
+namespace {
+
+constexpr int R = 512;           // kv_rank (latent, also V width)
+constexpr int P = 64;            // rope_dim
+constexpr int W = R + P;         // K row width
+constexpr int TT = 32;           // tokens per tile
+constexpr int KS = W + 4;        // padded smem row stride (conflict-free float4)
+constexpr int NT = 256;          // threads per CTA
+constexpr int NW = NT / 32;      // warps
+constexpr int KSLICE = W / NW;   // 72 K elements per warp in the QK stage
+constexpr int TARGET_WAVES = 4;  // work items per resident CTA (load balance)
+
+struct DecodeArgs {
+  uint32_t layer, num_blocks, block_size, nblk;
+  const float* kv;
+  const float* pe;
+  const int8_t* qs;
+  const uint16_t* sc;
+  uint32_t* status;
+  uint32_t n;
+  const uint32_t* seq_ids;
+  uint32_t n_seqs;
+  const uint32_t* toff;
+  const uint32_t* tables;
+  const uint32_t* lens;
+  const float* q;
+  uint32_t n_heads;
+  float scale;
+  float* out;
+  const kvcu_item* items;
+  const uint32_t* meta;
+  const uint32_t* seq_count;
+  float* part_o;
+  float* part_ml;
+  uint32_t ws_heads;
+};
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// ------------------------------------------------------------------ plan
+__global__ void __launch_bounds__(1024) k_plan(uint32_t n, const uint32_t* __restrict__ seq_ids,
+                                               uint32_t n_seqs, const uint32_t* __restrict__ lens,
+                                               uint32_t target_items, uint32_t max_items,
+                                               kvcu_item* __restrict__ items,
+                                               uint32_t* __restrict__ meta,
+                                               uint32_t* __restrict__ seq_first,
+                                               uint32_t* __restrict__ seq_count) {
+  __shared__ unsigned long long s_total;
+  __shared__ uint32_t s_warp[32];
+  __shared__ uint32_t s_carry;
+  const uint32_t tid = threadIdx.x, lane = tid & 31u, wid = tid >> 5;
+  if (tid == 0) {
+    s_total = 0;
+    s_carry = 0;
+  }
+  __syncthreads();
+  unsigned long long local = 0;
+  for (uint32_t b = tid; b < n; b += blockDim.x) {
+    const uint32_t s = seq_ids ? seq_ids[b] : b;
+    local += s < n_seqs ? lens[s] : 0u;
+  }
+  atomicAdd(&s_total, local);
+  __syncthreads();
+  const unsigned long long total = s_total;
+  unsigned long long c = (total + target_items - 1) / (target_items ? target_items : 1);
+  c = (c + TT - 1) / TT * TT;
+  if (c < TT) c = TT;
+  if (c > 0x40000000ull) c = 0x40000000ull;
+  const uint32_t C = (uint32_t)c;
+  for (uint32_t base = 0; base < n; base += blockDim.x) {
+    const uint32_t b = base + tid;
+    uint32_t len = 0, cnt = 0;
+    if (b < n) {
+      const uint32_t s = seq_ids ? seq_ids[b] : b;
+      len = s < n_seqs ? lens[s] : 0u;
+      cnt = len ? (len + C - 1) / C : 1u;
+    }
+    // block-wide exclusive scan of cnt
+    uint32_t x = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= (uint32_t)o) x += y;
+    }
+    if (lane == 31) s_warp[wid] = x;
+    __syncthreads();
+    if (wid == 0) {
+      uint32_t w = lane < (blockDim.x >> 5) ? s_warp[lane] : 0u;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xffffffffu, w, o);
+        if (lane >= (uint32_t)o) w += y;
+      }
+      s_warp[lane] = w;  // inclusive per-warp totals
+    }
+    __syncthreads();
+    const uint32_t warp_prefix = wid ? s_warp[wid - 1] : 0u;
+    const uint32_t first = s_carry + warp_prefix + x - cnt;
+    if (b < n) {
+      seq_first[b] = first;
+      seq_count[b] = cnt;
+      for (uint32_t k = 0; k < cnt; ++k) {
+        if (first + k >= max_items) break;
+        kvcu_item it;
+        it.b = b;
+        it.start = k * C;
+        // The last item is open-ended: decode clips it to the live length, so
+        // a plan stays valid while appends grow the sequences.
+        it.end = (k + 1 == cnt) ? 0xFFFFFFFFu : min(len, (k + 1) * C);
+        it.pad = 0;
+        items[first + k] = it;
+      }
+    }
+    __syncthreads();
+    if (tid == 0) s_carry += s_warp[(blockDim.x >> 5) - 1];
+    __syncthreads();
+  }
+  if (tid == 0) {
+    meta[0] = min(s_carry, max_items);
+    meta[1] = C;
+  }
+}
+
+// ------------------------------------------------------------------ decode
+// Resolve the pool row of position `pos` of the sequence with table [t0, t1);
+// -1 (and a status bit) when out of range.
+__device__ __forceinline__ long long pool_row(const DecodeArgs& a, uint32_t t0, uint32_t t1,
+                                              uint32_t pos) {
+  const uint32_t bi = pos / a.block_size;
+  if (bi >= t1 - t0) {
+    atomicOr(a.status, KVCU_STATUS_BAD_TABLE);
+    return -1;
+  }
+  const uint32_t blk = a.tables[t0 + bi];
+  if (blk >= a.num_blocks) {
+    atomicOr(a.status, KVCU_STATUS_BAD_BLOCK);
+    return -1;
+  }
+  return (long long)(((uint64_t)a.layer * a.num_blocks + blk) * a.block_size + pos % a.block_size);
+}
+
+template <bool QUANT, int NH>
+__global__ void __launch_bounds__(NT, 1) k_decode(DecodeArgs a) {
+  extern __shared__ __align__(16) float smem[];
+  float* q_s = smem;                     // [NH][W]
+  float* k_s = q_s + NH * W;             // [TT][KS]
+  float* red = k_s + TT * KS;            // [NW][NH][TT]
+  float* p_s = red + NW * NH * TT;       // [NH][TT]
+  float* m_s = p_s + NH * TT;            // [NH]
+  float* l_s = m_s + NH;                 // [NH]
+  float* c_s = l_s + NH;                 // [NH]
+
+  const uint32_t tid = threadIdx.x, lane = tid & 31u, wid = tid >> 5;
+  constexpr int HH = NH / 2;             // heads per PV thread group
+  const uint32_t c4 = tid & 127u;        // PV: output columns 4*c4 .. +3
+  const uint32_t hg = tid >> 7;          // PV: head group
+  const uint32_t n_items = a.meta[0];
+  const uint32_t H = a.n_heads;
+
+  for (uint32_t it = blockIdx.x; it < n_items; it += gridDim.x) {
+    const kvcu_item item = a.items[it];
+    const uint32_t b = item.b;
+    const uint32_t s = a.seq_ids ? a.seq_ids[b] : b;
+    uint32_t t0 = 0, t1 = 0, len = 0;
+    if (s < a.n_seqs) {
+      t0 = a.toff[s];
+      t1 = a.toff[s + 1];
+      if (t1 < t0) t1 = t0;
+      len = a.lens[s];
+      const uint64_t cap = (uint64_t)(t1 - t0) * a.block_size;
+      if (len > cap) {
+        if (tid == 0) atomicOr(a.status, KVCU_STATUS_BAD_LEN);
+        len = (uint32_t)cap;
+      }
+    } else if (tid == 0) {
+      atomicOr(a.status, KVCU_STATUS_BAD_SEQ);
+    }
+    const uint32_t start = item.start;
+    const uint32_t end = min(item.end, len);
+
+    // q for this batch entry (heads >= H are zero)
+    const float* qb = a.q + (uint64_t)b * H * W;
+    for (uint32_t i = tid; i < NH * (W / 4); i += NT) {
+      const uint32_t h = i / (W / 4), e = i % (W / 4);
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (h < H) v = reinterpret_cast<const float4*>(qb + (uint64_t)h * W)[e];
+      reinterpret_cast<float4*>(q_s + h * W)[e] = v;
+    }
+    if (tid < NH) {
+      m_s[tid] = -INFINITY;
+      l_s[tid] = 0.f;
+    }
+    float acc[HH][4];
+#pragma unroll
+    for (int j = 0; j < HH; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+    __syncthreads();
+
+    for (uint32_t tb = start; tb < end; tb += TT) {
+      const uint32_t tl = min((uint32_t)TT, end - tb);
+      // ---- stage the tile (dequantized) into k_s
+      if (QUANT) {
+        // 16-byte units: 36 per row (32 latent+rope payload halves of 16 B)
+        for (uint32_t u = tid; u < TT * (W / 16); u += NT) {
+          const uint32_t t = u / (W / 16), h16 = u % (W / 16);
+          float* dst = k_s + t * KS + 16 * h16;
+          long long row = -1;
+          if (t < tl) row = pool_row(a, t0, t1, tb + t);
+          if (row < 0) {
+#pragma unroll
+            for (int k = 0; k < 16; k += 4)
+              *reinterpret_cast<float4*>(dst + k) = make_float4(0.f, 0.f, 0.f, 0.f);
+            continue;
+          }
+          const int4 raw =
+              *reinterpret_cast<const int4*>(a.qs + (uint64_t)row * (32u * a.nblk) + 16u * h16);
+          const float d = kvcu::f16_to_f32(a.sc[(uint64_t)row * a.nblk + h16 / 2]);
+          const int8_t* q8 = reinterpret_cast<const int8_t*>(&raw);
+#pragma unroll
+          for (int k = 0; k < 16; k += 4) {
+            float4 v;
+            v.x = d * (float)q8[k + 0];
+            v.y = d * (float)q8[k + 1];
+            v.z = d * (float)q8[k + 2];
+            v.w = d * (float)q8[k + 3];
+            *reinterpret_cast<float4*>(dst + k) = v;
+          }
+        }
+      } else {
+        for (uint32_t u = tid; u < TT * (W / 4); u += NT) {
+          const uint32_t t = u / (W / 4), e4 = u % (W / 4);
+          float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+          long long row = -1;
+          if (t < tl) row = pool_row(a, t0, t1, tb + t);
+          if (row >= 0) {
+            if (e4 < R / 4)
+              v = reinterpret_cast<const float4*>(a.kv + (uint64_t)row * R)[e4];
+            else
+              v = reinterpret_cast<const float4*>(a.pe + (uint64_t)row * P)[e4 - R / 4];
+          }
+          *reinterpret_cast<float4*>(k_s + t * KS + 4 * e4) = v;
+        }
+      }
+      __syncthreads();
+
+      // ---- QK: warp wid covers K elements [72*wid, 72*wid+72); lane = token
+      {
+        float sacc[NH];
+#pragma unroll
+        for (int h = 0; h < NH; ++h) sacc[h] = 0.f;
+        const float* krow = k_s + lane * KS + KSLICE * wid;
+        const float* qcol = q_s + KSLICE * wid;
+#pragma unroll 2
+        for (int i = 0; i < KSLICE; i += 4) {
+          const float4 kv4 = *reinterpret_cast<const float4*>(krow + i);
+#pragma unroll
+          for (int h = 0; h < NH; ++h) {
+            const float4 q4 = *reinterpret_cast<const float4*>(qcol + h * W + i);
+            sacc[h] = fmaf(q4.x, kv4.x, sacc[h]);
+            sacc[h] = fmaf(q4.y, kv4.y, sacc[h]);
+            sacc[h] = fmaf(q4.z, kv4.z, sacc[h]);
+            sacc[h] = fmaf(q4.w, kv4.w, sacc[h]);
+          }
+        }
+#pragma unroll
+        for (int h = 0; h < NH; ++h) red[(wid * NH + h) * TT + lane] = sacc[h];
+      }
+      __syncthreads();
+      for (uint32_t i = tid; i < NH * TT; i += NT) {
+        const uint32_t h = i / TT, t = i % TT;
+        float sum = 0.f;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) sum += red[(w * NH + h) * TT + t];
+        p_s[h * TT + t] = t < tl ? sum * a.scale : -INFINITY;
+      }
+      __syncthreads();
+      // ---- online softmax per head (warp per head)
+      for (uint32_t h = wid; h < (uint32_t)NH; h += NW) {
+        const float sv = p_s[h * TT + lane];
+        const float mt = warp_max(sv);
+        const float m_old = m_s[h];
+        const float m_new = fmaxf(m_old, mt);
+        const float pv = lane < tl ? expf(sv - m_new) : 0.f;
+        const float ls = warp_sum(pv);
+        p_s[h * TT + lane] = pv;
+        if (lane == 0) {
+          const float corr = expf(m_old - m_new);
+          c_s[h] = corr;
+          l_s[h] = l_s[h] * corr + ls;
+          m_s[h] = m_new;
+        }
+      }
+      __syncthreads();
+      // ---- PV: thread owns columns 4*c4..+3 of heads [hg*HH, hg*HH+HH)
+      {
+#pragma unroll
+        for (int j = 0; j < HH; ++j) {
+          const float cr = c_s[hg * HH + j];
+          acc[j][0] *= cr;
+          acc[j][1] *= cr;
+          acc[j][2] *= cr;
+          acc[j][3] *= cr;
+        }
+        for (uint32_t t = 0; t < tl; ++t) {
+          const float4 v4 = *reinterpret_cast<const float4*>(k_s + t * KS + 4 * c4);
+#pragma unroll
+          for (int j = 0; j < HH; ++j) {
+            const float pw = p_s[(hg * HH + j) * TT + t];
+            acc[j][0] = fmaf(pw, v4.x, acc[j][0]);
+            acc[j][1] = fmaf(pw, v4.y, acc[j][1]);
+            acc[j][2] = fmaf(pw, v4.z, acc[j][2]);
+            acc[j][3] = fmaf(pw, v4.w, acc[j][3]);
+          }
+        }
+      }
+      __syncthreads();
+    }
+
+    // ---- epilogue: final output or split partial
+    const bool single = a.seq_count[b] == 1;
+#pragma unroll
+    for (int j = 0; j < HH; ++j) {
+      const uint32_t h = hg * HH + j;
+      if (h >= H) continue;
+      const float m = m_s[h], l = l_s[h];
+      if (single) {
+        const float inv = l > 0.f ? 1.0f / l : 0.f;
+        float4 o = make_float4(acc[j][0] * inv, acc[j][1] * inv, acc[j][2] * inv, acc[j][3] * inv);
+        if (!(l > 0.f)) o = make_float4(0.f, 0.f, 0.f, 0.f);
+        reinterpret_cast<float4*>(a.out + ((uint64_t)b * H + h) * R)[c4] = o;
+      } else {
+        reinterpret_cast<float4*>(a.part_o + ((uint64_t)it * a.ws_heads + h) * R)[c4] =
+            make_float4(acc[j][0], acc[j][1], acc[j][2], acc[j][3]);
+        if (c4 == 0) {
+          a.part_ml[((uint64_t)it * a.ws_heads + h) * 2 + 0] = m;
+          a.part_ml[((uint64_t)it * a.ws_heads + h) * 2 + 1] = l;
+        }
+      }
+    }
+    __syncthreads();  // m_s/l_s/q_s reused by the next item
+  }
+}
+
+// ------------------------------------------------------------------ combine
+// One CTA of 128 threads per (entry, head): merge the entry's partials.
+__global__ void __launch_bounds__(128) k_combine(uint32_t n, uint32_t H, uint32_t ws_heads,
+                                                 const uint32_t* __restrict__ seq_first,
+                                                 const uint32_t* __restrict__ seq_count,
+                                                 const float* __restrict__ part_o,
+                                                 const float* __restrict__ part_ml,
+                                                 float* __restrict__ out) {
+  const uint32_t b = blockIdx.x / H, h = blockIdx.x % H;
+  if (b >= n) return;
+  const uint32_t cnt = seq_count[b];
+  if (cnt <= 1) return;  // written by the decode kernel
+  const uint32_t first = seq_first[b];
+  float m = -INFINITY;
+  for (uint32_t k = 0; k < cnt; ++k) m = fmaxf(m, part_ml[((uint64_t)(first + k) * ws_heads + h) * 2]);
+  float l = 0.f;
+  float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (uint32_t k = 0; k < cnt; ++k) {
+    const uint64_t base = (uint64_t)(first + k) * ws_heads + h;
+    const float mk = part_ml[base * 2], lk = part_ml[base * 2 + 1];
+    const float f = (lk > 0.f) ? expf(mk - m) : 0.f;
+    l += lk * f;
+    const float4 v = reinterpret_cast<const float4*>(part_o + base * R)[threadIdx.x];
+    o.x += v.x * f;
+    o.y += v.y * f;
+    o.z += v.z * f;
+    o.w += v.w * f;
+  }
+  const float inv = l > 0.f ? 1.0f / l : 0.f;
+  float4 r = make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv);
+  if (!(l > 0.f)) r = make_float4(0.f, 0.f, 0.f, 0.f);
+  reinterpret_cast<float4*>(out + ((uint64_t)b * H + h) * R)[threadIdx.x] = r;
+}
+
+size_t decode_smem(int nh) {
+  return sizeof(float) * ((size_t)nh * W + (size_t)TT * KS + (size_t)NW * nh * TT + (size_t)nh * TT +
+                          3 * (size_t)nh);
+}
+
+template <bool QUANT, int NH>
+int launch_decode_t(kvcu_decode_ws* ws, const DecodeArgs& a, cudaStream_t st) {
+  const size_t smem = decode_smem(NH);
+  static bool configured = false;
+  if (!configured) {
+    int rc = kvcu_check_cuda(
+        cudaFuncSetAttribute(k_decode<QUANT, NH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem),
+        "cudaFuncSetAttribute(decode)");
+    if (rc) return rc;
+    configured = true;
+  }
+  k_decode<QUANT, NH><<<ws->num_sms, NT, smem, st>>>(a);
+  return kvcu_check_cuda(cudaGetLastError(), "decode kernel launch");
+}
+
+template <bool QUANT>
+int launch_decode_q(kvcu_decode_ws* ws, const DecodeArgs& a, cudaStream_t st) {
+  const uint32_t H = a.n_heads;
+  if (H <= 4) return launch_decode_t<QUANT, 4>(ws, a, st);
+  if (H <= 8) return launch_decode_t<QUANT, 8>(ws, a, st);
+  if (H <= 16) return launch_decode_t<QUANT, 16>(ws, a, st);
+  if (H <= 20) return launch_decode_t<QUANT, 20>(ws, a, st);
+  if (H <= 24) return launch_decode_t<QUANT, 24>(ws, a, st);
+  return launch_decode_t<QUANT, 32>(ws, a, st);
+}
+
+}  // namespace
+
+int kvcu_decode_setup(kvcu_decode_ws* ws) {
+  int sms = 0;
+  KVCU_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, ws->device));
+  ws->num_sms = sms > 0 ? sms : 148;
+  ws->decode_ctas = ws->num_sms;  // one 256-thread CTA per SM (smem-limited)
+  return KVCU_OK;
+}
+
+int kvcu_launch_plan(kvcu_decode_ws* ws, const kvcu_pool* p, uint32_t n, const uint32_t* seq_ids,
+                     uint32_t n_seqs, const uint32_t* lens, cudaStream_t st) {
+  (void)p;
+  const uint32_t target = (uint32_t)ws->decode_ctas * TARGET_WAVES;
+  k_plan<<<1, 1024, 0, st>>>(n, seq_ids, n_seqs, lens, target, ws->max_items, ws->items,
+                             ws->meta, ws->seq_first, ws->seq_count);
+  return kvcu_check_cuda(cudaGetLastError(), "plan kernel launch");
+}
+
+int kvcu_launch_decode(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint32_t n,
+                       const uint32_t* seq_ids, uint32_t n_seqs, const uint32_t* toff,
+                       const uint32_t* tables, const uint32_t* lens, const float* q,
+                       uint32_t n_heads, float scale, float* out, cudaStream_t st) {
+  if (p->kv_rank != (uint32_t)R || p->rope_dim != (uint32_t)P) {
+    kvcu_set_error("mla_decode: kernels are built for kv_rank=%d, rope_dim=%d (pool has %u, %u)", R,
+                   P, p->kv_rank, p->rope_dim);
+    return KVCU_ERR_UNSUPPORTED;
+  }
+  if (n_heads == 0 || n_heads > 32 || n_heads > ws->max_heads) {
+    kvcu_set_error("mla_decode: n_heads=%u outside [1, min(32, workspace %u)]", n_heads,
+                   ws->max_heads);
+    return KVCU_ERR_UNSUPPORTED;
+  }
+  if (n > ws->max_batch) {
+    kvcu_set_error("mla_decode: batch %u exceeds workspace capacity %u", n, ws->max_batch);
+    return KVCU_ERR_INVALID_ARG;
+  }
+  ws->last_launches = 0;
+  if (n == 0) return KVCU_OK;
+  DecodeArgs a;
+  a.layer = layer;
+  a.num_blocks = p->num_blocks;
+  a.block_size = p->block_size;
+  a.nblk = p->nblk;
+  a.kv = p->kv;
+  a.pe = p->pe;
+  a.qs = p->qs;
+  a.sc = p->sc;
+  a.status = p->status;
+  a.n = n;
+  a.seq_ids = seq_ids;
+  a.n_seqs = n_seqs;
+  a.toff = toff;
+  a.tables = tables;
+  a.lens = lens;
+  a.q = q;
+  a.n_heads = n_heads;
+  a.scale = scale;
+  a.out = out;
+  a.items = ws->items;
+  a.meta = ws->meta;
+  a.seq_count = ws->seq_count;
+  a.part_o = ws->part_o;
+  a.part_ml = ws->part_ml;
+  a.ws_heads = ws->max_heads;
+  int rc = p->quantized ? launch_decode_q<true>(ws, a, st) : launch_decode_q<false>(ws, a, st);
+  if (rc) return rc;
+  k_combine<<<n * n_heads, 128, 0, st>>>(n, n_heads, ws->max_heads, ws->seq_first, ws->seq_count,
+                                         ws->part_o, ws->part_ml, out);
+  rc = kvcu_check_cuda(cudaGetLastError(), "combine kernel launch");
+  if (rc) return rc;
+  ws->last_launches = 2;
+  return KVCU_OK;
+}

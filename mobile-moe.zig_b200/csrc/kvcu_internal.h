@@ -1,0 +1,78 @@
+// kvcu_internal.h — internal structures shared by the libkvcuda translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/kvcuda.h"
+
+struct kvcu_pool {
+  int device;
+  uint32_t n_layers, num_blocks, block_size, kv_rank, rope_dim;
+  uint32_t quantized;
+  uint32_t nbk, nbp, nblk;   // Q8_0 blocks: latent, rope, total per row
+  float* kv;                 // f32 [L][NB][BS][kv_rank]
+  float* pe;                 // f32 [L][NB][BS][rope_dim]
+  int8_t* qs;                // int8 [L][NB][BS][nblk*32]
+  uint16_t* sc;              // f16 bits [L][NB][BS][nblk]
+  uint32_t* status;          // device status word (KVCU_STATUS_* bits)
+  uint8_t* staging;          // device staging for checkpoint repacking
+  uint64_t staging_bytes;
+  uint64_t rows() const { return (uint64_t)n_layers * num_blocks * block_size; }
+};
+
+// Split-KV work item: batch entry b, tokens [start, end).
+struct kvcu_item {
+  uint32_t b, start, end, pad;
+};
+
+struct kvcu_decode_ws {
+  int device;
+  uint32_t max_batch, max_heads, max_items;
+  kvcu_item* items;          // [max_items]
+  uint32_t* meta;            // [0] n_items, [1] chunk tokens
+  uint32_t* seq_first;       // [max_batch] first item of entry b
+  uint32_t* seq_count;       // [max_batch] items of entry b
+  float* part_o;             // [max_items][max_heads][512]
+  float* part_ml;            // [max_items][max_heads][2] (m, l)
+  uint32_t last_launches;
+  int num_sms;
+  int decode_ctas;           // resident decode CTAs (grid of the persistent kernel)
+};
+
+// ---- error plumbing (kvcu_api.cu) ----
+void kvcu_set_error(const char* fmt, ...);
+int kvcu_check_cuda(cudaError_t e, const char* what);
+#define KVCU_CUDA(call) \
+  do { \
+    int _rc = kvcu_check_cuda((call), #call); \
+    if (_rc) return _rc; \
+  } while (0)
+
+// ---- kernel launchers (kvcu_kernels.cu) ----
+int kvcu_launch_append(kvcu_pool* p, uint32_t layer, uint32_t n_rows, const float* latent,
+                       uint64_t ls, const float* rope, uint64_t ps, const uint32_t* row_seq,
+                       const uint32_t* row_pos, uint32_t n_seqs, const uint32_t* table_offsets,
+                       const uint32_t* tables, uint32_t* lens, cudaStream_t st);
+int kvcu_launch_gather_rows(kvcu_pool* p, uint32_t layer, uint32_t n_rows, const uint32_t* row_seq,
+                            const uint32_t* row_pos, uint32_t n_seqs, const uint32_t* table_offsets,
+                            const uint32_t* tables, const uint32_t* table, uint32_t table_len,
+                            float* out, cudaStream_t st);
+int kvcu_launch_pack_q8(kvcu_pool* p, int part, uint64_t blk0, uint64_t nblocks, uint8_t* dst,
+                        cudaStream_t st);
+int kvcu_launch_unpack_q8(kvcu_pool* p, int part, uint64_t blk0, uint64_t nblocks,
+                          const uint8_t* src, cudaStream_t st);
+int kvcu_launch_synth(uint64_t seed, uint64_t a, uint32_t n_rows, const uint32_t* b,
+                      const uint32_t* c, uint32_t width, float outlier_p, float* out,
+                      cudaStream_t st);
+
+// ---- decode (kvcu_decode.cu) ----
+int kvcu_decode_setup(kvcu_decode_ws* ws);
+int kvcu_launch_plan(kvcu_decode_ws* ws, const kvcu_pool* p, uint32_t n, const uint32_t* seq_ids,
+                     uint32_t n_seqs, const uint32_t* lens, cudaStream_t st);
+int kvcu_launch_decode(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint32_t n,
+                       const uint32_t* seq_ids, uint32_t n_seqs, const uint32_t* table_offsets,
+                       const uint32_t* tables, const uint32_t* lens, const float* q,
+                       uint32_t n_heads, float scale, float* out, cudaStream_t st);

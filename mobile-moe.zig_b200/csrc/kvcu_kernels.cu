@@ -1,0 +1,304 @@
+// kvcu_kernels.cu — append (f32 -> Q8_0 quantize + block-table scatter),
+// block-table gather/dequant, checkpoint repacking and the seeded generator.
+//
+// Reference behaviour restated:
+//   append  = KVCache.put            src/kv_cache.zig:279-361
+//   gather  = getKVCompressed/getKPe src/kv_cache.zig:225-277
+//   repack  = the BlockQ8_0 byte order of saveToFile/loadFromFile
+//             (src/kv_cache.zig:484-492, :535-545; BlockQ8_0 src/dequant.zig:372-377)
+//
+// All three are HBM-bound byte/integer work with a little f32 arithmetic:
+// one warp owns one 32-element Q8_0 block (one 128-byte coalesced f32 read,
+// one 32-byte int8 write, a 5-step shuffle max), grids are sized in multiples
+// of the SM count and loop grid-stride.
+#include <cuda_runtime.h>
+
+#include "kvcu_internal.h"
+#include "kvcu_numeric.cuh"
+
+namespace {
+
+struct PoolArgs {
+  uint32_t layer, num_blocks, block_size, kv_rank, rope_dim, nbk, nbp, nblk;
+  float* kv;
+  float* pe;
+  int8_t* qs;
+  uint16_t* sc;
+  uint32_t* status;
+};
+
+PoolArgs pool_args(kvcu_pool* p, uint32_t layer) {
+  PoolArgs a;
+  a.layer = layer;
+  a.num_blocks = p->num_blocks;
+  a.block_size = p->block_size;
+  a.kv_rank = p->kv_rank;
+  a.rope_dim = p->rope_dim;
+  a.nbk = p->nbk;
+  a.nbp = p->nbp;
+  a.nblk = p->nblk;
+  a.kv = p->kv;
+  a.pe = p->pe;
+  a.qs = p->qs;
+  a.sc = p->sc;
+  a.status = p->status;
+  return a;
+}
+
+int grid_for(uint64_t warps, int threads) {
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+  }
+  uint64_t blocks = (warps * 32 + threads - 1) / threads;
+  uint64_t cap = (uint64_t)sms * 16;  // 16 resident 256-thread CTAs per SM at most
+  if (blocks > cap) blocks = cap;
+  if (blocks == 0) blocks = 1;
+  return (int)blocks;
+}
+
+// Resolve (sequence, position) -> pool row; returns false (and flags the
+// status word once per warp) when an index is out of range.
+__device__ __forceinline__ bool resolve_row(const PoolArgs& a, uint32_t s, uint32_t pos,
+                                            uint32_t n_seqs, const uint32_t* __restrict__ toff,
+                                            const uint32_t* __restrict__ tables, uint32_t lane,
+                                            uint64_t* row) {
+  if (s >= n_seqs) {
+    if (lane == 0) atomicOr(a.status, KVCU_STATUS_BAD_SEQ);
+    return false;
+  }
+  uint32_t t0 = toff[s], t1 = toff[s + 1];
+  uint32_t bi = pos / a.block_size;
+  if (t1 < t0 || bi >= t1 - t0) {
+    if (lane == 0) atomicOr(a.status, KVCU_STATUS_BAD_TABLE);
+    return false;
+  }
+  uint32_t blk = tables[t0 + bi];
+  if (blk >= a.num_blocks) {
+    if (lane == 0) atomicOr(a.status, KVCU_STATUS_BAD_BLOCK);
+    return false;
+  }
+  *row = ((uint64_t)a.layer * a.num_blocks + blk) * a.block_size + pos % a.block_size;
+  return true;
+}
+
+// One warp per (row, 32-element block).  Q8_0: amax over the block,
+// d = amax/127, d16 = f32ToF16(d), q = clamp(round(x/d)), tail zero-fill.
+template <bool QUANT>
+__global__ void __launch_bounds__(256) k_append(PoolArgs a, uint32_t n_rows,
+                                                const float* __restrict__ latent, uint64_t ls,
+                                                const float* __restrict__ rope, uint64_t ps,
+                                                const uint32_t* __restrict__ row_seq,
+                                                const uint32_t* __restrict__ row_pos,
+                                                uint32_t n_seqs, const uint32_t* __restrict__ toff,
+                                                const uint32_t* __restrict__ tables,
+                                                uint32_t* __restrict__ lens) {
+  const uint32_t lane = threadIdx.x & 31u;
+  const uint64_t nwarps = ((uint64_t)gridDim.x * blockDim.x) >> 5;
+  const uint32_t W = a.kv_rank + a.rope_dim;
+  const uint32_t nper = QUANT ? a.nblk : (W + 31u) / 32u;
+  const uint64_t total = (uint64_t)n_rows * nper;
+  for (uint64_t wi = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; wi < total;
+       wi += nwarps) {
+    const uint32_t r = (uint32_t)(wi / nper), b = (uint32_t)(wi % nper);
+    uint64_t row;
+    if (!resolve_row(a, row_seq[r], row_pos[r], n_seqs, toff, tables, lane, &row)) continue;
+    // len = max(len, pos + 1), src/kv_cache.zig:358-360 (once per row)
+    if (lens && b == 0 && lane == 0) atomicMax(lens + row_seq[r], row_pos[r] + 1u);
+    if (QUANT) {
+      const float* src;
+      uint32_t cnt;
+      if (b < a.nbk) {
+        src = latent + (uint64_t)r * ls + 32u * b;
+        cnt = min(32u, a.kv_rank - 32u * b);
+      } else {
+        src = rope + (uint64_t)r * ps + 32u * (b - a.nbk);
+        cnt = min(32u, a.rope_dim - 32u * (b - a.nbk));
+      }
+      const float x = lane < cnt ? src[lane] : 0.0f;
+      float amax = fabsf(x);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      const float d = kvcu::q8_scale(amax);
+      const int8_t q = (d > 0.0f && lane < cnt) ? kvcu::q8_value(x, d) : (int8_t)0;
+      a.qs[row * (32u * a.nblk) + 32u * b + lane] = q;
+      if (lane == 0) a.sc[row * a.nblk + b] = kvcu::f32_to_f16(d);
+    } else {
+      const uint32_t e = 32u * b + lane;
+      if (e < a.kv_rank) a.kv[row * a.kv_rank + e] = latent[(uint64_t)r * ls + e];
+      else if (e < W) a.pe[row * a.rope_dim + (e - a.kv_rank)] = rope[(uint64_t)r * ps + (e - a.kv_rank)];
+    }
+  }
+}
+
+// One warp per (row, 32-element block): out = f16ToF32(d) * q, or the f32 row.
+// Rows come either from one table (table != nullptr, row r = position r) or
+// from (row_seq[r], row_pos[r]) through the CSR tables.
+template <bool QUANT>
+__global__ void __launch_bounds__(256) k_gather(PoolArgs a, uint32_t n_rows,
+                                                const uint32_t* __restrict__ row_seq,
+                                                const uint32_t* __restrict__ row_pos,
+                                                uint32_t n_seqs, const uint32_t* __restrict__ toff,
+                                                const uint32_t* __restrict__ tables,
+                                                const uint32_t* __restrict__ table,
+                                                uint32_t table_len, float* __restrict__ out) {
+  const uint32_t lane = threadIdx.x & 31u;
+  const uint64_t nwarps = ((uint64_t)gridDim.x * blockDim.x) >> 5;
+  const uint32_t W = a.kv_rank + a.rope_dim;
+  const uint32_t nper = QUANT ? a.nblk : (W + 31u) / 32u;
+  const uint64_t total = (uint64_t)n_rows * nper;
+  for (uint64_t wi = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; wi < total;
+       wi += nwarps) {
+    const uint32_t r = (uint32_t)(wi / nper), b = (uint32_t)(wi % nper);
+    uint64_t row;
+    if (table) {
+      const uint32_t bi = r / a.block_size;
+      if (bi >= table_len) {
+        if (lane == 0) atomicOr(a.status, KVCU_STATUS_BAD_TABLE);
+        continue;
+      }
+      const uint32_t blk = table[bi];
+      if (blk >= a.num_blocks) {
+        if (lane == 0) atomicOr(a.status, KVCU_STATUS_BAD_BLOCK);
+        continue;
+      }
+      row = ((uint64_t)a.layer * a.num_blocks + blk) * a.block_size + r % a.block_size;
+    } else if (!resolve_row(a, row_seq[r], row_pos[r], n_seqs, toff, tables, lane, &row)) {
+      continue;
+    }
+    float* dst = out + (uint64_t)r * W;
+    if (QUANT) {
+      uint32_t e, cnt;
+      if (b < a.nbk) {
+        e = 32u * b;
+        cnt = min(32u, a.kv_rank - e);
+      } else {
+        e = a.kv_rank + 32u * (b - a.nbk);
+        cnt = min(32u, a.rope_dim - 32u * (b - a.nbk));
+      }
+      if (lane < cnt) {
+        const float d = kvcu::f16_to_f32(a.sc[row * a.nblk + b]);
+        const float q = (float)a.qs[row * (32u * a.nblk) + 32u * b + lane];
+        dst[e + lane] = __fmul_rn(d, q);
+      }
+    } else {
+      const uint32_t e = 32u * b + lane;
+      if (e < a.kv_rank) dst[e] = a.kv[row * a.kv_rank + e];
+      else if (e < W) dst[e] = a.pe[row * a.rope_dim + (e - a.kv_rank)];
+    }
+  }
+}
+
+// Checkpoint repacking between the device layout (qs / sc split) and the
+// reference's 34-byte BlockQ8_0 order.  part 0 = latent blocks of every row,
+// part 1 = rope blocks of every row.  One warp per 34-byte block.
+__global__ void __launch_bounds__(256) k_pack_q8(PoolArgs a, int part, uint64_t blk0,
+                                                 uint64_t nblocks, uint8_t* __restrict__ dst) {
+  const uint32_t lane = threadIdx.x & 31u;
+  const uint64_t nwarps = ((uint64_t)gridDim.x * blockDim.x) >> 5;
+  const uint32_t per = part == 0 ? a.nbk : a.nbp;
+  for (uint64_t wi = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; wi < nblocks;
+       wi += nwarps) {
+    const uint64_t k = blk0 + wi;
+    const uint64_t row = k / per;
+    const uint32_t j = (uint32_t)(k % per) + (part == 0 ? 0u : a.nbk);
+    uint8_t* o = dst + wi * 34u;
+    o[2 + lane] = (uint8_t)a.qs[row * (32u * a.nblk) + 32u * j + lane];
+    if (lane == 0) {
+      const uint16_t d = a.sc[row * a.nblk + j];
+      o[0] = (uint8_t)(d & 0xFFu);
+      o[1] = (uint8_t)(d >> 8);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256) k_unpack_q8(PoolArgs a, int part, uint64_t blk0,
+                                                   uint64_t nblocks, const uint8_t* __restrict__ src) {
+  const uint32_t lane = threadIdx.x & 31u;
+  const uint64_t nwarps = ((uint64_t)gridDim.x * blockDim.x) >> 5;
+  const uint32_t per = part == 0 ? a.nbk : a.nbp;
+  for (uint64_t wi = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; wi < nblocks;
+       wi += nwarps) {
+    const uint64_t k = blk0 + wi;
+    const uint64_t row = k / per;
+    const uint32_t j = (uint32_t)(k % per) + (part == 0 ? 0u : a.nbk);
+    const uint8_t* s = src + wi * 34u;
+    a.qs[row * (32u * a.nblk) + 32u * j + lane] = (int8_t)s[2 + lane];
+    if (lane == 0) a.sc[row * a.nblk + j] = (uint16_t)(s[0] | ((uint16_t)s[1] << 8));
+  }
+}
+
+__global__ void __launch_bounds__(256) k_synth(uint64_t seed, uint64_t a, uint32_t n_rows,
+                                               const uint32_t* __restrict__ b,
+                                               const uint32_t* __restrict__ c, uint32_t width,
+                                               float outlier_p, float* __restrict__ out) {
+  const uint64_t total = (uint64_t)n_rows * width;
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+    const uint32_t r = (uint32_t)(i / width), e = (uint32_t)(i % width);
+    out[i] = kvcu::gen_normal(seed, a, b[r], (uint64_t)c[r] * 1024u + e, outlier_p);
+  }
+}
+
+}  // namespace
+
+int kvcu_launch_append(kvcu_pool* p, uint32_t layer, uint32_t n_rows, const float* latent,
+                       uint64_t ls, const float* rope, uint64_t ps, const uint32_t* row_seq,
+                       const uint32_t* row_pos, uint32_t n_seqs, const uint32_t* toff,
+                       const uint32_t* tables, uint32_t* lens, cudaStream_t st) {
+  if (n_rows == 0) return KVCU_OK;
+  PoolArgs a = pool_args(p, layer);
+  const uint32_t nper = p->quantized ? p->nblk : (p->kv_rank + p->rope_dim + 31) / 32;
+  const int g = grid_for((uint64_t)n_rows * nper, 256);
+  if (p->quantized)
+    k_append<true><<<g, 256, 0, st>>>(a, n_rows, latent, ls, rope, ps, row_seq, row_pos, n_seqs,
+                                      toff, tables, lens);
+  else
+    k_append<false><<<g, 256, 0, st>>>(a, n_rows, latent, ls, rope, ps, row_seq, row_pos, n_seqs,
+                                       toff, tables, lens);
+  return kvcu_check_cuda(cudaGetLastError(), "append kernel launch");
+}
+
+int kvcu_launch_gather_rows(kvcu_pool* p, uint32_t layer, uint32_t n_rows, const uint32_t* row_seq,
+                            const uint32_t* row_pos, uint32_t n_seqs, const uint32_t* toff,
+                            const uint32_t* tables, const uint32_t* table, uint32_t table_len,
+                            float* out, cudaStream_t st) {
+  if (n_rows == 0) return KVCU_OK;
+  PoolArgs a = pool_args(p, layer);
+  const uint32_t nper = p->quantized ? p->nblk : (p->kv_rank + p->rope_dim + 31) / 32;
+  const int g = grid_for((uint64_t)n_rows * nper, 256);
+  if (p->quantized)
+    k_gather<true><<<g, 256, 0, st>>>(a, n_rows, row_seq, row_pos, n_seqs, toff, tables, table,
+                                      table_len, out);
+  else
+    k_gather<false><<<g, 256, 0, st>>>(a, n_rows, row_seq, row_pos, n_seqs, toff, tables, table,
+                                       table_len, out);
+  return kvcu_check_cuda(cudaGetLastError(), "gather kernel launch");
+}
+
+int kvcu_launch_pack_q8(kvcu_pool* p, int part, uint64_t blk0, uint64_t nblocks, uint8_t* dst,
+                        cudaStream_t st) {
+  if (!nblocks) return KVCU_OK;
+  k_pack_q8<<<grid_for(nblocks, 256), 256, 0, st>>>(pool_args(p, 0), part, blk0, nblocks, dst);
+  return kvcu_check_cuda(cudaGetLastError(), "pack kernel launch");
+}
+
+int kvcu_launch_unpack_q8(kvcu_pool* p, int part, uint64_t blk0, uint64_t nblocks,
+                          const uint8_t* src, cudaStream_t st) {
+  if (!nblocks) return KVCU_OK;
+  k_unpack_q8<<<grid_for(nblocks, 256), 256, 0, st>>>(pool_args(p, 0), part, blk0, nblocks, src);
+  return kvcu_check_cuda(cudaGetLastError(), "unpack kernel launch");
+}
+
+int kvcu_launch_synth(uint64_t seed, uint64_t a, uint32_t n_rows, const uint32_t* b,
+                      const uint32_t* c, uint32_t width, float outlier_p, float* out,
+                      cudaStream_t st) {
+  const uint64_t total = (uint64_t)n_rows * width;
+  if (!total) return KVCU_OK;
+  k_synth<<<grid_for((total + 31) / 32, 256), 256, 0, st>>>(seed, a, n_rows, b, c, width,
+                                                           outlier_p, out);
+  return kvcu_check_cuda(cudaGetLastError(), "synth kernel launch");
+}

@@ -161,12 +161,15 @@ int kvo_pool_init(kvo_pool* p, uint32_t n_layers, uint32_t num_blocks, uint32_t 
   p->kv_rank = kv_rank;
   p->rope_dim = rope_dim;
   uint64_t rows = (uint64_t)n_layers * num_blocks * block_size;
-  /* src/kv_cache.zig:72-78: f32 pools always exist and are zeroed. */
-  p->kv = (float*)calloc(rows * kv_rank, sizeof(float));
-  p->pe = (float*)calloc(rows * rope_dim, sizeof(float));
-  if (!p->kv || !p->pe) {
-    kvo_pool_free(p);
-    return KVO_ERR_NO_MEMORY;
+  /* src/kv_cache.zig:72-78: zeroed f32 pools.  A pool created quantized has
+   * no f32 pools (the single-sequence kvo_cache keeps both, as the reference). */
+  if (!quantized) {
+    p->kv = (float*)calloc(rows * kv_rank, sizeof(float));
+    p->pe = (float*)calloc(rows * rope_dim, sizeof(float));
+    if (!p->kv || !p->pe) {
+      kvo_pool_free(p);
+      return KVO_ERR_NO_MEMORY;
+    }
   }
   if (quantized) {
     p->kv_q8 = (kvo_block_q8*)calloc(rows * nq8(kv_rank), sizeof(kvo_block_q8));
@@ -204,6 +207,13 @@ void kvo_pool_put(kvo_pool* p, uint32_t layer, uint32_t block, uint32_t offset,
     memcpy(p->kv + r * p->kv_rank, kv_comp, sizeof(float) * p->kv_rank);
     memcpy(p->pe + r * p->rope_dim, k_pe, sizeof(float) * p->rope_dim);
   }
+}
+
+void kvo_pool_put_rows(kvo_pool* p, uint32_t layer, uint32_t n, const uint32_t* blocks,
+                       const uint32_t* offsets, const float* rows) {
+  const uint64_t w = p->kv_rank + p->rope_dim;
+  for (uint32_t r = 0; r < n; ++r)
+    kvo_pool_put(p, layer, blocks[r], offsets[r], rows + r * w, rows + r * w + p->kv_rank);
 }
 
 /* src/kv_cache.zig:225-277 */

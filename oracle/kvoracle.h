@@ -101,6 +101,9 @@ void kvo_pool_free(kvo_pool* p);
 /* Write one row (kv_comp[kv_rank], k_pe[rope_dim]) at (layer, block, offset). */
 void kvo_pool_put(kvo_pool* p, uint32_t layer, uint32_t block, uint32_t offset,
                   const float* kv_comp, const float* k_pe);
+/* Batched put: row r (rows[r][kv_rank+rope_dim]) goes to (blocks[r], offsets[r]). */
+void kvo_pool_put_rows(kvo_pool* p, uint32_t layer, uint32_t n, const uint32_t* blocks,
+                       const uint32_t* offsets, const float* rows);
 /* Read (dequantize) one row. */
 void kvo_pool_get(const kvo_pool* p, uint32_t layer, uint32_t block, uint32_t offset,
                   float* kv_out, float* pe_out);

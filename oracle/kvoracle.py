@@ -70,6 +70,7 @@ def lib():
             "kvo_pool_free": (None, [P]),
             "kvo_pool_put": (None, [P, u32, u32, u32, vp, vp]),
             "kvo_pool_get": (None, [P, u32, u32, u32, vp, vp]),
+            "kvo_pool_put_rows": (None, [P, u32, u32, vp, vp, vp]),
             "kvo_pool_gather": (None, [P, u32, vp, u32, vp]),
             "kvo_pool_bytes": (u64, [P]),
             "kvo_pool_serialize": (None, [P, vp]),
@@ -174,13 +175,13 @@ class Pool:
         k_pe = np.ascontiguousarray(k_pe, np.float32)
         lib().kvo_pool_put(self.ref, layer, block, offset, _ptr(kv_comp), _ptr(k_pe))
 
-    def put_rows(self, layer, slots, rows):
-        """rows: [n][kv_rank+rope_dim]; slots: physical row ids (block*BS + offset)."""
+    def put_rows(self, layer, blocks, offsets, rows):
+        """rows: [n][kv_rank+rope_dim] written to (blocks[r], offsets[r])."""
         rows = np.ascontiguousarray(rows, np.float32)
-        for s, row in zip(np.asarray(slots).tolist(), rows):
-            row = np.ascontiguousarray(row)
-            self.put(layer, s // self.block_size, s % self.block_size, row[: self.kv_rank],
-                     row[self.kv_rank:])
+        blocks = np.ascontiguousarray(blocks, np.uint32)
+        offsets = np.ascontiguousarray(offsets, np.uint32)
+        assert rows.shape == (blocks.size, self.kv_rank + self.rope_dim)
+        lib().kvo_pool_put_rows(self.ref, layer, blocks.size, _ptr(blocks), _ptr(offsets), _ptr(rows))
 
     def get(self, layer, block, offset):
         kv = np.zeros(self.kv_rank, np.float32)
