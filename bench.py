@@ -265,14 +265,15 @@ def run_ours(args, rank, world, local_rank):
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     kvcu.init(local_rank)
-    lens_all = config5_lengths()
+    NL = args.layers
+    lens_all = config5_lengths(n=args.seqs)
     parts, loads = lpt_partition(lens_all, world)
     mine = np.array(parts[rank], np.int64)
     lens0 = lens_all[mine]
     n = mine.size
     total_steps = args.warmup + args.steps + args.e2e_warmup + args.e2e_steps
     nb = int(sum((int(L) + total_steps + BS - 1) // BS for L in lens0)) + 8
-    cache = kvcu.KVCache.with_blocks(N_LAYERS, R, P, nb, BS, quantized=True, device=local_rank)
+    cache = kvcu.KVCache.with_blocks(NL, R, P, nb, BS, quantized=True, device=local_rank)
     for _ in range(n - 1):
         cache.seq_create()
     ids = np.arange(n, dtype=np.uint32)
@@ -280,7 +281,7 @@ def run_ours(args, rank, world, local_rank):
         cache.seq_ensure_capacity(i, int(lens0[i]) + total_steps)
     # ---- prefill (device generator + batched append); also the large-append measurement
     t_pre = time.perf_counter()
-    for layer in range(N_LAYERS):
+    for layer in range(NL):
         cache.prefill_synthetic(layer, ids, lens0, SEED, OUTLIER_P, seq_tags=mine)
     torch.cuda.synchronize()
     t_pre = time.perf_counter() - t_pre
@@ -294,24 +295,24 @@ def run_ours(args, rank, world, local_rank):
             pos_dev[k] = torch.from_numpy((lens0 + k).astype(np.int32)).to(dev)
         ids_dev = torch.from_numpy(ids.astype(np.int32)).to(dev)
         tags_dev = torch.from_numpy(mine.astype(np.int32)).to(dev)
-        rows = torch.empty((W_steps, N_LAYERS, n, W), dtype=torch.float32, device=dev)
+        rows = torch.empty((W_steps, NL, n, W), dtype=torch.float32, device=dev)
         for k in range(W_steps):
-            for layer in range(N_LAYERS):
+            for layer in range(NL):
                 kvcu.synth_rows(SEED, layer, tags_dev, pos_dev[k], W, rows[k, layer], OUTLIER_P, st)
-        qs = torch.empty((N_LAYERS, n, H, W), dtype=torch.float32, device=dev)
+        qs = torch.empty((NL, n, H, W), dtype=torch.float32, device=dev)
         qtag = (mine.astype(np.int64) * 64)[:, None] + np.arange(H)[None, :]
         qb = torch.from_numpy(qtag.reshape(-1).astype(np.int32)).to(dev)
         qc = torch.zeros(n * H, dtype=torch.int32, device=dev)
-        for layer in range(N_LAYERS):
+        for layer in range(NL):
             kvcu.synth_rows(SEED + 1, 100 + layer, qb, qc, W, qs[layer].view(n * H, W), 0.0, st)
-        outs = torch.empty((N_LAYERS, n, H, R), dtype=torch.float32, device=dev)
+        outs = torch.empty((NL, n, H, R), dtype=torch.float32, device=dev)
     st.synchronize()
 
     ev = {"dec": [], "launches": 0}
 
     def step(k, timed):
         pos_h = (lens0 + k).astype(np.uint32)
-        for layer in range(N_LAYERS):
+        for layer in range(NL):
             cache.appendBatch_dev(layer, ids, pos_h, ids_dev, pos_dev[k], rows[k, layer], st)
             ev["launches"] += cache.last_launches
             if timed:
@@ -338,11 +339,13 @@ def run_ours(args, rank, world, local_rank):
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
     with ClockSampler(physical_gpu(local_rank)) as clk:
+        torch.cuda.nvtx.range_push("timed")
         t_start.record(st)
         for k in range(args.warmup, args.warmup + args.steps):
             step(k, True)
-            ctx_tokens += int((lens0 + k + 1).sum()) * N_LAYERS
+            ctx_tokens += int((lens0 + k + 1).sum()) * NL
         t_end.record(st)
+        torch.cuda.nvtx.range_pop()
         st.synchronize()
     barrier()
     torch.cuda.synchronize()
@@ -362,22 +365,22 @@ def run_ours(args, rank, world, local_rank):
         dist.all_reduce(tot, op=dist.ReduceOp.SUM)
         dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
         job_tokens, job_time = tot[0].item(), tmax[1].item()
-        dec_gbs = tot[2].item() / world
+        dec_gbs = tot[2].item() / world / 1e9
     else:
         job_tokens, job_time = ctx_tokens, elapsed
-        dec_gbs = dec_bytes / avg_dec
+        dec_gbs = dec_bytes / avg_dec / 1e9
     value = job_tokens / job_time
 
     # ---- e2e through the host-buffer API (pinned host memory, copies inside)
     q_host = qs.cpu().pin_memory()
-    out_host = torch.empty((N_LAYERS, n, H, R), dtype=torch.float32).pin_memory()
-    rows_host = torch.empty((N_LAYERS, n, W), dtype=torch.float32).pin_memory()
+    out_host = torch.empty((NL, n, H, R), dtype=torch.float32).pin_memory()
+    rows_host = torch.empty((NL, n, W), dtype=torch.float32).pin_memory()
     rows_host.copy_(rows[0])  # same distribution; content does not change the work
     base = W_steps
 
     def e2e_step(k):
         pos_h = (lens0 + base + k).astype(np.uint32)
-        for layer in range(N_LAYERS):
+        for layer in range(NL):
             cache.appendBatch(layer, ids, pos_h, rows_host[layer].numpy())
             cache.mlaDecode_ptr(layer, n, ids, q_host[layer].data_ptr(), H, SCALE, out_host[layer].data_ptr())
             _ = out_host[layer, 0, 0, 0].item()
@@ -390,7 +393,7 @@ def run_ours(args, rank, world, local_rank):
     e2e_tokens = 0
     for k in range(args.e2e_warmup, args.e2e_warmup + args.e2e_steps):
         e2e_step(k)
-        e2e_tokens += int((lens0 + base + k + 1).sum()) * N_LAYERS
+        e2e_tokens += int((lens0 + base + k + 1).sum()) * NL
     torch.cuda.synchronize()
     e2e_time = time.perf_counter() - t0
     e = torch.tensor([float(e2e_tokens), e2e_time], dtype=torch.float64, device=dev)
@@ -400,9 +403,9 @@ def run_ours(args, rank, world, local_rank):
         dist.all_reduce(emax, op=dist.ReduceOp.MAX)
         e2e_value = e[0].item() / emax[1].item()
     else:
-        e2e_value = e2e_tokens / e2e_time
-    h2d = N_LAYERS * n * (W * 4 + 8 + H * W * 4)
-    d2h = N_LAYERS * n * H * R * 4
+        e2e_value = e2e_tokens / e2e_time if e2e_time > 0 else None
+    h2d = NL * n * (W * 4 + 8 + H * W * 4)
+    d2h = NL * n * H * R * 4
 
     append_gbs = measure_append(kvcu, torch, dev, local_rank)
     clk_sum = clk.summary()
@@ -424,8 +427,9 @@ def run_ours(args, rank, world, local_rank):
             "warmup": args.warmup, "ms_per_step": 1e3 * job_time / args.steps,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded N(0,1) rows with 1% x20 outliers, random q)",
-            "config": {"workload": "config5_sharded_serving_step", "n_seqs": N_SEQS,
-                       "layers": N_LAYERS, "block_size": BS, "heads": H, "kv_rank": R, "rope_dim": P,
+            "config": {"workload": ("config5_sharded_serving_step" if (args.seqs, NL) == (N_SEQS, N_LAYERS)
+                                    else f"config5_reduced_{args.seqs}seqs_{NL}layers"), "n_seqs": args.seqs,
+                       "layers": NL, "block_size": BS, "heads": H, "kv_rank": R, "rope_dim": P,
                        "kv_dtype": "q8_0", "lengths": f"log-uniform[{LEN_LO},{LEN_HI}] seed {SEED}",
                        "ctx_tokens_per_step": int(job_tokens / args.steps),
                        "parallelism": f"sequence-sharded x{world} (LPT by tokens), no collective",
@@ -462,6 +466,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-sample-tokens", type=int, default=400_000)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--seqs", type=int, default=N_SEQS, help="sequences (config 5: 512)")
+    ap.add_argument("--layers", type=int, default=N_LAYERS, help="layers (config 5: 8)")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
