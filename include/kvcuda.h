@@ -169,6 +169,16 @@ int kvcu_mla_decode(kvcu_decode_ws* ws, kvcu_pool* pool, uint32_t layer, uint32_
                     uint32_t n_heads, float scale, float* out, void* stream);
 /* Kernel launches the last kvcu_mla_decode issued (for launch accounting). */
 uint32_t kvcu_decode_last_launches(const kvcu_decode_ws* ws);
+/* Decode kernel selection.  AUTO uses the tcgen05 tensor-core kernel for Q8_0
+ * pools with kv_rank 512 / rope_dim 64 / <= 24 heads / block sizes dividing or
+ * multiples of 128, and the CUDA-core kernel otherwise (f32 pools, 25..32
+ * heads).  Forcing TENSOR_CORE on an unsupported shape returns
+ * KVCU_ERR_UNSUPPORTED.  kvcu_decode_last_impl reports the kernel used. */
+#define KVCU_DECODE_AUTO 0
+#define KVCU_DECODE_CUDA_CORE 1
+#define KVCU_DECODE_TENSOR_CORE 2
+int kvcu_decode_ws_set_impl(kvcu_decode_ws* ws, int impl);
+int kvcu_decode_last_impl(const kvcu_decode_ws* ws);
 
 /* ------------------------------------------------------------ checkpoint I/O
  * Bytes of the pool section of a v1 checkpoint in the reference's order
@@ -265,6 +275,10 @@ int kvcache_mla_decode_dev(kvcache* c, uint32_t layer, uint32_t n, const uint32_
                            void* stream);
 /* Launches issued by the last kvcache_* data call (for launch accounting). */
 uint32_t kvcache_last_launches(const kvcache* c);
+/* Decode kernel selection for this cache (KVCU_DECODE_*), and the kernel the
+ * last decode used. */
+int kvcache_set_decode_impl(kvcache* c, int impl);
+int kvcache_last_decode_impl(const kvcache* c);
 /* Multi-sequence checkpoint (v2: header, per-sequence lengths and tables,
  * pool).  Single-sequence caches use kvcache_save_to_file (v1, byte-exact). */
 int kvcache_save_to_file_v2(kvcache* c, const char* path);

@@ -178,6 +178,7 @@ struct kvcache {
   uint64_t plan_epoch = ~0ull, epoch = 0;
   uint64_t plan_tokens = 0;
   uint32_t last_launches = 0;
+  int decode_impl = KVCU_DECODE_AUTO;
 
   bool quantized() const { return pool && pool->quantized; }
   uint32_t row_width() const { return kv_rank + rope_dim; }
@@ -444,7 +445,9 @@ int ensure_ws(kvcache* c, uint32_t n, uint32_t n_heads) {
   c->ws_heads = std::max<uint32_t>(n_heads, c->ws_heads);
   c->ws = kvcu_decode_ws_create(c->device, c->ws_batch, c->ws_heads);
   if (!c->ws) return KVCU_ERR_NO_MEMORY;
+  kvcu_decode_ws_set_impl(c->ws, c->decode_impl);
   c->plan_epoch = ~0ull;
+  c->plan_ids.clear();
   return KVCU_OK;
 }
 
@@ -780,6 +783,14 @@ int kvcache_mla_decode_dev(kvcache* c, uint32_t layer, uint32_t n, const uint32_
 }
 
 uint32_t kvcache_last_launches(const kvcache* c) { return c ? c->last_launches : 0; }
+
+int kvcache_set_decode_impl(kvcache* c, int impl) {
+  if (!c || impl < KVCU_DECODE_AUTO || impl > KVCU_DECODE_TENSOR_CORE) return KVCU_ERR_INVALID_ARG;
+  c->decode_impl = impl;
+  return c->ws ? kvcu_decode_ws_set_impl(c->ws, impl) : KVCU_OK;
+}
+
+int kvcache_last_decode_impl(const kvcache* c) { return c && c->ws ? kvcu_decode_last_impl(c->ws) : 0; }
 
 // ---- checkpoints ----
 namespace {

@@ -339,6 +339,14 @@ int kvcu_mla_decode(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint32_t n
 
 uint32_t kvcu_decode_last_launches(const kvcu_decode_ws* ws) { return ws ? ws->last_launches : 0; }
 
+int kvcu_decode_ws_set_impl(kvcu_decode_ws* ws, int impl) {
+  if (!ws || impl < KVCU_DECODE_AUTO || impl > KVCU_DECODE_TENSOR_CORE) return KVCU_ERR_INVALID_ARG;
+  ws->impl = impl;
+  return KVCU_OK;
+}
+
+int kvcu_decode_last_impl(const kvcu_decode_ws* ws) { return ws ? ws->last_impl : 0; }
+
 // ---------------------------------------------------------------- checkpoint
 static int ensure_staging(kvcu_pool* p) {
   if (p->staging) return KVCU_OK;

@@ -461,6 +461,28 @@ int kvcu_launch_decode(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint32_
                        const uint32_t* seq_ids, uint32_t n_seqs, const uint32_t* toff,
                        const uint32_t* tables, const uint32_t* lens, const float* q,
                        uint32_t n_heads, float scale, float* out, cudaStream_t st) {
+  const bool tc_ok = kvcu_decode_tc_supported(p, n_heads) && n_heads <= ws->max_heads &&
+                     n <= ws->max_batch;
+  if (ws->impl == KVCU_DECODE_TENSOR_CORE && !tc_ok) {
+    kvcu_set_error("mla_decode: the tensor-core kernel needs a Q8_0 pool with kv_rank 512, rope_dim "
+                   "64, <= 24 heads and a block size dividing (or a multiple of) 128");
+    return KVCU_ERR_UNSUPPORTED;
+  }
+  if (tc_ok && ws->impl != KVCU_DECODE_CUDA_CORE) {
+    ws->last_launches = 0;
+    if (n == 0) return KVCU_OK;
+    int rc = kvcu_launch_decode_tc(ws, p, layer, n, seq_ids, n_seqs, toff, tables, lens, q, n_heads,
+                                   scale, out, st);
+    if (rc) return rc;
+    k_combine<<<n * n_heads, 128, 0, st>>>(n, n_heads, ws->max_heads, ws->seq_first, ws->seq_count,
+                                           ws->part_o, ws->part_ml, out);
+    rc = kvcu_check_cuda(cudaGetLastError(), "combine kernel launch");
+    if (rc) return rc;
+    ws->last_launches = 2;
+    ws->last_impl = KVCU_DECODE_TENSOR_CORE;
+    return KVCU_OK;
+  }
+  ws->last_impl = KVCU_DECODE_CUDA_CORE;
   if (p->kv_rank != (uint32_t)R || p->rope_dim != (uint32_t)P) {
     kvcu_set_error("mla_decode: kernels are built for kv_rank=%d, rope_dim=%d (pool has %u, %u)", R,
                    P, p->kv_rank, p->rope_dim);

@@ -1,0 +1,965 @@
+// kvcu_decode_tc.cu — paged MLA decode on the sm_100a tensor cores (tcgen05 + TMA).
+//
+// Same contract as k_decode in kvcu_decode.cu (the attention core of
+// src/inference.zig:518-660 in absorbed form, over a Q8_0 pool), same work
+// items and partial format, so k_plan / k_combine are shared.  One persistent
+// CTA per SM, 10 warps with fixed roles:
+//
+//   warp 0     TMA producer: per 128-token tile, the Q8_0 payload rows of the
+//              sequence's physical blocks (2-D tensor maps over the pool,
+//              128B swizzle for the 512 latent bytes, 64B for the 64 rope
+//              bytes) and the f16 scales (1-D bulk copies) -> raw stage ring (2).
+//   warp 1     TMEM owner + single-thread MMA issuer:
+//                QK  = 18 x tcgen05.mma.kind::i8 per tile (one per Q8_0 block:
+//                      A = the raw int8 tile [128 tok x 32], B = the query as two
+//                      int8 digits [48 x 32]); exact int32 dot products per
+//                      block, into a ring of 8 TMEM slots;
+//                PV  = 8 chunks x 4 tcgen05.mma.kind::f16 (M = 128 latent
+//                      columns, N = 32 heads, K = 16 tokens): O^T += V^T P^T,
+//                      accumulated in TMEM across the whole work item.
+//   warps 2-5  epilogue: per token row, combine the 18 per-block dot products
+//              with the block scales, online softmax over the tile (lazy
+//              rescale of O in TMEM only when a head's max grows by > 2^8),
+//              P (f16) -> shared memory; at item end O / l -> output.
+//   warps 6-9  converter: V = f16(d * q) for the tile's 512 latent columns,
+//              16 tokens at a time, into the MN-major f16 operand layout.
+//
+// The QK path is exact (int32 accumulation per 32-element Q8_0 block), so the
+// only roundings are the query's two-digit int8 form (|err| <= amax/65024),
+// V and P in f16, and f32 accumulation.  Every mbarrier wait is bounded
+// (~2 s of clocks); on timeout the CTA sets KVCU_STATUS_TIMEOUT, every role
+// unwinds, in-flight copies and MMAs are waited for (bounded) and TMEM is freed.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <math.h>
+
+#include "kvcu_internal.h"
+
+namespace {
+
+constexpr int R = 512, P = 64, W = 576;
+constexpr int TILE = 128;            // tokens per tile (MMA M for QK)
+constexpr int NBLK = 18;             // Q8_0 blocks per row (16 latent + 2 rope)
+constexpr int NQK_MAX = 48;          // QK N: 2 digits x up to 24 heads
+constexpr int HMAX = NQK_MAX / 2;    // heads supported by the tensor-core kernel
+constexpr int NPV = 32;              // PV N: heads padded to 32
+constexpr int QK_SLOTS = 7;          // TMEM ring of per-block QK accumulators (cols 0..335)
+constexpr int PV_COL = 352;          // O^T accumulator: 4 M-tiles x 32 cols = [352, 480)
+constexpr int L_COL = 480;           // softmax denominators l[h] (ones x P^T) = [480, 512)
+constexpr int TMEM_COLS = 512;
+static_assert(QK_SLOTS * NQK_MAX <= PV_COL, "TMEM map");
+constexpr int VCH = 16;              // tokens per V chunk (one f16 MMA K-step)
+constexpr int NCH = TILE / VCH;      // 8 chunks per tile
+constexpr int NTHREADS = 320;        // 10 warps
+constexpr uint32_t MAGIC_I = 0x4B400000u;    // float 12582912 = 1.5 * 2^23
+constexpr float MAGIC_F = 12582912.0f;
+constexpr float RESCALE_LOG2 = 8.0f;         // lazy rescale threshold (factor 256)
+constexpr uint32_t STATUS_TIMEOUT = 0x10u;
+
+// ---- shared memory map (offsets from a 1024-aligned base) ----
+constexpr uint32_t ST_LAT = 0;                   // 4 x [128 rows][128 B], SW128
+constexpr uint32_t ST_ROPE = 4 * 16384;          // [128 rows][64 B], SW64
+constexpr uint32_t ST_SC = ST_ROPE + 8192;       // [128][18] u16 scales
+constexpr uint32_t STAGE_BYTES = 79872;          // 78,336 rounded up to 1024
+constexpr uint32_t OFF_QD = 2 * STAGE_BYTES;     // query digits: 4 x [<=48][128 B] + [<=48][64 B]
+constexpr uint32_t QD_LAT_BYTES = NQK_MAX * 128;  // 6144 per latent region
+constexpr uint32_t OFF_QD_ROPE = OFF_QD + 4 * QD_LAT_BYTES;
+constexpr uint32_t OFF_VR = OFF_QD + 4 * QD_LAT_BYTES + 3072;  // 187392: V chunk ring (2 x 16 KB)
+constexpr uint32_t VCH_BYTES = 16384;
+constexpr uint32_t OFF_P = OFF_VR + 2 * VCH_BYTES;            // P^T: 2 regions x [32][128 B]
+constexpr uint32_t OFF_MISC = OFF_P + 8192;                   // 228352
+// misc: barriers then small arrays
+constexpr int B_KV_FULL = 0, B_KV_EMPTY = 2, B_QK_FULL = 4, B_QK_EMPTY = 12, B_V_FULL = 20,
+              B_V_EMPTY = 22, B_P_FULL = 24, B_P_EMPTY = 25, B_PV_DONE = 26, B_PV_EMPTY = 27,
+              B_Q_FULL = 28, B_FINAL = 29, B_EPI = 30, NUM_BARS = 31;
+constexpr uint32_t OFF_TMEM_BASE = OFF_MISC + NUM_BARS * 8;   // u32
+constexpr uint32_t OFF_ABORT = OFF_TMEM_BASE + 4;             // u32
+constexpr uint32_t OFF_QSCALE = OFF_MISC + 256;               // float[24]
+constexpr uint32_t OFF_REDMAX = OFF_QSCALE + 128;             // float[2][4][24]
+constexpr uint32_t OFF_ONES = OFF_REDMAX + 2 * 4 * 24 * 4;    // 128 B of f16 1.0 (l = ones x P^T)
+constexpr uint32_t SMEM_USED = OFF_ONES + 128;
+constexpr uint32_t SMEM_ALLOC = SMEM_USED + 1024;             // slack for 1024 alignment
+static_assert(SMEM_ALLOC <= 232448, "shared memory budget");
+
+struct TcArgs {
+  uint32_t layer, num_blocks, block_size, box_rows;
+  const uint16_t* sc;  // f16 scale pool [rows][18]
+  uint32_t* status;
+  uint32_t n;
+  const uint32_t* seq_ids;
+  uint32_t n_seqs;
+  const uint32_t* toff;
+  const uint32_t* tables;
+  const uint32_t* lens;
+  const float* q;
+  uint32_t n_heads;
+  float scale_log2;    // softmax scale * log2(e)
+  float* out;
+  const kvcu_item* items;
+  const uint32_t* meta;
+  const uint32_t* seq_count;
+  float* part_o;
+  float* part_ml;
+  uint32_t ws_heads;
+};
+
+// ------------------------------------------------------------------ PTX helpers
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_tx(uint32_t bar, uint32_t tx) {
+  asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(tx)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: gives up after ~2^31 clocks (about a second) or when another
+// role has aborted; records the timeout in the status word.
+__device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile uint32_t* abort_flag,
+                                       uint32_t* status) {
+  if (mbar_try(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (true) {
+    if (mbar_try(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (clock64() - t0 > (1ll << 31)) {
+      *abort_flag = 1u;
+      atomicOr(status, STATUS_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void fence_proxy_async() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
+// UMMA shared-memory descriptor (sm_100): start>>4 @0, LBO>>4 @16, SBO>>4 @32,
+// version 1 @46, layout type @61 (2 = 128B swizzle, 4 = 64B swizzle).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo,
+                                              uint32_t layout) {
+  return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | ((uint64_t)layout << 61);
+}
+constexpr uint32_t LAYOUT_SW128 = 2, LAYOUT_SW64 = 4;
+
+// Instruction descriptors: kind::i8 (s8 x s8 -> s32, both K-major, M=128, N=nqk)
+// and kind::f16 (f16 x f16 -> f32, A MN-major, B K-major, M=128, N=32).
+constexpr uint32_t idesc_qk(int nqk) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(nqk >> 3) << 17) | ((uint32_t)(TILE >> 4) << 24);
+}
+// Head bucket HK (8, 16, 20 or 24 heads per kernel instance): the query digit
+// rows are [0, HK) for digit 0 and [HK, 2HK) for digit 1, N = 2HK rounded to 16.
+template <int HK>
+struct Cfg {
+  static constexpr int NQK = (2 * HK + 15) / 16 * 16;
+  static_assert(NQK <= NQK_MAX, "head bucket too large");
+};
+constexpr uint32_t IDESC_PV = (1u << 4) | (0u << 7) | (0u << 10) | (1u << 15) |
+                              ((uint32_t)(NPV >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+// l-accumulation: A = all-ones (K-major, no swizzle, zero strides: every row and
+// K index reads the same 128-byte block of 1.0), B = P^T as in PV.
+constexpr uint32_t IDESC_L = (1u << 4) | ((uint32_t)(NPV >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+constexpr uint32_t LAYOUT_NONE = 0;
+
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+               : "memory");
+}
+
+#define TMEM_LD32(taddr, r)                                                                         \
+  asm volatile(                                                                                     \
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14," \
+      "%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"              \
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),         \
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),     \
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]),  \
+        "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]),  \
+        "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])                                          \
+      : "r"(taddr))
+#define TMEM_LD16(taddr, r)                                                                         \
+  asm volatile(                                                                                     \
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14," \
+      "%15}, [%16];"                                                                                \
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),         \
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),     \
+        "=r"(r[14]), "=r"(r[15])                                                                    \
+      : "r"(taddr))
+#define TMEM_LD8(taddr, r)                                                                          \
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"              \
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),            \
+                 "=r"(r[6]), "=r"(r[7])                                                             \
+               : "r"(taddr))
+#define TMEM_ST16(taddr, r)                                                                         \
+  asm volatile(                                                                                     \
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13," \
+      "%14,%15,%16};" ::"r"(taddr),                                                                 \
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),       \
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])  \
+      : "memory")
+#define TMEM_ST8(taddr, r)                                                                          \
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), \
+               "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]),         \
+               "r"(r[7])                                                                            \
+               : "memory")
+
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// Byte offset of (row, byte) inside a K-major 128B-swizzled region whose rows
+// are 128 B and whose 8-row atoms are 1024 B apart (region base 1024-aligned).
+__device__ __forceinline__ uint32_t sw128_off(uint32_t row, uint32_t byte) {
+  return (row >> 3) * 1024u + (row & 7u) * 128u + ((((byte >> 4) ^ row) & 7u) << 4) + (byte & 15u);
+}
+// Same for 64-byte rows with the 64B swizzle (8-row atoms of 512 B).
+__device__ __forceinline__ uint32_t sw64_off(uint32_t row, uint32_t byte) {
+  return (row >> 3) * 512u + (row & 7u) * 64u + ((((byte >> 4) ^ ((row & 7u) >> 1)) & 3u) << 4) +
+         (byte & 15u);
+}
+
+struct Item {
+  uint32_t b, s, t0, t1, tok0, tok1;  // entry, sequence, table range, token range
+  uint32_t ntiles;
+};
+
+__device__ __forceinline__ Item load_item(const TcArgs& a, uint32_t it) {
+  const kvcu_item ki = a.items[it];
+  Item r;
+  r.b = ki.b;
+  r.s = a.seq_ids ? a.seq_ids[ki.b] : ki.b;
+  r.t0 = r.t1 = 0;
+  uint32_t len = 0;
+  if (r.s < a.n_seqs) {
+    r.t0 = a.toff[r.s];
+    r.t1 = a.toff[r.s + 1];
+    if (r.t1 < r.t0) r.t1 = r.t0;
+    len = a.lens[r.s];
+    const uint64_t cap = (uint64_t)(r.t1 - r.t0) * a.block_size;
+    if (len > cap) len = (uint32_t)cap;
+  }
+  r.tok0 = ki.start;
+  r.tok1 = min(ki.end, len);
+  r.ntiles = r.tok1 > r.tok0 ? (r.tok1 - r.tok0 + TILE - 1) / TILE : 0u;
+  return r;
+}
+
+// ------------------------------------------------------------------ the kernel
+template <int HK>
+__global__ void __launch_bounds__(NTHREADS, 1)
+    k_decode_tc(const __grid_constant__ CUtensorMap map_lat, const __grid_constant__ CUtensorMap map_rope,
+                TcArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+  auto bar = [&](int i) { return sbase + OFF_MISC + 8u * (uint32_t)i; };
+  volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + OFF_ABORT);
+  const uint32_t n_items = a.meta[0];
+  const uint32_t H = a.n_heads;
+
+  // ---- set-up: barriers, TMEM
+  if (threadIdx.x == 0) {
+    mbar_init(bar(B_KV_FULL + 0), 1);
+    mbar_init(bar(B_KV_FULL + 1), 1);
+    mbar_init(bar(B_KV_EMPTY + 0), 9);
+    mbar_init(bar(B_KV_EMPTY + 1), 9);
+    for (int i = 0; i < QK_SLOTS; ++i) {
+      mbar_init(bar(B_QK_FULL + i), 1);
+      mbar_init(bar(B_QK_EMPTY + i), 4);
+    }
+    mbar_init(bar(B_V_FULL + 0), 4);
+    mbar_init(bar(B_V_FULL + 1), 4);
+    mbar_init(bar(B_V_EMPTY + 0), 1);
+    mbar_init(bar(B_V_EMPTY + 1), 1);
+    mbar_init(bar(B_P_FULL), 4);
+    mbar_init(bar(B_P_EMPTY), 1);
+    mbar_init(bar(B_PV_DONE), 1);
+    mbar_init(bar(B_PV_EMPTY), 4);
+    mbar_init(bar(B_Q_FULL), 4);
+    mbar_init(bar(B_FINAL), 1);
+    mbar_init(bar(B_EPI), 4);
+    *abort_flag = 0u;
+    uint32_t* ones = reinterpret_cast<uint32_t*>(smem + OFF_ONES);
+    for (int i = 0; i < 32; ++i) ones[i] = 0x3C003C00u;  // f16 1.0 pairs
+    fence_proxy_async();
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     sbase + OFF_TMEM_BASE),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + OFF_TMEM_BASE);
+
+  if (warp >= 2 && warp < 6) {
+    // epilogue warps pre-load every QK slot with the conversion bias
+    const uint32_t q = warp & 3u;
+    uint32_t mg[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) mg[i] = MAGIC_I;
+    for (int c = 0; c < QK_SLOTS * Cfg<HK>::NQK; c += 16) TMEM_ST16(tmem + ((32u * q) << 16) + (uint32_t)c, mg);
+    tmem_wait_st();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+
+  if (warp == 0) {
+    // ================================================================ producer
+    if (lane == 0) {
+      uint32_t g = 0;
+      const uint32_t br = a.box_rows;
+      for (uint32_t it = blockIdx.x; it < n_items && !*abort_flag; it += gridDim.x) {
+        const Item im = load_item(a, it);
+        for (uint32_t k = 0; k < im.ntiles && !*abort_flag; ++k, ++g) {
+          const uint32_t s = g & 1u;
+          if (!mbar_wait(bar(B_KV_EMPTY + s), ((g >> 1) & 1u) ^ 1u, abort_flag, a.status)) break;
+          const uint32_t tt0 = im.tok0 + k * TILE;
+          const uint32_t tt1 = min(tt0 + TILE, im.tok1);
+          // count the bytes first (one arrive.expect_tx per stage)
+          uint32_t segs = 0, bytes = 0;
+          for (uint32_t off = 0; tt0 + off < tt1; off += br) {
+            const uint32_t pos = tt0 + off;
+            const uint32_t blk = a.tables[im.t0 + pos / a.block_size];
+            if (blk < a.num_blocks) {
+              segs++;
+              bytes += br * (4u * 128u + 64u + 36u);
+            } else {
+              atomicOr(a.status, KVCU_STATUS_BAD_BLOCK);
+            }
+          }
+          (void)segs;
+          const uint32_t stage = sbase + s * STAGE_BYTES;
+          mbar_arrive_tx(bar(B_KV_FULL + s), bytes);
+          for (uint32_t off = 0; tt0 + off < tt1; off += br) {
+            const uint32_t pos = tt0 + off;
+            const uint32_t blk = a.tables[im.t0 + pos / a.block_size];
+            if (blk >= a.num_blocks) continue;
+            const uint64_t row =
+                ((uint64_t)a.layer * a.num_blocks + blk) * a.block_size + pos % a.block_size;
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              tma_load_2d(stage + ST_LAT + (uint32_t)j * 16384u + off * 128u, &map_lat, j * 128, (int)row,
+                          bar(B_KV_FULL + s));
+            tma_load_2d(stage + ST_ROPE + off * 64u, &map_rope, 512, (int)row, bar(B_KV_FULL + s));
+            bulk_load(stage + ST_SC + off * 36u, a.sc + row * NBLK, br * 36u, bar(B_KV_FULL + s));
+          }
+        }
+      }
+      // wait (bounded) for the copies of the last two stages to land
+      for (uint32_t k = (g >= 2 ? g - 2 : 0); k < g; ++k)
+        mbar_wait(bar(B_KV_FULL + (k & 1u)), (k >> 1) & 1u, abort_flag, a.status);
+    }
+  } else if (warp == 1) {
+    // ================================================================ MMA issuer
+    if (lane == 0) {
+      uint32_t g = 0, item_no = 0;
+      uint32_t prev_valid = 0, prev_g = 0, prev_first = 0;  // pending PV tile
+      bool ok = true;
+      auto issue_pv = [&](uint32_t pg, uint32_t first_of_item, uint32_t item_ord) -> bool {
+        if (first_of_item && item_ord > 0) {
+          // the epilogue drained the previous item's O
+          if (!mbar_wait(bar(B_PV_EMPTY), (item_ord - 1) & 1u, abort_flag, a.status)) return false;
+        }
+        if (!mbar_wait(bar(B_P_FULL), pg & 1u, abort_flag, a.status)) return false;
+        tc_fence_after();
+        for (uint32_t c = 0; c < NCH; ++c) {
+          const uint32_t kv = pg * NCH + c, vs = kv & 1u;
+          if (!mbar_wait(bar(B_V_FULL + vs), (kv >> 1) & 1u, abort_flag, a.status)) return false;
+          tc_fence_after();
+          const uint32_t vbase = sbase + OFF_VR + vs * VCH_BYTES;
+          const uint32_t pbase = sbase + OFF_P + (c >> 2) * 4096u + (c & 3u) * 32u;
+          const uint64_t bdesc = smem_desc(pbase, 16, 1024, LAYOUT_SW128);
+          const uint32_t acc_flag = (first_of_item && c == 0) ? 0u : 1u;
+#pragma unroll
+          for (uint32_t mt = 0; mt < 4; ++mt) {
+            const uint64_t adesc = smem_desc(vbase + mt * 4096u, 2048, 1024, LAYOUT_SW128);
+            mma_f16(tmem + PV_COL + mt * NPV, adesc, bdesc, IDESC_PV, acc_flag);
+          }
+          mma_f16(tmem + L_COL, smem_desc(sbase + OFF_ONES, 0, 0, LAYOUT_NONE), bdesc, IDESC_L, acc_flag);
+          mma_commit(bar(B_V_EMPTY + vs));
+        }
+        mma_commit(bar(B_PV_DONE));
+        mma_commit(bar(B_P_EMPTY));
+        return true;
+      };
+      uint32_t prev_item_ord = 0;
+      for (uint32_t it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+        const Item im = load_item(a, it);
+        if (im.ntiles == 0) continue;
+        // The previous item's last PV goes first: the epilogue drains that item
+        // before it writes this item's query digits (no circular wait).
+        if (prev_valid) {
+          if (!issue_pv(prev_g, prev_first, prev_item_ord)) break;
+          prev_valid = 0;
+        }
+        if (!mbar_wait(bar(B_Q_FULL), item_no & 1u, abort_flag, a.status)) break;
+        tc_fence_after();
+        for (uint32_t k = 0; k < im.ntiles; ++k, ++g) {
+          const uint32_t s = g & 1u;
+          if (!mbar_wait(bar(B_KV_FULL + s), (g >> 1) & 1u, abort_flag, a.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t stage = sbase + s * STAGE_BYTES;
+          for (uint32_t b = 0; b < NBLK; ++b) {
+            const uint32_t kk = g * NBLK + b, slot = kk % QK_SLOTS;
+            if (!mbar_wait(bar(B_QK_EMPTY + slot), ((kk / QK_SLOTS) & 1u) ^ 1u, abort_flag, a.status)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            uint64_t ad, bd;
+            if (b < 16) {
+              ad = smem_desc(stage + ST_LAT + (b >> 2) * 16384u + (b & 3u) * 32u, 16, 1024, LAYOUT_SW128);
+              bd = smem_desc(sbase + OFF_QD + (b >> 2) * QD_LAT_BYTES + (b & 3u) * 32u, 16, 1024,
+                             LAYOUT_SW128);
+            } else {
+              ad = smem_desc(stage + ST_ROPE + (b - 16u) * 32u, 16, 512, LAYOUT_SW64);
+              bd = smem_desc(sbase + OFF_QD_ROPE + (b - 16u) * 32u, 16, 512, LAYOUT_SW64);
+            }
+            mma_i8(tmem + slot * Cfg<HK>::NQK, ad, bd, idesc_qk(Cfg<HK>::NQK), 1u);
+            mma_commit(bar(B_QK_FULL + slot));
+          }
+          if (!ok) break;
+          mma_commit(bar(B_KV_EMPTY + s));
+          // PV of the previous tile of this item (it overlaps this tile's QK epilogue)
+          if (prev_valid && !issue_pv(prev_g, prev_first, prev_item_ord)) {
+            ok = false;
+            break;
+          }
+          prev_valid = 1;
+          prev_g = g;
+          prev_first = (k == 0);
+          prev_item_ord = item_no;
+        }
+        ++item_no;
+      }
+      if (ok && prev_valid) issue_pv(prev_g, prev_first, prev_item_ord);
+      // all issued tcgen05 work retires before TMEM is freed
+      mma_commit(bar(B_FINAL));
+      mbar_wait(bar(B_FINAL), 0, abort_flag, a.status);
+    }
+  } else if (warp < 6) {
+    // ================================================================ epilogue
+    const uint32_t q4 = warp & 3u;             // TMEM lane quarter
+    const uint32_t trow = 32u * q4 + lane;     // token row in the tile / latent row in an M-tile
+    const uint32_t ew = warp - 2u;             // 0..3
+    const uint32_t lane_addr = (32u * q4) << 16;
+    float* qscale = reinterpret_cast<float*>(smem + OFF_QSCALE);
+    float* redmax = reinterpret_cast<float*>(smem + OFF_REDMAX);
+    uint32_t g = 0, esync = 0;
+    bool ok = true;
+    // bounded barrier among the 4 epilogue warps (an mbarrier, so a timeout
+    // elsewhere cannot strand a warp in bar.sync)
+    auto epi_sync = [&]() -> bool {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(B_EPI));
+      const bool r = mbar_wait(bar(B_EPI), esync & 1u, abort_flag, a.status);
+      ++esync;
+      return r;
+    };
+    for (uint32_t it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+      const Item im = load_item(a, it);
+      const bool single = a.seq_count[im.b] == 1;
+      if (im.ntiles == 0) {
+        // empty item: zeros, or an empty partial
+        for (uint32_t i = ew * 32 + lane; i < H * (uint32_t)R; i += 128) {
+          const uint32_t h = i / R, c = i % R;
+          if (single) a.out[((uint64_t)im.b * H + h) * R + c] = 0.f;
+          else a.part_o[((uint64_t)it * a.ws_heads + h) * R + c] = 0.f;
+        }
+        if (!single && ew == 0 && lane < H) {
+          a.part_ml[((uint64_t)it * a.ws_heads + lane) * 2 + 0] = -INFINITY;
+          a.part_ml[((uint64_t)it * a.ws_heads + lane) * 2 + 1] = 0.f;
+        }
+        continue;
+      }
+      // ---- query -> two int8 digits per element (x = s_h * (d0 + d1/256)), per-head scale
+      {
+        const float* qb = a.q + (uint64_t)im.b * H * W;
+        for (uint32_t h = ew; h < (uint32_t)HK; h += 4) {
+          float amax = 0.f;
+          float v[18];
+#pragma unroll
+          for (int j = 0; j < 18; ++j) {
+            v[j] = h < H ? qb[(uint64_t)h * W + lane + 32 * j] : 0.f;
+            amax = fmaxf(amax, fabsf(v[j]));
+          }
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+          const float sh = amax > 0.f ? amax / 127.0f : 1.0f;
+          const float inv = 1.0f / sh;
+#pragma unroll
+          for (int j = 0; j < 18; ++j) {
+            const uint32_t kcol = lane + 32u * j;
+            const float x = v[j] * inv;
+            const float d0 = fminf(fmaxf(rintf(x), -127.f), 127.f);
+            const float d1 = fminf(fmaxf(rintf((x - d0) * 256.f), -127.f), 127.f);
+            uint8_t* base;
+            uint32_t o0, o1;
+            if (kcol < 512) {
+              base = smem + OFF_QD + (kcol >> 7) * QD_LAT_BYTES;
+              o0 = sw128_off(h, kcol & 127u);
+              o1 = sw128_off(h + HK, kcol & 127u);
+            } else {
+              base = smem + OFF_QD_ROPE;
+              o0 = sw64_off(h, kcol - 512u);
+              o1 = sw64_off(h + HK, kcol - 512u);
+            }
+            base[o0] = (uint8_t)(int8_t)(int)d0;
+            base[o1] = (uint8_t)(int8_t)(int)d1;
+          }
+          if (lane == 0) qscale[h] = sh * (1.0f / 256.0f) * a.scale_log2;
+        }
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(B_Q_FULL));
+        if (!epi_sync()) break;  // qscale visible to every epilogue thread
+      }
+      float m_ref[HK];
+#pragma unroll
+      for (int h = 0; h < HK; ++h) m_ref[h] = -INFINITY;
+      for (uint32_t k = 0; k < im.ntiles && ok; ++k, ++g) {
+        const uint32_t s = g & 1u;
+        const uint32_t tt0 = im.tok0 + k * TILE;
+        const bool valid = tt0 + trow < im.tok1;
+        // raw stage s holds this tile's block scales
+        if (!mbar_wait(bar(B_KV_FULL + s), (g >> 1) & 1u, abort_flag, a.status)) {
+          ok = false;
+          break;
+        }
+        const uint16_t* scrow =
+            reinterpret_cast<const uint16_t*>(smem + s * STAGE_BYTES + ST_SC) + trow * NBLK;
+        float acc[HK];
+#pragma unroll
+        for (int h = 0; h < HK; ++h) acc[h] = 0.f;
+        for (uint32_t b = 0; b < NBLK; ++b) {
+          const uint32_t kk = g * NBLK + b, slot = kk % QK_SLOTS;
+          if (!mbar_wait(bar(B_QK_FULL + slot), (kk / QK_SLOTS) & 1u, abort_flag, a.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          // columns [0, HK): digit 0 of each head, [HK, 2HK): digit 1
+          constexpr int NQ = Cfg<HK>::NQK;
+          constexpr int NL = 2 * HK;  // columns actually used
+          uint32_t r[NL];
+          const uint32_t ta = tmem + lane_addr + slot * NQ;
+          if constexpr (NL >= 32) {
+            TMEM_LD32(ta, r);
+            if constexpr (NL == 48) TMEM_LD16(ta + 32, (r + 32));
+            if constexpr (NL == 40) TMEM_LD8(ta + 32, (r + 32));
+          } else {
+            TMEM_LD16(ta, r);
+          }
+          tmem_wait_ld();
+          {
+            uint32_t mg[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) mg[i] = MAGIC_I;
+#pragma unroll
+            for (int c = 0; c < NQ; c += 16) TMEM_ST16(ta + (uint32_t)c, mg);
+            tmem_wait_st();
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(B_QK_EMPTY + slot));
+          const float d = __half2float(__ushort_as_half(scrow[b]));
+#pragma unroll
+          for (int h = 0; h < HK; ++h) {
+            const float x0 = __uint_as_float(r[h]) - MAGIC_F;  // exact: |dot| < 2^22
+            const float x1 = __uint_as_float(r[h + HK]) - MAGIC_F;
+            acc[h] = fmaf(d, fmaf(x0, 256.f, x1), acc[h]);
+          }
+        }
+        if (!ok) break;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(B_KV_EMPTY + s));  // done with the stage's scales
+        // ---- online softmax over the tile (log2 domain): scores into acc[]
+#pragma unroll
+        for (int h = 0; h < HK; ++h) {
+          const float v = acc[h] * qscale[h];
+          acc[h] = (valid && h < (int)H && v == v) ? v : -INFINITY;
+        }
+        float* rm = redmax + (g & 1u) * (4 * 24);
+#pragma unroll
+        for (int h = 0; h < HK; ++h) {
+          float m = acc[h];
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+          if (lane == 0) rm[ew * 24 + h] = m;
+        }
+        if (!epi_sync()) {
+          ok = false;
+          break;
+        }
+        // lazy rescale: a head's reference max moves only when the tile max
+        // exceeds it by more than 2^8 (so P <= 256 otherwise)
+        auto tile_max = [&](int h) {
+          return fmaxf(fmaxf(rm[h], rm[24 + h]), fmaxf(rm[48 + h], rm[72 + h]));
+        };
+        bool need_rescale = false;
+#pragma unroll
+        for (int h = 0; h < HK; ++h)
+          need_rescale |= (m_ref[h] != -INFINITY) && (tile_max(h) > m_ref[h] + RESCALE_LOG2);
+        if (need_rescale) {
+          // O holds the PV of this item's earlier tiles: retire it, then scale
+          if (!mbar_wait(bar(B_PV_DONE), (g - 1) & 1u, abort_flag, a.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          // the 4 O^T M-tiles and the l columns (index 4) share the head columns
+#pragma unroll 1
+          for (uint32_t mt = 0; mt < 5; ++mt) {
+            uint32_t o[32];
+            const uint32_t ta = tmem + lane_addr + (mt < 4 ? PV_COL + mt * NPV : L_COL);
+            TMEM_LD32(ta, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int h = 0; h < HK; ++h) {
+              const float tm = tile_max(h);
+              if (m_ref[h] != -INFINITY && tm > m_ref[h] + RESCALE_LOG2)
+                o[h] = __float_as_uint(__uint_as_float(o[h]) * exp2f(m_ref[h] - tm));
+            }
+            TMEM_ST16(ta, o);
+            TMEM_ST16(ta + 16, (o + 16));
+            tmem_wait_st();
+          }
+          tc_fence_before();
+        }
+#pragma unroll
+        for (int h = 0; h < HK; ++h) {
+          const float tm = tile_max(h);
+          if (tm > m_ref[h] + RESCALE_LOG2) m_ref[h] = tm;
+        }
+        // ---- P (f16) -> shared memory, K-major 128B-swizzled [head][token]
+        if (!mbar_wait(bar(B_P_EMPTY), (g & 1u) ^ 1u, abort_flag, a.status)) {
+          ok = false;
+          break;
+        }
+        {
+          uint8_t* pb = smem + OFF_P + (trow >> 6) * 4096u;
+          const uint32_t tb = (trow & 63u) * 2u;
+#pragma unroll
+          for (int h = 0; h < HK; ++h) {
+            const float p = acc[h] == -INFINITY ? 0.f : exp2f(acc[h] - m_ref[h]);
+            *reinterpret_cast<__half*>(pb + sw128_off((uint32_t)h, tb)) = __float2half_rn(p);
+          }
+        }
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(B_P_FULL));
+      }
+      if (!ok) break;
+      // ---- item end: l (every TMEM lane holds it), drain O, write the output or the partial
+      {
+        if (!mbar_wait(bar(B_PV_DONE), (g - 1) & 1u, abort_flag, a.status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        float ltot[HK];
+        {
+          uint32_t lv[32];
+          TMEM_LD32(tmem + lane_addr + L_COL, lv);
+          tmem_wait_ld();
+#pragma unroll
+          for (int h = 0; h < HK; ++h) ltot[h] = __uint_as_float(lv[h]);
+        }
+#pragma unroll 1
+        for (uint32_t mt = 0; mt < 4; ++mt) {
+          uint32_t o[32];
+          TMEM_LD32(tmem + lane_addr + PV_COL + mt * NPV, o);
+          tmem_wait_ld();
+          const uint32_t c = mt * 128u + trow;
+#pragma unroll
+          for (int h = 0; h < HK; ++h) {
+            if (h >= (int)H) continue;
+            const float v = __uint_as_float(o[h]);
+            if (single) {
+              a.out[((uint64_t)im.b * H + h) * R + c] = ltot[h] > 0.f ? v / ltot[h] : 0.f;
+            } else {
+              a.part_o[((uint64_t)it * a.ws_heads + h) * R + c] = v;
+            }
+          }
+        }
+        if (!single && ew == 0 && lane < H) {
+          const float ln2 = 0.69314718055994531f;
+          float mh = -INFINITY, lh = 0.f;
+#pragma unroll
+          for (int h = 0; h < HK; ++h)
+            if ((uint32_t)h == lane) {
+              mh = m_ref[h] * ln2;
+              lh = ltot[h];
+            }
+          a.part_ml[((uint64_t)it * a.ws_heads + lane) * 2 + 0] = mh;
+          a.part_ml[((uint64_t)it * a.ws_heads + lane) * 2 + 1] = lh;
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(B_PV_EMPTY));
+      }
+    }
+  } else {
+    // ================================================================ converter
+    const uint32_t cw = warp - 6u;                 // 0..3
+    const uint32_t tid = cw * 32u + lane;          // 0..127
+    const uint32_t tl = tid & 15u;                 // token within the chunk
+    const uint32_t gq = tid >> 4;                  // 64-column group (MN atom) 0..7
+    uint32_t g = 0;
+    bool ok = true;
+    for (uint32_t it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+      const Item im = load_item(a, it);
+      for (uint32_t k = 0; k < im.ntiles && ok; ++k, ++g) {
+        const uint32_t s = g & 1u;
+        const uint32_t tt0 = im.tok0 + k * TILE;
+        if (!mbar_wait(bar(B_KV_FULL + s), (g >> 1) & 1u, abort_flag, a.status)) {
+          ok = false;
+          break;
+        }
+        const uint8_t* stage = smem + s * STAGE_BYTES;
+        for (uint32_t c = 0; c < NCH; ++c) {
+          const uint32_t kv = g * NCH + c, vs = kv & 1u;
+          if (!mbar_wait(bar(B_V_EMPTY + vs), ((kv >> 1) & 1u) ^ 1u, abort_flag, a.status)) {
+            ok = false;
+            break;
+          }
+          const uint32_t t = c * VCH + tl;  // token row in the tile
+          const bool valid = tt0 + t < im.tok1;
+          uint8_t* vrow = smem + OFF_VR + vs * VCH_BYTES + gq * 2048u + (tl >> 3) * 1024u + (tl & 7u) * 128u;
+          if (valid) {
+            const uint32_t j = gq >> 1;                  // latent box
+            const uint8_t* src = stage + ST_LAT + j * 16384u;
+            const uint32_t sc2 = *reinterpret_cast<const uint32_t*>(stage + ST_SC + t * 36u + gq * 4u);
+            const __half2 d0 = __half2half2(__ushort_as_half((uint16_t)(sc2 & 0xFFFFu)));
+            const __half2 d1 = __half2half2(__ushort_as_half((uint16_t)(sc2 >> 16)));
+            const __half2 bias = __float2half2_rn(1152.0f);
+#pragma unroll
+            for (uint32_t i = 0; i < 4; ++i) {
+              const uint32_t logical = (gq & 1u) * 4u + i;  // 16-byte chunk within the 128-byte row
+              const uint4 raw = *reinterpret_cast<const uint4*>(src + sw128_off(t, logical * 16u));
+              const __half2 dd = i < 2 ? d0 : d1;
+              uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+              uint32_t hv[8];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const uint32_t u = w[e] ^ 0x80808080u;  // q + 128 per byte
+                const uint32_t lo = __byte_perm(u, 0x64646464u, 0x4140u);
+                const uint32_t hi = __byte_perm(u, 0x64646464u, 0x4342u);
+                __half2 a0 = __hsub2(*reinterpret_cast<const __half2*>(&lo), bias);
+                __half2 a1 = __hsub2(*reinterpret_cast<const __half2*>(&hi), bias);
+                a0 = __hmul2(a0, dd);
+                a1 = __hmul2(a1, dd);
+                hv[2 * e] = *reinterpret_cast<uint32_t*>(&a0);
+                hv[2 * e + 1] = *reinterpret_cast<uint32_t*>(&a1);
+              }
+              // 16 values = two 8-element (16-byte) chunks of the MN-major atom row
+#pragma unroll
+              for (uint32_t hlf = 0; hlf < 2; ++hlf) {
+                const uint32_t ch = 2u * i + hlf;  // chunk 0..7 along the 64 columns
+                *reinterpret_cast<uint4*>(vrow + (((ch ^ tl) & 7u) << 4)) =
+                    make_uint4(hv[4 * hlf], hv[4 * hlf + 1], hv[4 * hlf + 2], hv[4 * hlf + 3]);
+              }
+            }
+          } else {
+#pragma unroll
+            for (uint32_t ch = 0; ch < 8; ++ch)
+              *reinterpret_cast<uint4*>(vrow + (ch << 4)) = make_uint4(0, 0, 0, 0);
+          }
+          fence_proxy_async();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(B_V_FULL + vs));
+        }
+        if (!ok) break;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(B_KV_EMPTY + s));
+      }
+    }
+  }
+
+  // ---- teardown
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS)
+                 : "memory");
+  }
+}
+
+// ------------------------------------------------------------------ host side
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*,
+                                  CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                  CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+int make_maps(const kvcu_pool* p, uint32_t box_rows, CUtensorMap* lat, CUtensorMap* rope) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) {
+    kvcu_set_error("cuTensorMapEncodeTiled unavailable");
+    return KVCU_ERR_CUDA;
+  }
+  const uint64_t rows = p->rows();
+  const cuuint64_t dims[2] = {(cuuint64_t)W, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)W};
+  const cuuint32_t estr[2] = {1, 1};
+  const cuuint32_t box_lat[2] = {128, box_rows};
+  const cuuint32_t box_rope[2] = {64, box_rows};
+  CUresult r = enc(lat, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, p->qs, dims, strides, box_lat, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    kvcu_set_error("cuTensorMapEncodeTiled(latent) failed: %d", (int)r);
+    return KVCU_ERR_CUDA;
+  }
+  r = enc(rope, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, p->qs, dims, strides, box_rope, estr,
+          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    kvcu_set_error("cuTensorMapEncodeTiled(rope) failed: %d", (int)r);
+    return KVCU_ERR_CUDA;
+  }
+  return KVCU_OK;
+}
+
+template <int HK>
+int launch_tc(int grid, const CUtensorMap& lat, const CUtensorMap& rope, const TcArgs& a, cudaStream_t st) {
+  static bool configured = false;
+  if (!configured) {
+    int rc = kvcu_check_cuda(cudaFuncSetAttribute(k_decode_tc<HK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                  (int)SMEM_ALLOC),
+                             "cudaFuncSetAttribute(decode_tc)");
+    if (rc) return rc;
+    configured = true;
+  }
+  k_decode_tc<HK><<<grid, NTHREADS, SMEM_ALLOC, st>>>(lat, rope, a);
+  return kvcu_check_cuda(cudaGetLastError(), "decode_tc kernel launch");
+}
+
+}  // namespace
+
+// Whether the tensor-core kernel handles this pool / head count.
+bool kvcu_decode_tc_supported(const kvcu_pool* p, uint32_t n_heads) {
+  if (!p->quantized || p->kv_rank != (uint32_t)R || p->rope_dim != (uint32_t)P) return false;
+  if (n_heads == 0 || n_heads > (uint32_t)HMAX) return false;
+  if (p->block_size % 16 != 0) return false;
+  if (p->block_size < TILE && TILE % p->block_size != 0) return false;
+  if (p->block_size > TILE && p->block_size % TILE != 0) return false;
+  if (p->rows() > 0x7FFFFFFFull) return false;  // TMA coordinates are int32
+  return true;
+}
+
+int kvcu_launch_decode_tc(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint32_t n,
+                          const uint32_t* seq_ids, uint32_t n_seqs, const uint32_t* toff,
+                          const uint32_t* tables, const uint32_t* lens, const float* q,
+                          uint32_t n_heads, float scale, float* out, cudaStream_t st) {
+  const uint32_t box_rows = p->block_size < (uint32_t)TILE ? p->block_size : (uint32_t)TILE;
+  CUtensorMap lat, rope;
+  int rc = make_maps(p, box_rows, &lat, &rope);
+  if (rc) return rc;
+  TcArgs a;
+  a.layer = layer;
+  a.num_blocks = p->num_blocks;
+  a.block_size = p->block_size;
+  a.box_rows = box_rows;
+  a.sc = p->sc;
+  a.status = p->status;
+  a.n = n;
+  a.seq_ids = seq_ids;
+  a.n_seqs = n_seqs;
+  a.toff = toff;
+  a.tables = tables;
+  a.lens = lens;
+  a.q = q;
+  a.n_heads = n_heads;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  a.out = out;
+  a.items = ws->items;
+  a.meta = ws->meta;
+  a.seq_count = ws->seq_count;
+  a.part_o = ws->part_o;
+  a.part_ml = ws->part_ml;
+  a.ws_heads = ws->max_heads;
+  if (n_heads <= 8) return launch_tc<8>(ws->num_sms, lat, rope, a, st);
+  if (n_heads <= 16) return launch_tc<16>(ws->num_sms, lat, rope, a, st);
+  if (n_heads <= 20) return launch_tc<20>(ws->num_sms, lat, rope, a, st);
+  return launch_tc<24>(ws->num_sms, lat, rope, a, st);
+}

@@ -40,6 +40,8 @@ struct kvcu_decode_ws {
   uint32_t last_launches;
   int num_sms;
   int decode_ctas;           // resident decode CTAs (grid of the persistent kernel)
+  int impl;                  // KVCU_DECODE_AUTO / _CUDA_CORE / _TENSOR_CORE
+  int last_impl;             // the kernel the last decode used
 };
 
 // ---- error plumbing (kvcu_api.cu) ----
@@ -72,6 +74,12 @@ int kvcu_launch_synth(uint64_t seed, uint64_t a, uint32_t n_rows, const uint32_t
 int kvcu_decode_setup(kvcu_decode_ws* ws);
 int kvcu_launch_plan(kvcu_decode_ws* ws, const kvcu_pool* p, uint32_t n, const uint32_t* seq_ids,
                      uint32_t n_seqs, const uint32_t* lens, cudaStream_t st);
+// ---- tensor-core decode (kvcu_decode_tc.cu) ----
+bool kvcu_decode_tc_supported(const kvcu_pool* p, uint32_t n_heads);
+int kvcu_launch_decode_tc(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint32_t n,
+                          const uint32_t* seq_ids, uint32_t n_seqs, const uint32_t* toff,
+                          const uint32_t* tables, const uint32_t* lens, const float* q,
+                          uint32_t n_heads, float scale, float* out, cudaStream_t st);
 int kvcu_launch_decode(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint32_t n,
                        const uint32_t* seq_ids, uint32_t n_seqs, const uint32_t* table_offsets,
                        const uint32_t* tables, const uint32_t* lens, const float* q,

@@ -28,6 +28,7 @@ ERROR_NAMES = {
     -14: "OutOfMemory", -15: "BadBlockId", -16: "Unsupported", -17: "NoDevice",
 }
 NO_HASH = (1 << 64) - 1
+DECODE_AUTO, DECODE_CUDA_CORE, DECODE_TENSOR_CORE = 0, 1, 2
 
 
 class KVCudaError(RuntimeError):
@@ -70,6 +71,8 @@ _SIGS = {
     "kvcu_decode_plan": (_i32, [_vp, _vp, _u32, _vp, _u32, _vp, _vp]),
     "kvcu_mla_decode": (_i32, [_vp, _vp, _u32, _u32, _vp, _u32, _vp, _vp, _vp, _vp, _u32, _f32, _vp, _vp]),
     "kvcu_decode_last_launches": (_u32, [_vp]),
+    "kvcu_decode_ws_set_impl": (_i32, [_vp, _i32]),
+    "kvcu_decode_last_impl": (_i32, [_vp]),
     "kvcu_pool_read_checkpoint": (_i32, [_vp, _u64, _u64, _vp, _vp]),
     "kvcu_pool_write_checkpoint": (_i32, [_vp, _u64, _u64, _vp, _vp]),
     "kvcu_synth_rows": (_i32, [_u64, _u64, _u32, _vp, _vp, _u32, _f32, _vp, _vp]),
@@ -113,6 +116,8 @@ _SIGS = {
     "kvcache_mla_decode": (_i32, [_vp, _u32, _u32, _vp, _vp, _u32, _f32, _vp]),
     "kvcache_mla_decode_dev": (_i32, [_vp, _u32, _u32, _vp, _vp, _u32, _f32, _vp, _vp]),
     "kvcache_last_launches": (_u32, [_vp]),
+    "kvcache_set_decode_impl": (_i32, [_vp, _i32]),
+    "kvcache_last_decode_impl": (_i32, [_vp]),
     "kvcache_save_to_file_v2": (_i32, [_vp, _cp]),
     "kvcache_load_from_file_v2": (_i32, [_vp, _cp]),
 }
@@ -296,6 +301,13 @@ class DecodeWorkspace:
     @property
     def last_launches(self):
         return lib().kvcu_decode_last_launches(self._h)
+
+    def set_impl(self, impl):
+        check(lib().kvcu_decode_ws_set_impl(self._h, impl), "kvcu_decode_ws_set_impl")
+
+    @property
+    def last_impl(self):
+        return lib().kvcu_decode_last_impl(self._h)
 
 
 def synth_rows(seed, a, b, c, width, out, outlier_p=0.0, stream=None):
@@ -552,6 +564,13 @@ class KVCache:
     @property
     def last_launches(self):
         return lib().kvcache_last_launches(self._h)
+
+    def set_decode_impl(self, impl):
+        check(lib().kvcache_set_decode_impl(self._h, impl), "set_decode_impl")
+
+    @property
+    def last_decode_impl(self):
+        return lib().kvcache_last_decode_impl(self._h)
 
     def prefill_synthetic(self, layer, seqs, lens, seed, outlier_p=0.0, seq_tags=None,
                           chunk_rows=1 << 16, stream=None, start=None):

@@ -260,9 +260,12 @@ def test_q8_edge_values_bit_exact(kv, oracle):
 
 
 # ------------------------------------------------------------------ decode parity
-def _decode_case(kv, oracle, lens, bs, quant, n_heads, seed, outlier_p=0.0, n_layers=1):
+def _decode_case(kv, oracle, lens, bs, quant, n_heads, seed, outlier_p=0.0, n_layers=1, impl=None,
+                 expect_impl=None):
     nb = sum((int(L) + bs - 1) // bs for L in lens) + 3
     c, o, rows = _multi_seq_cache(kv, oracle, lens, bs, nb, seed, quant, outlier_p, n_layers)
+    if impl is not None:
+        c.set_decode_impl(impl)
     rng = np.random.default_rng(seed + 100)
     offs = [0]
     tabs = []
@@ -274,6 +277,8 @@ def _decode_case(kv, oracle, lens, bs, quant, n_heads, seed, outlier_p=0.0, n_la
     for layer in range(n_layers):
         q = rng.standard_normal((len(lens), n_heads, W)).astype(np.float32)
         got = c.mlaDecode(layer, q, np.arange(len(lens), dtype=np.uint32), SCALE)
+        if expect_impl is not None:
+            assert c.last_decode_impl == expect_impl
         want = o.attention_batch(layer, offs, tabs, np.array(lens, np.uint32), q, SCALE, n_threads=8)
         err = rel_err_rows(got, want)
         assert err <= REL_TOL, (layer, err)
@@ -285,23 +290,74 @@ def _decode_case(kv, oracle, lens, bs, quant, n_heads, seed, outlier_p=0.0, n_la
 
 def test_config3_decode_f32(kv, oracle):
     lens = np.random.default_rng(3).integers(1, 4097, 16).tolist()
-    _decode_case(kv, oracle, lens, 16, False, 20, 3)
+    _decode_case(kv, oracle, lens, 16, False, 20, 3, expect_impl=kv.DECODE_CUDA_CORE)
 
 
-def test_decode_q8_config4_shape_reduced(kv, oracle):
+@pytest.mark.parametrize("impl", [1, 2])
+def test_decode_q8_config4_shape_reduced(kv, oracle, impl):
     lens = np.random.default_rng(4).integers(1000, 9000, 6).tolist()
-    _decode_case(kv, oracle, lens, 64, True, 20, 4, outlier_p=0.01, n_layers=2)
+    _decode_case(kv, oracle, lens, 64, True, 20, 4, outlier_p=0.01, n_layers=2, impl=impl,
+                 expect_impl=impl)
 
 
-@pytest.mark.parametrize("bs", [16, 32, 64, 128])
+@pytest.mark.parametrize("bs", [16, 32, 64, 128, 256])
 def test_decode_block_sizes_and_ragged_lengths(kv, oracle, bs):
-    lens = [0, 1, 15, 16, 17, 63, 64, 65, 127, 129, 300]
-    _decode_case(kv, oracle, lens, bs, True, 20, 10 + bs)
+    lens = [0, 1, 15, 16, 17, 63, 64, 65, 127, 129, 300, 1000]
+    _decode_case(kv, oracle, lens, bs, True, 20, 10 + bs, expect_impl=kv.DECODE_TENSOR_CORE)
 
 
-@pytest.mark.parametrize("n_heads", [1, 4, 7, 16, 24, 32])
+@pytest.mark.parametrize("n_heads", [1, 4, 7, 8, 9, 16, 17, 20, 21, 24, 25, 32])
 def test_decode_head_counts(kv, oracle, n_heads):
-    _decode_case(kv, oracle, [5, 200, 1000], 16, True, n_heads, 50 + n_heads)
+    expect = kv.DECODE_TENSOR_CORE if n_heads <= 24 else kv.DECODE_CUDA_CORE
+    _decode_case(kv, oracle, [5, 200, 1000], 16, True, n_heads, 50 + n_heads, expect_impl=expect)
+
+
+def test_decode_tensor_core_vs_cuda_core_same_data(kv, oracle):
+    lens = [1, 130, 4000, 9000]
+    c = _decode_case(kv, oracle, lens, 64, True, 20, 77, outlier_p=0.01)
+    q = np.random.default_rng(78).standard_normal((len(lens), 20, W)).astype(np.float32)
+    ids = np.arange(len(lens), dtype=np.uint32)
+    c.set_decode_impl(kv.DECODE_TENSOR_CORE)
+    a = c.mlaDecode(0, q, ids, SCALE)
+    assert c.last_decode_impl == kv.DECODE_TENSOR_CORE
+    c.set_decode_impl(kv.DECODE_CUDA_CORE)
+    b = c.mlaDecode(0, q, ids, SCALE)
+    assert c.last_decode_impl == kv.DECODE_CUDA_CORE
+    assert rel_err_rows(a, b) <= REL_TOL
+
+
+def test_decode_lazy_rescale_when_scores_jump(kv, oracle):
+    """Late tokens with much larger scores force the tensor-core kernel to
+    rescale the TMEM accumulators (max grows by far more than 2^8)."""
+    L, bs = 3000, 64
+    c = kv.KVCache.with_blocks(1, R, P, (L + bs - 1) // bs + 1, bs, quantized=True)
+    o = oracle.Pool(1, (L + bs - 1) // bs + 1, bs, R, P, True)
+    c.ensureCapacity(L)
+    rows = gen_seq_rows(oracle, 91, 0, 0, L, 0.0)
+    rows[1500:] *= np.float32(4.0)
+    rows[2900:] *= np.float32(3.0)
+    c.appendBatch(0, np.zeros(L, np.uint32), np.arange(L, dtype=np.uint32), rows)
+    tab = np.array(c.block_table, np.uint32)
+    t = np.arange(L)
+    o.put_rows(0, tab[t // bs], t % bs, rows)
+    q = np.random.default_rng(92).standard_normal((1, 20, W)).astype(np.float32)
+    got = c.mlaDecode(0, q, np.zeros(1, np.uint32), SCALE)
+    assert c.last_decode_impl == kv.DECODE_TENSOR_CORE
+    want = o.attention(0, tab, L, q[0], SCALE)[None]
+    assert rel_err_rows(got, want) <= REL_TOL
+
+
+def test_tensor_core_forced_on_f32_pool_is_unsupported(kv):
+    c = kv.KVCache.with_blocks(1, R, P, 4, 16, quantized=False)
+    c.ensureCapacity(16)
+    c.appendBatch(0, np.zeros(3, np.uint32), np.arange(3, dtype=np.uint32), np.ones((3, W), np.float32))
+    c.set_decode_impl(kv.DECODE_TENSOR_CORE)
+    with pytest.raises(kv.KVCudaError) as e:
+        c.mlaDecode(0, np.ones((1, 20, W), np.float32), np.zeros(1, np.uint32), SCALE)
+    assert e.value.name == "Unsupported"
+    c.set_decode_impl(kv.DECODE_AUTO)
+    out = c.mlaDecode(0, np.ones((1, 20, W), np.float32), np.zeros(1, np.uint32), SCALE)
+    assert np.allclose(out, 1.0)
 
 
 def test_decode_device_api_plan_reuse_with_growth(kv, oracle, torch_mod):
