@@ -67,6 +67,8 @@ extern "C" {
 #define KVCU_STATUS_BAD_BLOCK 0x2u   /* table entry >= num_blocks */
 #define KVCU_STATUS_BAD_SEQ 0x4u     /* sequence id >= n_seqs */
 #define KVCU_STATUS_BAD_LEN 0x8u     /* lens[s] > table length * block_size */
+#define KVCU_STATUS_TIMEOUT 0x10u    /* a bounded device-side wait gave up */
+#define KVCU_STATUS_MISALIGNED 0x20u /* a decode tile did not start on a block-row boundary */
 
 /* metal_get_last_error, src/metal_bridge.c:50-52.  Thread-local. */
 const char* kvcu_get_last_error(void);

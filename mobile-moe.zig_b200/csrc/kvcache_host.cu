@@ -769,8 +769,7 @@ int kvcache_mla_decode(kvcache* c, uint32_t layer, uint32_t n, const uint32_t* s
   rc = decode_impl(c, layer, n, seq_ids, c->d_f, n_heads, scale, c->d_f2, c->stream);
   if (rc) return rc;
   KVCU_CUDA(cudaMemcpyAsync(out, c->d_f2, on * 4, cudaMemcpyDeviceToHost, c->stream));
-  KVCU_CUDA(cudaStreamSynchronize(c->stream));
-  return KVCU_OK;
+  return check_status(c);  // synchronises; bad indices / timeouts become KVCU_ERR_DEVICE
 }
 
 int kvcache_mla_decode_dev(kvcache* c, uint32_t layer, uint32_t n, const uint32_t* seq_ids,

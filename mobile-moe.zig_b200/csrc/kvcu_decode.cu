@@ -70,9 +70,12 @@ __device__ __forceinline__ float warp_sum(float v) {
 }
 
 // ------------------------------------------------------------------ plan
+// Items start at multiples of `align` (= max(128, block size)), so every
+// 128-token tile of the tensor-core kernel covers whole physical blocks (or a
+// 128-row-aligned part of one).
 __global__ void __launch_bounds__(1024) k_plan(uint32_t n, const uint32_t* __restrict__ seq_ids,
                                                uint32_t n_seqs, const uint32_t* __restrict__ lens,
-                                               uint32_t target_items, uint32_t max_items,
+                                               uint32_t target_items, uint32_t align, uint32_t max_items,
                                                kvcu_item* __restrict__ items,
                                                uint32_t* __restrict__ meta,
                                                uint32_t* __restrict__ seq_first,
@@ -95,8 +98,8 @@ __global__ void __launch_bounds__(1024) k_plan(uint32_t n, const uint32_t* __res
   __syncthreads();
   const unsigned long long total = s_total;
   unsigned long long c = (total + target_items - 1) / (target_items ? target_items : 1);
-  c = (c + TT - 1) / TT * TT;
-  if (c < TT) c = TT;
+  c = (c + align - 1) / align * align;
+  if (c < align) c = align;
   if (c > 0x40000000ull) c = 0x40000000ull;
   const uint32_t C = (uint32_t)c;
   for (uint32_t base = 0; base < n; base += blockDim.x) {
@@ -450,9 +453,9 @@ int kvcu_decode_setup(kvcu_decode_ws* ws) {
 
 int kvcu_launch_plan(kvcu_decode_ws* ws, const kvcu_pool* p, uint32_t n, const uint32_t* seq_ids,
                      uint32_t n_seqs, const uint32_t* lens, cudaStream_t st) {
-  (void)p;
   const uint32_t target = (uint32_t)ws->decode_ctas * TARGET_WAVES;
-  k_plan<<<1, 1024, 0, st>>>(n, seq_ids, n_seqs, lens, target, ws->max_items, ws->items,
+  const uint32_t align = p->block_size > 128u ? p->block_size : 128u;
+  k_plan<<<1, 1024, 0, st>>>(n, seq_ids, n_seqs, lens, target, align, ws->max_items, ws->items,
                              ws->meta, ws->seq_first, ws->seq_count);
   return kvcu_check_cuda(cudaGetLastError(), "plan kernel launch");
 }

@@ -55,7 +55,7 @@ constexpr int NTHREADS = 320;        // 10 warps
 constexpr uint32_t MAGIC_I = 0x4B400000u;    // float 12582912 = 1.5 * 2^23
 constexpr float MAGIC_F = 12582912.0f;
 constexpr float RESCALE_LOG2 = 8.0f;         // lazy rescale threshold (factor 256)
-constexpr uint32_t STATUS_TIMEOUT = 0x10u;
+constexpr uint32_t STATUS_TIMEOUT = KVCU_STATUS_TIMEOUT;
 
 // ---- shared memory map (offsets from a 1024-aligned base) ----
 constexpr uint32_t ST_LAT = 0;                   // 4 x [128 rows][128 B], SW128
@@ -381,14 +381,18 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           const uint32_t tt1 = min(tt0 + TILE, im.tok1);
           // count the bytes first (one arrive.expect_tx per stage)
           uint32_t segs = 0, bytes = 0;
+          // every segment is one box of br rows inside one physical block (the
+          // plan aligns items to max(128, block size); anything else is refused)
           for (uint32_t off = 0; tt0 + off < tt1; off += br) {
             const uint32_t pos = tt0 + off;
             const uint32_t blk = a.tables[im.t0 + pos / a.block_size];
-            if (blk < a.num_blocks) {
+            if (blk >= a.num_blocks) {
+              atomicOr(a.status, KVCU_STATUS_BAD_BLOCK);
+            } else if (pos % a.block_size + br > a.block_size) {
+              atomicOr(a.status, KVCU_STATUS_MISALIGNED);
+            } else {
               segs++;
               bytes += br * (4u * 128u + 64u + 36u);
-            } else {
-              atomicOr(a.status, KVCU_STATUS_BAD_BLOCK);
             }
           }
           (void)segs;
@@ -397,7 +401,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           for (uint32_t off = 0; tt0 + off < tt1; off += br) {
             const uint32_t pos = tt0 + off;
             const uint32_t blk = a.tables[im.t0 + pos / a.block_size];
-            if (blk >= a.num_blocks) continue;
+            if (blk >= a.num_blocks || pos % a.block_size + br > a.block_size) continue;
             const uint64_t row =
                 ((uint64_t)a.layer * a.num_blocks + blk) * a.block_size + pos % a.block_size;
 #pragma unroll

@@ -276,7 +276,7 @@ def _decode_case(kv, oracle, lens, bs, quant, n_heads, seed, outlier_p=0.0, n_la
     tabs = np.array(tabs if tabs else [0], np.uint32)
     for layer in range(n_layers):
         q = rng.standard_normal((len(lens), n_heads, W)).astype(np.float32)
-        got = c.mlaDecode(layer, q, np.arange(len(lens), dtype=np.uint32), SCALE)
+        got = c.mlaDecode(layer, q, np.arange(len(lens), dtype=np.uint32), SCALE)  # checks the status word
         if expect_impl is not None:
             assert c.last_decode_impl == expect_impl
         want = o.attention_batch(layer, offs, tabs, np.array(lens, np.uint32), q, SCALE, n_threads=8)
