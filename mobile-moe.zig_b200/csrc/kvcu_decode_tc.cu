@@ -51,7 +51,7 @@ constexpr int TMEM_COLS = 512;
 static_assert(QK_SLOTS * NQK_MAX <= PV_COL, "TMEM map");
 constexpr int VCH = 16;              // tokens per V chunk (one f16 MMA K-step)
 constexpr int NCH = TILE / VCH;      // 8 chunks per tile
-constexpr int NTHREADS = 320;        // 10 warps
+constexpr int NTHREADS = 384;        // 3 warpgroups: issue (0-3), epilogue (4-7), converter (8-11)
 constexpr uint32_t MAGIC_I = 0x4B400000u;    // float 12582912 = 1.5 * 2^23
 constexpr float MAGIC_F = 12582912.0f;
 constexpr float RESCALE_LOG2 = 8.0f;         // lazy rescale threshold (factor 256)
@@ -72,13 +72,14 @@ constexpr uint32_t OFF_MISC = OFF_P + 8192;                   // 228352
 // misc: barriers then small arrays
 constexpr int B_KV_FULL = 0, B_KV_EMPTY = 2, B_QK_FULL = 4, B_QK_EMPTY = 12, B_V_FULL = 20,
               B_V_EMPTY = 22, B_P_FULL = 24, B_P_EMPTY = 25, B_PV_DONE = 26, B_PV_EMPTY = 27,
-              B_Q_FULL = 28, B_FINAL = 29, B_EPI = 30, NUM_BARS = 31;
+              B_Q_FULL = 28, B_FINAL = 29, B_EPI = 30, B_FINAL_PV = 31, NUM_BARS = 32;
 constexpr uint32_t OFF_TMEM_BASE = OFF_MISC + NUM_BARS * 8;   // u32
 constexpr uint32_t OFF_ABORT = OFF_TMEM_BASE + 4;             // u32
 constexpr uint32_t OFF_QSCALE = OFF_MISC + 256;               // float[24]
 constexpr uint32_t OFF_REDMAX = OFF_QSCALE + 128;             // float[2][4][24]
 constexpr uint32_t OFF_ONES = OFF_REDMAX + 2 * 4 * 24 * 4;    // 128 B of f16 1.0 (l = ones x P^T)
-constexpr uint32_t SMEM_USED = OFF_ONES + 128;
+constexpr uint32_t OFF_MREF = OFF_ONES + 128;                 // float[4 warps][24] reference max
+constexpr uint32_t SMEM_USED = OFF_MREF + 4 * 24 * 4;
 constexpr uint32_t SMEM_ALLOC = SMEM_USED + 1024;             // slack for 1024 alignment
 static_assert(SMEM_ALLOC <= 232448, "shared memory budget");
 
@@ -132,9 +133,8 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
 
 // Bounded wait: gives up after ~2^31 clocks (about a second) or when another
 // role has aborted; records the timeout in the status word.
-__device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile uint32_t* abort_flag,
-                                       uint32_t* status) {
-  if (mbar_try(bar, parity)) return true;
+__device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity,
+                                            volatile uint32_t* abort_flag, uint32_t* status) {
   const long long t0 = clock64();
   while (true) {
     if (mbar_try(bar, parity)) return true;
@@ -145,6 +145,10 @@ __device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile u
       return false;
     }
   }
+}
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile uint32_t* abort_flag,
+                                          uint32_t* status) {
+  return mbar_try(bar, parity) || mbar_wait_slow(bar, parity, abort_flag, status);
 }
 
 __device__ __forceinline__ void fence_proxy_async() {
@@ -335,6 +339,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     mbar_init(bar(B_PV_EMPTY), 4);
     mbar_init(bar(B_Q_FULL), 4);
     mbar_init(bar(B_FINAL), 1);
+    mbar_init(bar(B_FINAL_PV), 1);
     mbar_init(bar(B_EPI), 4);
     *abort_flag = 0u;
     uint32_t* ones = reinterpret_cast<uint32_t*>(smem + OFF_ONES);
@@ -354,7 +359,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + OFF_TMEM_BASE);
 
-  if (warp >= 2 && warp < 6) {
+  if (warp >= 4 && warp < 8) {
     // epilogue warps pre-load every QK slot with the conversion bias
     const uint32_t q = warp & 3u;
     uint32_t mg[16];
@@ -366,6 +371,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+
 
   if (warp == 0) {
     // ================================================================ producer
@@ -418,48 +424,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         mbar_wait(bar(B_KV_FULL + (k & 1u)), (k >> 1) & 1u, abort_flag, a.status);
     }
   } else if (warp == 1) {
-    // ================================================================ MMA issuer
+    // ================================================================ QK issuer
     if (lane == 0) {
       uint32_t g = 0, item_no = 0;
-      uint32_t prev_valid = 0, prev_g = 0, prev_first = 0;  // pending PV tile
       bool ok = true;
-      auto issue_pv = [&](uint32_t pg, uint32_t first_of_item, uint32_t item_ord) -> bool {
-        if (first_of_item && item_ord > 0) {
-          // the epilogue drained the previous item's O
-          if (!mbar_wait(bar(B_PV_EMPTY), (item_ord - 1) & 1u, abort_flag, a.status)) return false;
-        }
-        if (!mbar_wait(bar(B_P_FULL), pg & 1u, abort_flag, a.status)) return false;
-        tc_fence_after();
-        for (uint32_t c = 0; c < NCH; ++c) {
-          const uint32_t kv = pg * NCH + c, vs = kv & 1u;
-          if (!mbar_wait(bar(B_V_FULL + vs), (kv >> 1) & 1u, abort_flag, a.status)) return false;
-          tc_fence_after();
-          const uint32_t vbase = sbase + OFF_VR + vs * VCH_BYTES;
-          const uint32_t pbase = sbase + OFF_P + (c >> 2) * 4096u + (c & 3u) * 32u;
-          const uint64_t bdesc = smem_desc(pbase, 16, 1024, LAYOUT_SW128);
-          const uint32_t acc_flag = (first_of_item && c == 0) ? 0u : 1u;
-#pragma unroll
-          for (uint32_t mt = 0; mt < 4; ++mt) {
-            const uint64_t adesc = smem_desc(vbase + mt * 4096u, 2048, 1024, LAYOUT_SW128);
-            mma_f16(tmem + PV_COL + mt * NPV, adesc, bdesc, IDESC_PV, acc_flag);
-          }
-          mma_f16(tmem + L_COL, smem_desc(sbase + OFF_ONES, 0, 0, LAYOUT_NONE), bdesc, IDESC_L, acc_flag);
-          mma_commit(bar(B_V_EMPTY + vs));
-        }
-        mma_commit(bar(B_PV_DONE));
-        mma_commit(bar(B_P_EMPTY));
-        return true;
-      };
-      uint32_t prev_item_ord = 0;
       for (uint32_t it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
         const Item im = load_item(a, it);
         if (im.ntiles == 0) continue;
-        // The previous item's last PV goes first: the epilogue drains that item
-        // before it writes this item's query digits (no circular wait).
-        if (prev_valid) {
-          if (!issue_pv(prev_g, prev_first, prev_item_ord)) break;
-          prev_valid = 0;
-        }
         if (!mbar_wait(bar(B_Q_FULL), item_no & 1u, abort_flag, a.status)) break;
         tc_fence_after();
         for (uint32_t k = 0; k < im.ntiles; ++k, ++g) {
@@ -490,29 +461,70 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             mma_commit(bar(B_QK_FULL + slot));
           }
           if (!ok) break;
-          mma_commit(bar(B_KV_EMPTY + s));
-          // PV of the previous tile of this item (it overlaps this tile's QK epilogue)
-          if (prev_valid && !issue_pv(prev_g, prev_first, prev_item_ord)) {
-            ok = false;
-            break;
-          }
-          prev_valid = 1;
-          prev_g = g;
-          prev_first = (k == 0);
-          prev_item_ord = item_no;
+          mma_commit(bar(B_KV_EMPTY + s));  // the raw stage's int8 rows are no longer read
         }
         ++item_no;
       }
-      if (ok && prev_valid) issue_pv(prev_g, prev_first, prev_item_ord);
       // all issued tcgen05 work retires before TMEM is freed
       mma_commit(bar(B_FINAL));
       mbar_wait(bar(B_FINAL), 0, abort_flag, a.status);
     }
-  } else if (warp < 6) {
+  } else if (warp == 2) {
+    // ================================================================ PV issuer
+    if (lane == 0) {
+      uint32_t g = 0, item_ord = 0;
+      bool ok = true;
+      const uint64_t ones_desc = smem_desc(sbase + OFF_ONES, 0, 0, LAYOUT_NONE);
+      for (uint32_t it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+        const Item im = load_item(a, it);
+        if (im.ntiles == 0) continue;
+        for (uint32_t k = 0; k < im.ntiles && ok; ++k, ++g) {
+          if (k == 0 && item_ord > 0) {
+            // the epilogue has drained the previous item's O and l
+            if (!mbar_wait(bar(B_PV_EMPTY), (item_ord - 1) & 1u, abort_flag, a.status)) {
+              ok = false;
+              break;
+            }
+          }
+          if (!mbar_wait(bar(B_P_FULL), g & 1u, abort_flag, a.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          for (uint32_t c = 0; c < NCH; ++c) {
+            const uint32_t kv = g * NCH + c, vs = kv & 1u;
+            if (!mbar_wait(bar(B_V_FULL + vs), (kv >> 1) & 1u, abort_flag, a.status)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t vbase = sbase + OFF_VR + vs * VCH_BYTES;
+            const uint64_t bdesc = smem_desc(sbase + OFF_P + (c >> 2) * 4096u + (c & 3u) * 32u, 16, 1024,
+                                             LAYOUT_SW128);
+            const uint32_t acc_flag = (k == 0 && c == 0) ? 0u : 1u;
+#pragma unroll
+            for (uint32_t mt = 0; mt < 4; ++mt)
+              mma_f16(tmem + PV_COL + mt * NPV, smem_desc(vbase + mt * 4096u, 2048, 1024, LAYOUT_SW128),
+                      bdesc, IDESC_PV, acc_flag);
+            mma_f16(tmem + L_COL, ones_desc, bdesc, IDESC_L, acc_flag);
+            mma_commit(bar(B_V_EMPTY + vs));
+          }
+          if (!ok) break;
+          mma_commit(bar(B_PV_DONE));
+          mma_commit(bar(B_P_EMPTY));
+        }
+        ++item_ord;
+      }
+      mma_commit(bar(B_FINAL_PV));
+      mbar_wait(bar(B_FINAL_PV), 0, abort_flag, a.status);
+    }
+  } else if (warp == 3) {
+    // spare warp of the issue warpgroup
+  } else if (warp < 8) {
     // ================================================================ epilogue
     const uint32_t q4 = warp & 3u;             // TMEM lane quarter
     const uint32_t trow = 32u * q4 + lane;     // token row in the tile / latent row in an M-tile
-    const uint32_t ew = warp - 2u;             // 0..3
+    const uint32_t ew = warp - 4u;             // 0..3
     const uint32_t lane_addr = (32u * q4) << 16;
     float* qscale = reinterpret_cast<float*>(smem + OFF_QSCALE);
     float* redmax = reinterpret_cast<float*>(smem + OFF_REDMAX);
@@ -585,9 +597,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         if (lane == 0) mbar_arrive(bar(B_Q_FULL));
         if (!epi_sync()) break;  // qscale visible to every epilogue thread
       }
-      float m_ref[HK];
-#pragma unroll
-      for (int h = 0; h < HK; ++h) m_ref[h] = -INFINITY;
+      // running reference max per head: a warp-private copy in shared memory
+      // (uniform across the warp; lane 0 writes between __syncwarp()s)
+      float* m_ref = reinterpret_cast<float*>(smem + OFF_MREF) + ew * 24;
+      if (lane == 0)
+        for (int h = 0; h < HK; ++h) m_ref[h] = -INFINITY;
+      __syncwarp();
       for (uint32_t k = 0; k < im.ntiles && ok; ++k, ++g) {
         const uint32_t s = g & 1u;
         const uint32_t tt0 = im.tok0 + k * TILE;
@@ -602,9 +617,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         float acc[HK];
 #pragma unroll
         for (int h = 0; h < HK; ++h) acc[h] = 0.f;
-        for (uint32_t b = 0; b < NBLK; ++b) {
-          const uint32_t kk = g * NBLK + b, slot = kk % QK_SLOTS;
-          if (!mbar_wait(bar(B_QK_FULL + slot), (kk / QK_SLOTS) & 1u, abort_flag, a.status)) {
+        // two Q8_0 blocks per TMEM round trip (18 blocks -> 9 rounds)
+        for (uint32_t b = 0; b < NBLK; b += 2) {
+          const uint32_t kk = g * NBLK + b;
+          const uint32_t slot0 = kk % QK_SLOTS, slot1 = (kk + 1) % QK_SLOTS;
+          if (!mbar_wait(bar(B_QK_FULL + slot0), (kk / QK_SLOTS) & 1u, abort_flag, a.status) ||
+              !mbar_wait(bar(B_QK_FULL + slot1), ((kk + 1) / QK_SLOTS) & 1u, abort_flag, a.status)) {
             ok = false;
             break;
           }
@@ -612,14 +630,22 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           // columns [0, HK): digit 0 of each head, [HK, 2HK): digit 1
           constexpr int NQ = Cfg<HK>::NQK;
           constexpr int NL = 2 * HK;  // columns actually used
-          uint32_t r[NL];
-          const uint32_t ta = tmem + lane_addr + slot * NQ;
+          uint32_t r0[NL], r1[NL];
+          const uint32_t ta0 = tmem + lane_addr + slot0 * NQ, ta1 = tmem + lane_addr + slot1 * NQ;
           if constexpr (NL >= 32) {
-            TMEM_LD32(ta, r);
-            if constexpr (NL == 48) TMEM_LD16(ta + 32, (r + 32));
-            if constexpr (NL == 40) TMEM_LD8(ta + 32, (r + 32));
+            TMEM_LD32(ta0, r0);
+            TMEM_LD32(ta1, r1);
+            if constexpr (NL == 48) {
+              TMEM_LD16(ta0 + 32, (r0 + 32));
+              TMEM_LD16(ta1 + 32, (r1 + 32));
+            }
+            if constexpr (NL == 40) {
+              TMEM_LD8(ta0 + 32, (r0 + 32));
+              TMEM_LD8(ta1 + 32, (r1 + 32));
+            }
           } else {
-            TMEM_LD16(ta, r);
+            TMEM_LD16(ta0, r0);
+            TMEM_LD16(ta1, r1);
           }
           tmem_wait_ld();
           {
@@ -627,18 +653,28 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
             for (int i = 0; i < 16; ++i) mg[i] = MAGIC_I;
 #pragma unroll
-            for (int c = 0; c < NQ; c += 16) TMEM_ST16(ta + (uint32_t)c, mg);
+            for (int c = 0; c < NQ; c += 16) {
+              TMEM_ST16(ta0 + (uint32_t)c, mg);
+              TMEM_ST16(ta1 + (uint32_t)c, mg);
+            }
             tmem_wait_st();
           }
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(bar(B_QK_EMPTY + slot));
-          const float d = __half2float(__ushort_as_half(scrow[b]));
+          if (lane == 0) {
+            mbar_arrive(bar(B_QK_EMPTY + slot0));
+            mbar_arrive(bar(B_QK_EMPTY + slot1));
+          }
+          const uint32_t d2 = *reinterpret_cast<const uint32_t*>(scrow + b);  // scales of b, b+1
+          const float d0 = __half2float(__ushort_as_half((uint16_t)(d2 & 0xFFFFu)));
+          const float d1 = __half2float(__ushort_as_half((uint16_t)(d2 >> 16)));
 #pragma unroll
           for (int h = 0; h < HK; ++h) {
-            const float x0 = __uint_as_float(r[h]) - MAGIC_F;  // exact: |dot| < 2^22
-            const float x1 = __uint_as_float(r[h + HK]) - MAGIC_F;
-            acc[h] = fmaf(d, fmaf(x0, 256.f, x1), acc[h]);
+            // exact int32 -> f32 through the bias: |dot| < 2^22
+            const float x00 = __uint_as_float(r0[h]) - MAGIC_F, x01 = __uint_as_float(r0[h + HK]) - MAGIC_F;
+            const float x10 = __uint_as_float(r1[h]) - MAGIC_F, x11 = __uint_as_float(r1[h + HK]) - MAGIC_F;
+            acc[h] = fmaf(d0, fmaf(x00, 256.f, x01), acc[h]);
+            acc[h] = fmaf(d1, fmaf(x10, 256.f, x11), acc[h]);
           }
         }
         if (!ok) break;
@@ -697,11 +733,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           }
           tc_fence_before();
         }
-#pragma unroll
-        for (int h = 0; h < HK; ++h) {
-          const float tm = tile_max(h);
-          if (tm > m_ref[h] + RESCALE_LOG2) m_ref[h] = tm;
+        __syncwarp();
+        if (lane == 0) {
+          for (int h = 0; h < HK; ++h) {
+            const float tm = tile_max(h);
+            if (tm > m_ref[h] + RESCALE_LOG2) m_ref[h] = tm;
+          }
         }
+        __syncwarp();
         // ---- P (f16) -> shared memory, K-major 128B-swizzled [head][token]
         if (!mbar_wait(bar(B_P_EMPTY), (g & 1u) ^ 1u, abort_flag, a.status)) {
           ok = false;
@@ -755,13 +794,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         if (!single && ew == 0 && lane < H) {
           const float ln2 = 0.69314718055994531f;
-          float mh = -INFINITY, lh = 0.f;
+          const float mh = m_ref[lane] * ln2;
+          float lh = 0.f;
 #pragma unroll
           for (int h = 0; h < HK; ++h)
-            if ((uint32_t)h == lane) {
-              mh = m_ref[h] * ln2;
-              lh = ltot[h];
-            }
+            if ((uint32_t)h == lane) lh = ltot[h];
           a.part_ml[((uint64_t)it * a.ws_heads + lane) * 2 + 0] = mh;
           a.part_ml[((uint64_t)it * a.ws_heads + lane) * 2 + 1] = lh;
         }
@@ -772,7 +809,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
   } else {
     // ================================================================ converter
-    const uint32_t cw = warp - 6u;                 // 0..3
+    const uint32_t cw = warp - 8u;                 // 0..3
     const uint32_t tid = cw * 32u + lane;          // 0..127
     const uint32_t tl = tid & 15u;                 // token within the chunk
     const uint32_t gq = tid >> 4;                  // 64-column group (MN atom) 0..7
