@@ -73,9 +73,10 @@ constexpr uint32_t OFF_MISC = OFF_P + 8192;                   // 228352
 constexpr int B_KV_FULL = 0, B_KV_EMPTY = 2, B_QK_FULL = 4, B_QK_EMPTY = 12, B_V_FULL = 20,
               B_V_EMPTY = 22, B_P_FULL = 24, B_P_EMPTY = 25, B_PV_DONE = 26, B_PV_EMPTY = 27,
               B_Q_FULL = 28, B_FINAL = 29, B_EPI = 30, B_FINAL_PV = 31, NUM_BARS = 32;
-constexpr uint32_t OFF_TMEM_BASE = OFF_MISC + NUM_BARS * 8;   // u32
-constexpr uint32_t OFF_ABORT = OFF_TMEM_BASE + 4;             // u32
-constexpr uint32_t OFF_QSCALE = OFF_MISC + 256;               // float[24]
+constexpr uint32_t OFF_TMEM_BASE = OFF_MISC + 384;            // u32
+constexpr uint32_t OFF_ABORT = OFF_MISC + 388;                // u32
+static_assert(NUM_BARS * 8 <= 384, "mbarriers overlap the misc words");
+constexpr uint32_t OFF_QSCALE = OFF_MISC + 512;               // float[24]
 constexpr uint32_t OFF_REDMAX = OFF_QSCALE + 128;             // float[2][4][24]
 constexpr uint32_t OFF_ONES = OFF_REDMAX + 2 * 4 * 24 * 4;    // 128 B of f16 1.0 (l = ones x P^T)
 constexpr uint32_t OFF_MREF = OFF_ONES + 128;                 // float[4 warps][24] reference max
@@ -138,7 +139,10 @@ __device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity,
   const long long t0 = clock64();
   while (true) {
     if (mbar_try(bar, parity)) return true;
-    if (*abort_flag) return false;
+    if (*abort_flag) {
+      atomicOr(status, STATUS_TIMEOUT);  // never unwind silently
+      return false;
+    }
     if (clock64() - t0 > (1ll << 31)) {
       *abort_flag = 1u;
       atomicOr(status, STATUS_TIMEOUT);
