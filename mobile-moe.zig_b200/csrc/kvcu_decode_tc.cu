@@ -3,31 +3,36 @@
 // Same contract as k_decode in kvcu_decode.cu (the attention core of
 // src/inference.zig:518-660 in absorbed form, over a Q8_0 pool), same work
 // items and partial format, so k_plan / k_combine are shared.  One persistent
-// CTA per SM, 10 warps with fixed roles:
+// CTA per SM, 16 warps in 4 warpgroups with fixed roles:
 //
-//   warp 0     TMA producer: per 128-token tile, the Q8_0 payload rows of the
-//              sequence's physical blocks (2-D tensor maps over the pool,
-//              128B swizzle for the 512 latent bytes, 64B for the 64 rope
-//              bytes) and the f16 scales (1-D bulk copies) -> raw stage ring (2).
-//   warp 1     TMEM owner + single-thread MMA issuer:
-//                QK  = 18 x tcgen05.mma.kind::i8 per tile (one per Q8_0 block:
-//                      A = the raw int8 tile [128 tok x 32], B = the query as two
-//                      int8 digits [48 x 32]); exact int32 dot products per
-//                      block, into a ring of 8 TMEM slots;
-//                PV  = 8 chunks x 4 tcgen05.mma.kind::f16 (M = 128 latent
-//                      columns, N = 32 heads, K = 16 tokens): O^T += V^T P^T,
-//                      accumulated in TMEM across the whole work item.
-//   warps 2-5  epilogue: per token row, combine the 18 per-block dot products
-//              with the block scales, online softmax over the tile (lazy
-//              rescale of O in TMEM only when a head's max grows by > 2^8),
-//              P (f16) -> shared memory; at item end O / l -> output.
-//   warps 6-9  converter: V = f16(d * q) for the tile's 512 latent columns,
-//              16 tokens at a time, into the MN-major f16 operand layout.
+//   warp 0      TMA producer: per 128-token tile, the Q8_0 payload rows of the
+//               sequence's physical blocks (2-D tensor maps over the pool,
+//               128B swizzle for the 512 latent bytes, 64B for the 64 rope
+//               bytes) and the f16 scales (1-D bulk copies) -> raw stage ring (2).
+//   warp 1      TMEM owner + QK issuer: 18 x tcgen05.mma.kind::i8 per tile, one
+//               per Q8_0 block (A = the raw int8 tile [128 tok x 32], B = the
+//               query as two int8 digits [2H x 32]): exact int32 dot products
+//               per block into a ring of 3 TMEM slot pairs.
+//   warp 2      PV issuer: per 16-token V chunk, four tcgen05.mma.kind::f16
+//               (M = 128 latent columns, N = 32 heads, K = 16 tokens):
+//               O^T += V^T P^T, accumulated in TMEM across the whole work item,
+//               and l = ones x P^T by one more MMA.
+//   warps 4-11  epilogue (two halves of the heads, each over all 128 token
+//               rows): combine the 18 per-block dot products with the block
+//               scales, online softmax over the tile (lazy rescale of O / l in
+//               TMEM only when a head's max grows by > 2^8), P (f16) -> shared
+//               memory; at item end O / l -> output (or the split partial).
+//   warps 12-15 converter: V = f16(d * q) for the tile's 512 latent columns in
+//               16 KB chunks through a 2-deep ring, in the MN-major f16 layout.
+//
+// The issue warps run converged and issue through one elected lane: an
+// mbarrier wait costs ~100+ cycles even when the phase is complete, so they
+// wait once per block pair / V chunk rather than once per MMA.
 //
 // The QK path is exact (int32 accumulation per 32-element Q8_0 block), so the
 // only roundings are the query's two-digit int8 form (|err| <= amax/65024),
 // V and P in f16, and f32 accumulation.  Every mbarrier wait is bounded
-// (~2 s of clocks); on timeout the CTA sets KVCU_STATUS_TIMEOUT, every role
+// (~1 s of clocks); on timeout the CTA sets KVCU_STATUS_TIMEOUT, every role
 // unwinds, in-flight copies and MMAs are waited for (bounded) and TMEM is freed.
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -44,14 +49,19 @@ constexpr int NBLK = 18;             // Q8_0 blocks per row (16 latent + 2 rope)
 constexpr int NQK_MAX = 48;          // QK N: 2 digits x up to 24 heads
 constexpr int HMAX = NQK_MAX / 2;    // heads supported by the tensor-core kernel
 constexpr int NPV = 32;              // PV N: heads padded to 32
-constexpr int QK_SLOTS = 7;          // TMEM ring of per-block QK accumulators (cols 0..335)
+constexpr int QK_PAIRS = 3;          // TMEM ring of QK accumulator pairs (2 blocks each; cols 0..287)
+constexpr int NPAIR = NBLK / 2;      // 9 block pairs per tile
 constexpr int PV_COL = 352;          // O^T accumulator: 4 M-tiles x 32 cols = [352, 480)
 constexpr int L_COL = 480;           // softmax denominators l[h] (ones x P^T) = [480, 512)
 constexpr int TMEM_COLS = 512;
-static_assert(QK_SLOTS * NQK_MAX <= PV_COL, "TMEM map");
+static_assert(QK_PAIRS * 2 * NQK_MAX <= PV_COL, "TMEM map");
 constexpr int VCH = 16;              // tokens per V chunk (one f16 MMA K-step)
-constexpr int NCH = TILE / VCH;      // 8 chunks per tile
-constexpr int NTHREADS = 384;        // 3 warpgroups: issue (0-3), epilogue (4-7), converter (8-11)
+constexpr int NCH = TILE / VCH;      // 8 token chunks per tile
+constexpr int V_SLOTS = 2;           // V chunk ring depth
+constexpr uint32_t VU_BYTES = 4096;  // one V unit: 16 tokens x 128 columns (one M-tile) x f16
+constexpr uint32_t VCH_BYTES = 4 * VU_BYTES;  // one V chunk: 16 tokens x 512 columns
+constexpr int NTHREADS = 512;        // 4 warpgroups: issue, epilogue x2, converter
+constexpr int EPI_WARPS = 8;
 constexpr uint32_t MAGIC_I = 0x4B400000u;    // float 12582912 = 1.5 * 2^23
 constexpr float MAGIC_F = 12582912.0f;
 constexpr float RESCALE_LOG2 = 8.0f;         // lazy rescale threshold (factor 256)
@@ -66,21 +76,20 @@ constexpr uint32_t OFF_QD = 2 * STAGE_BYTES;     // query digits: 4 x [<=48][128
 constexpr uint32_t QD_LAT_BYTES = NQK_MAX * 128;  // 6144 per latent region
 constexpr uint32_t OFF_QD_ROPE = OFF_QD + 4 * QD_LAT_BYTES;
 constexpr uint32_t OFF_VR = OFF_QD + 4 * QD_LAT_BYTES + 3072;  // 187392: V chunk ring (2 x 16 KB)
-constexpr uint32_t VCH_BYTES = 16384;
-constexpr uint32_t OFF_P = OFF_VR + 2 * VCH_BYTES;            // P^T: 2 regions x [32][128 B]
-constexpr uint32_t OFF_MISC = OFF_P + 8192;                   // 228352
-// misc: barriers then small arrays
-constexpr int B_KV_FULL = 0, B_KV_EMPTY = 2, B_QK_FULL = 4, B_QK_EMPTY = 12, B_V_FULL = 20,
-              B_V_EMPTY = 22, B_P_FULL = 24, B_P_EMPTY = 25, B_PV_DONE = 26, B_PV_EMPTY = 27,
-              B_Q_FULL = 28, B_FINAL = 29, B_EPI = 30, B_FINAL_PV = 31, NUM_BARS = 32;
-constexpr uint32_t OFF_TMEM_BASE = OFF_MISC + 384;            // u32
-constexpr uint32_t OFF_ABORT = OFF_MISC + 388;                // u32
-static_assert(NUM_BARS * 8 <= 384, "mbarriers overlap the misc words");
+constexpr uint32_t OFF_P = OFF_VR + V_SLOTS * VCH_BYTES;        // P^T: 2 regions x [32][128 B]
+constexpr uint32_t OFF_MISC = OFF_P + 8192;                     // 228352
+// misc: mbarriers, then small words and arrays
+constexpr int B_KV_FULL = 0, B_KV_EMPTY = 2, B_QK_FULL = 4, B_QK_EMPTY = 7, B_V_FULL = 10,
+              B_V_EMPTY = 12, B_P_FULL = 14, B_P_EMPTY = 15, B_PV_DONE = 16, B_PV_EMPTY = 17,
+              B_Q_FULL = 18, B_FINAL = 19, B_FINAL_PV = 20, B_EPI = 21, NUM_BARS = 22;
+static_assert(NUM_BARS * 8 <= 352, "mbarriers overlap the misc words");
+constexpr uint32_t OFF_TMEM_BASE = OFF_MISC + 352;            // u32
+constexpr uint32_t OFF_ABORT = OFF_MISC + 356;                // u32
+constexpr uint32_t OFF_ONES = OFF_MISC + 384;                 // 128 B of f16 1.0 (l = ones x P^T)
 constexpr uint32_t OFF_QSCALE = OFF_MISC + 512;               // float[24]
-constexpr uint32_t OFF_REDMAX = OFF_QSCALE + 128;             // float[2][4][24]
-constexpr uint32_t OFF_ONES = OFF_REDMAX + 2 * 4 * 24 * 4;    // 128 B of f16 1.0 (l = ones x P^T)
-constexpr uint32_t OFF_MREF = OFF_ONES + 128;                 // float[4 warps][24] reference max
-constexpr uint32_t SMEM_USED = OFF_MREF + 4 * 24 * 4;
+constexpr uint32_t OFF_REDMAX = OFF_MISC + 640;               // float[2][8 warps][24]
+constexpr uint32_t OFF_MREF = OFF_REDMAX + 2 * EPI_WARPS * 24 * 4;  // float[8 warps][24]
+constexpr uint32_t SMEM_USED = OFF_MREF + EPI_WARPS * 24 * 4;
 constexpr uint32_t SMEM_ALLOC = SMEM_USED + 1024;             // slack for 1024 alignment
 static_assert(SMEM_ALLOC <= 232448, "shared memory budget");
 
@@ -133,17 +142,13 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
 }
 
 // Bounded wait: gives up after ~2^31 clocks (about a second) or when another
-// role has aborted; records the timeout in the status word.
+// role has aborted; any give-up records a timeout in the status word.
 __device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity,
                                             volatile uint32_t* abort_flag, uint32_t* status) {
   const long long t0 = clock64();
   while (true) {
     if (mbar_try(bar, parity)) return true;
-    if (*abort_flag) {
-      atomicOr(status, STATUS_TIMEOUT);  // never unwind silently
-      return false;
-    }
-    if (clock64() - t0 > (1ll << 31)) {
+    if (*abort_flag || clock64() - t0 > (1ll << 31)) {
       *abort_flag = 1u;
       atomicOr(status, STATUS_TIMEOUT);
       return false;
@@ -153,6 +158,32 @@ __device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity,
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile uint32_t* abort_flag,
                                           uint32_t* status) {
   return mbar_try(bar, parity) || mbar_wait_slow(bar, parity, abort_flag, status);
+}
+// Warp-wide wait with one verdict for the whole warp (the issue warps run
+// converged so that their MMA operands stay warp-uniform).
+__device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, volatile uint32_t* abort_flag,
+                                               uint32_t* status) {
+  const bool ok = mbar_wait(bar, parity, abort_flag, status);
+  return __all_sync(0xffffffffu, ok);
+}
+// One lane of a converged warp (the lane that issues tcgen05 work).
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n .reg .b32 r;\n .reg .pred p;\n elect.sync r|p, 0xffffffff;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(pred));
+  return pred != 0;
+}
+// Wait for this CTA's own asynchronous work (copies, MMAs) to retire: bounded
+// by time only, so it still waits after another role has aborted.
+__device__ __noinline__ void mbar_wait_drain(uint32_t bar, uint32_t parity, uint32_t* status) {
+  const long long t0 = clock64();
+  while (!mbar_try(bar, parity)) {
+    if (clock64() - t0 > (1ll << 31)) {
+      atomicOr(status, STATUS_TIMEOUT);
+      return;
+    }
+  }
 }
 
 __device__ __forceinline__ void fence_proxy_async() {
@@ -181,32 +212,36 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
 }
 
 // UMMA shared-memory descriptor (sm_100): start>>4 @0, LBO>>4 @16, SBO>>4 @32,
-// version 1 @46, layout type @61 (2 = 128B swizzle, 4 = 64B swizzle).
+// version 1 @46, layout type @61 (0 = none, 2 = 128B swizzle, 4 = 64B swizzle).
 __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo,
                                               uint32_t layout) {
   return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
          ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | ((uint64_t)layout << 61);
 }
-constexpr uint32_t LAYOUT_SW128 = 2, LAYOUT_SW64 = 4;
+constexpr uint32_t LAYOUT_NONE = 0, LAYOUT_SW128 = 2, LAYOUT_SW64 = 4;
 
-// Instruction descriptors: kind::i8 (s8 x s8 -> s32, both K-major, M=128, N=nqk)
-// and kind::f16 (f16 x f16 -> f32, A MN-major, B K-major, M=128, N=32).
+// Instruction descriptors: kind::i8 (s8 x s8 -> s32, both K-major, M=128, N=nqk),
+// kind::f16 (f16 x f16 -> f32, A MN-major, B K-major, M=128, N=32) for PV, and
+// the same with a K-major A for the l accumulation (A = all ones, zero strides:
+// every row and K index reads the same 128 bytes of 1.0).
 constexpr uint32_t idesc_qk(int nqk) {
   return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(nqk >> 3) << 17) | ((uint32_t)(TILE >> 4) << 24);
 }
-// Head bucket HK (8, 16, 20 or 24 heads per kernel instance): the query digit
-// rows are [0, HK) for digit 0 and [HK, 2HK) for digit 1, N = 2HK rounded to 16.
+constexpr uint32_t IDESC_PV = (1u << 4) | (1u << 15) | ((uint32_t)(NPV >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+constexpr uint32_t IDESC_L = (1u << 4) | ((uint32_t)(NPV >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+
+// Head bucket HK (8, 16, 20 or 24 heads per kernel instance).  Each epilogue
+// half owns HH = HK/2 heads.  Query digit rows (= QK accumulator columns) of
+// half f start at f*NQH, head-local hl's digits d at f*NQH + 2hl + d, so each
+// half drains one 8-column-aligned run of 2HH columns per block.  P rows (= PV
+// accumulator columns) of half f start at 16f.
 template <int HK>
 struct Cfg {
-  static constexpr int NQK = (2 * HK + 15) / 16 * 16;
-  static_assert(NQK <= NQK_MAX, "head bucket too large");
+  static constexpr int HH = HK / 2;
+  static constexpr int NQH = (2 * HH + 7) / 8 * 8;
+  static constexpr int NQK = 2 * NQH;
+  static_assert(NQK <= NQK_MAX && NQK % 16 == 0 && HK % 2 == 0 && HH <= 16, "head bucket");
 };
-constexpr uint32_t IDESC_PV = (1u << 4) | (0u << 7) | (0u << 10) | (1u << 15) |
-                              ((uint32_t)(NPV >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
-// l-accumulation: A = all-ones (K-major, no swizzle, zero strides: every row and
-// K index reads the same 128-byte block of 1.0), B = P^T as in PV.
-constexpr uint32_t IDESC_L = (1u << 4) | ((uint32_t)(NPV >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
-constexpr uint32_t LAYOUT_NONE = 0;
 
 __device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
                                        uint32_t accumulate) {
@@ -229,42 +264,90 @@ __device__ __forceinline__ void mma_commit(uint32_t bar) {
                : "memory");
 }
 
-#define TMEM_LD32(taddr, r)                                                                         \
-  asm volatile(                                                                                     \
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14," \
-      "%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"              \
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),         \
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),     \
-        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]),  \
-        "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]),  \
-        "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])                                          \
-      : "r"(taddr))
-#define TMEM_LD16(taddr, r)                                                                         \
-  asm volatile(                                                                                     \
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14," \
-      "%15}, [%16];"                                                                                \
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),         \
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),     \
-        "=r"(r[14]), "=r"(r[15])                                                                    \
-      : "r"(taddr))
-#define TMEM_LD8(taddr, r)                                                                          \
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"              \
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),            \
-                 "=r"(r[6]), "=r"(r[7])                                                             \
-               : "r"(taddr))
-#define TMEM_ST16(taddr, r)                                                                         \
-  asm volatile(                                                                                     \
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13," \
-      "%14,%15,%16};" ::"r"(taddr),                                                                 \
-      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),       \
-      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])  \
-      : "memory")
-#define TMEM_ST8(taddr, r)                                                                          \
-  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), \
-               "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]),         \
-               "r"(r[7])                                                                            \
-               : "memory")
-
+// TMEM loads / stores of N consecutive 32-bit columns of the warp's 32 lanes.
+__device__ __forceinline__ void tld1(uint32_t ta, uint32_t* r) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r[0]) : "r"(ta));
+}
+__device__ __forceinline__ void tld2(uint32_t ta, uint32_t* r) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0,%1}, [%2];" : "=r"(r[0]), "=r"(r[1]) : "r"(ta));
+}
+__device__ __forceinline__ void tld4(uint32_t ta, uint32_t* r) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(ta));
+}
+__device__ __forceinline__ void tld8(uint32_t ta, uint32_t* r) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+                 "=r"(r[7])
+               : "r"(ta));
+}
+template <int N>
+__device__ __forceinline__ void tmem_ld(uint32_t ta, uint32_t* r) {
+  if constexpr (N >= 8) {
+    tld8(ta, r);
+    tmem_ld<N - 8>(ta + 8, r + 8);
+  } else if constexpr (N >= 4) {
+    tld4(ta, r);
+    tmem_ld<N - 4>(ta + 4, r + 4);
+  } else if constexpr (N >= 2) {
+    tld2(ta, r);
+    tmem_ld<N - 2>(ta + 2, r + 2);
+  } else if constexpr (N == 1) {
+    tld1(ta, r);
+  }
+}
+__device__ __forceinline__ void tst1(uint32_t ta, const uint32_t* r) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};" ::"r"(ta), "r"(r[0]) : "memory");
+}
+__device__ __forceinline__ void tst2(uint32_t ta, const uint32_t* r) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x2.b32 [%0], {%1,%2};" ::"r"(ta), "r"(r[0]), "r"(r[1])
+               : "memory");
+}
+__device__ __forceinline__ void tst4(uint32_t ta, const uint32_t* r) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1,%2,%3,%4};" ::"r"(ta), "r"(r[0]),
+               "r"(r[1]), "r"(r[2]), "r"(r[3])
+               : "memory");
+}
+__device__ __forceinline__ void tst8(uint32_t ta, const uint32_t* r) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(ta),
+               "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
+}
+template <int N>
+__device__ __forceinline__ void tmem_st(uint32_t ta, const uint32_t* r) {
+  if constexpr (N >= 8) {
+    tst8(ta, r);
+    tmem_st<N - 8>(ta + 8, r + 8);
+  } else if constexpr (N >= 4) {
+    tst4(ta, r);
+    tmem_st<N - 4>(ta + 4, r + 4);
+  } else if constexpr (N >= 2) {
+    tst2(ta, r);
+    tmem_st<N - 2>(ta + 2, r + 2);
+  } else if constexpr (N == 1) {
+    tst1(ta, r);
+  }
+}
+// N columns of the conversion bias
+template <int N>
+__device__ __forceinline__ void tmem_st_magic(uint32_t ta) {
+  uint32_t m[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m[i] = MAGIC_I;
+  if constexpr (N >= 8) {
+    tst8(ta, m);
+    tmem_st_magic<N - 8>(ta + 8);
+  } else if constexpr (N >= 4) {
+    tst4(ta, m);
+    tmem_st_magic<N - 4>(ta + 4);
+  } else if constexpr (N >= 2) {
+    tst2(ta, m);
+    tmem_st_magic<N - 2>(ta + 2);
+  } else if constexpr (N == 1) {
+    tst1(ta, m);
+  }
+}
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -314,6 +397,8 @@ template <int HK>
 __global__ void __launch_bounds__(NTHREADS, 1)
     k_decode_tc(const __grid_constant__ CUtensorMap map_lat, const __grid_constant__ CUtensorMap map_rope,
                 TcArgs a) {
+  constexpr int NQ = Cfg<HK>::NQK;
+  constexpr int HH = Cfg<HK>::HH;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
@@ -323,28 +408,28 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const uint32_t n_items = a.meta[0];
   const uint32_t H = a.n_heads;
 
-  // ---- set-up: barriers, TMEM
+  // ---- set-up: barriers, constant operands, TMEM
   if (threadIdx.x == 0) {
     mbar_init(bar(B_KV_FULL + 0), 1);
     mbar_init(bar(B_KV_FULL + 1), 1);
-    mbar_init(bar(B_KV_EMPTY + 0), 9);
-    mbar_init(bar(B_KV_EMPTY + 1), 9);
-    for (int i = 0; i < QK_SLOTS; ++i) {
+    mbar_init(bar(B_KV_EMPTY + 0), 1 + 4 + EPI_WARPS);  // QK issuer commit + converter + epilogue
+    mbar_init(bar(B_KV_EMPTY + 1), 1 + 4 + EPI_WARPS);
+    for (int i = 0; i < QK_PAIRS; ++i) {
       mbar_init(bar(B_QK_FULL + i), 1);
-      mbar_init(bar(B_QK_EMPTY + i), 4);
+      mbar_init(bar(B_QK_EMPTY + i), EPI_WARPS);
     }
-    mbar_init(bar(B_V_FULL + 0), 4);
-    mbar_init(bar(B_V_FULL + 1), 4);
-    mbar_init(bar(B_V_EMPTY + 0), 1);
-    mbar_init(bar(B_V_EMPTY + 1), 1);
-    mbar_init(bar(B_P_FULL), 4);
+    for (int i = 0; i < V_SLOTS; ++i) {
+      mbar_init(bar(B_V_FULL + i), 4);
+      mbar_init(bar(B_V_EMPTY + i), 1);
+    }
+    mbar_init(bar(B_P_FULL), EPI_WARPS);
     mbar_init(bar(B_P_EMPTY), 1);
     mbar_init(bar(B_PV_DONE), 1);
-    mbar_init(bar(B_PV_EMPTY), 4);
-    mbar_init(bar(B_Q_FULL), 4);
+    mbar_init(bar(B_PV_EMPTY), EPI_WARPS);
+    mbar_init(bar(B_Q_FULL), EPI_WARPS);
     mbar_init(bar(B_FINAL), 1);
     mbar_init(bar(B_FINAL_PV), 1);
-    mbar_init(bar(B_EPI), 4);
+    mbar_init(bar(B_EPI), EPI_WARPS);
     *abort_flag = 0u;
     uint32_t* ones = reinterpret_cast<uint32_t*>(smem + OFF_ONES);
     for (int i = 0; i < 32; ++i) ones[i] = 0x3C003C00u;  // f16 1.0 pairs
@@ -364,18 +449,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + OFF_TMEM_BASE);
 
   if (warp >= 4 && warp < 8) {
-    // epilogue warps pre-load every QK slot with the conversion bias
-    const uint32_t q = warp & 3u;
-    uint32_t mg[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) mg[i] = MAGIC_I;
-    for (int c = 0; c < QK_SLOTS * Cfg<HK>::NQK; c += 16) TMEM_ST16(tmem + ((32u * q) << 16) + (uint32_t)c, mg);
+    // pre-load every QK slot with the conversion bias (one warp per lane quarter)
+    const uint32_t ta = tmem + ((32u * (warp & 3u)) << 16);
+    for (int c = 0; c < QK_PAIRS * 2 * NQ; c += 8) tmem_st_magic<8>(ta + (uint32_t)c);
     tmem_wait_st();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-
 
   if (warp == 0) {
     // ================================================================ producer
@@ -389,23 +470,16 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           if (!mbar_wait(bar(B_KV_EMPTY + s), ((g >> 1) & 1u) ^ 1u, abort_flag, a.status)) break;
           const uint32_t tt0 = im.tok0 + k * TILE;
           const uint32_t tt1 = min(tt0 + TILE, im.tok1);
-          // count the bytes first (one arrive.expect_tx per stage)
-          uint32_t segs = 0, bytes = 0;
           // every segment is one box of br rows inside one physical block (the
           // plan aligns items to max(128, block size); anything else is refused)
+          uint32_t bytes = 0;
           for (uint32_t off = 0; tt0 + off < tt1; off += br) {
             const uint32_t pos = tt0 + off;
             const uint32_t blk = a.tables[im.t0 + pos / a.block_size];
-            if (blk >= a.num_blocks) {
-              atomicOr(a.status, KVCU_STATUS_BAD_BLOCK);
-            } else if (pos % a.block_size + br > a.block_size) {
-              atomicOr(a.status, KVCU_STATUS_MISALIGNED);
-            } else {
-              segs++;
-              bytes += br * (4u * 128u + 64u + 36u);
-            }
+            if (blk >= a.num_blocks) atomicOr(a.status, KVCU_STATUS_BAD_BLOCK);
+            else if (pos % a.block_size + br > a.block_size) atomicOr(a.status, KVCU_STATUS_MISALIGNED);
+            else bytes += br * (4u * 128u + 64u + 36u);
           }
-          (void)segs;
           const uint32_t stage = sbase + s * STAGE_BYTES;
           mbar_arrive_tx(bar(B_KV_FULL + s), bytes);
           for (uint32_t off = 0; tt0 + off < tt1; off += br) {
@@ -425,116 +499,136 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       }
       // wait (bounded) for the copies of the last two stages to land
       for (uint32_t k = (g >= 2 ? g - 2 : 0); k < g; ++k)
-        mbar_wait(bar(B_KV_FULL + (k & 1u)), (k >> 1) & 1u, abort_flag, a.status);
+        mbar_wait_drain(bar(B_KV_FULL + (k & 1u)), (k >> 1) & 1u, a.status);
     }
   } else if (warp == 1) {
     // ================================================================ QK issuer
-    if (lane == 0) {
-      uint32_t g = 0, item_no = 0;
-      bool ok = true;
-      for (uint32_t it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
-        const Item im = load_item(a, it);
-        if (im.ntiles == 0) continue;
-        if (!mbar_wait(bar(B_Q_FULL), item_no & 1u, abort_flag, a.status)) break;
+    // The whole warp runs the loop (warp-uniform operands); one elected lane
+    // issues each MMA / commit.  One wait per pair of Q8_0 blocks.
+    uint32_t g = 0, item_no = 0;
+    bool ok = true;
+    for (uint32_t it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+      const Item im = load_item(a, it);
+      if (im.ntiles == 0) continue;
+      if (!mbar_wait_warp(bar(B_Q_FULL), item_no & 1u, abort_flag, a.status)) break;
+      tc_fence_after();
+      for (uint32_t k = 0; k < im.ntiles; ++k, ++g) {
+        const uint32_t s = g & 1u;
+        if (!mbar_wait_warp(bar(B_KV_FULL + s), (g >> 1) & 1u, abort_flag, a.status)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
-        for (uint32_t k = 0; k < im.ntiles; ++k, ++g) {
-          const uint32_t s = g & 1u;
-          if (!mbar_wait(bar(B_KV_FULL + s), (g >> 1) & 1u, abort_flag, a.status)) {
+        const uint32_t stage = sbase + s * STAGE_BYTES;
+        for (uint32_t pr = 0; pr < (uint32_t)NPAIR; ++pr) {
+          const uint32_t kk = g * NPAIR + pr, slot = kk % QK_PAIRS;
+          if (!mbar_wait_warp(bar(B_QK_EMPTY + slot), ((kk / QK_PAIRS) & 1u) ^ 1u, abort_flag, a.status)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t stage = sbase + s * STAGE_BYTES;
-          for (uint32_t b = 0; b < NBLK; ++b) {
-            const uint32_t kk = g * NBLK + b, slot = kk % QK_SLOTS;
-            if (!mbar_wait(bar(B_QK_EMPTY + slot), ((kk / QK_SLOTS) & 1u) ^ 1u, abort_flag, a.status)) {
-              ok = false;
-              break;
+          if (elect_one()) {
+#pragma unroll
+            for (uint32_t e = 0; e < 2; ++e) {
+              const uint32_t b = 2u * pr + e;
+              uint64_t ad, bd;
+              if (b < 16) {
+                ad = smem_desc(stage + ST_LAT + (b >> 2) * 16384u + (b & 3u) * 32u, 16, 1024, LAYOUT_SW128);
+                bd = smem_desc(sbase + OFF_QD + (b >> 2) * QD_LAT_BYTES + (b & 3u) * 32u, 16, 1024,
+                               LAYOUT_SW128);
+              } else {
+                ad = smem_desc(stage + ST_ROPE + (b - 16u) * 32u, 16, 512, LAYOUT_SW64);
+                bd = smem_desc(sbase + OFF_QD_ROPE + (b - 16u) * 32u, 16, 512, LAYOUT_SW64);
+              }
+              mma_i8(tmem + (2u * slot + e) * NQ, ad, bd, idesc_qk(NQ), 1u);
             }
-            tc_fence_after();
-            uint64_t ad, bd;
-            if (b < 16) {
-              ad = smem_desc(stage + ST_LAT + (b >> 2) * 16384u + (b & 3u) * 32u, 16, 1024, LAYOUT_SW128);
-              bd = smem_desc(sbase + OFF_QD + (b >> 2) * QD_LAT_BYTES + (b & 3u) * 32u, 16, 1024,
-                             LAYOUT_SW128);
-            } else {
-              ad = smem_desc(stage + ST_ROPE + (b - 16u) * 32u, 16, 512, LAYOUT_SW64);
-              bd = smem_desc(sbase + OFF_QD_ROPE + (b - 16u) * 32u, 16, 512, LAYOUT_SW64);
-            }
-            mma_i8(tmem + slot * Cfg<HK>::NQK, ad, bd, idesc_qk(Cfg<HK>::NQK), 1u);
             mma_commit(bar(B_QK_FULL + slot));
           }
-          if (!ok) break;
-          mma_commit(bar(B_KV_EMPTY + s));  // the raw stage's int8 rows are no longer read
+          __syncwarp();
         }
-        ++item_no;
+        if (!ok) break;
+        if (elect_one()) mma_commit(bar(B_KV_EMPTY + s));  // the raw stage's int8 rows are no longer read
+        __syncwarp();
       }
-      // all issued tcgen05 work retires before TMEM is freed
-      mma_commit(bar(B_FINAL));
-      mbar_wait(bar(B_FINAL), 0, abort_flag, a.status);
+      ++item_no;
     }
+    // all issued tcgen05 work retires before TMEM is freed
+    if (elect_one()) mma_commit(bar(B_FINAL));
+    __syncwarp();
+    mbar_wait_drain(bar(B_FINAL), 0, a.status);
   } else if (warp == 2) {
     // ================================================================ PV issuer
-    if (lane == 0) {
-      uint32_t g = 0, item_ord = 0;
-      bool ok = true;
-      const uint64_t ones_desc = smem_desc(sbase + OFF_ONES, 0, 0, LAYOUT_NONE);
-      for (uint32_t it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
-        const Item im = load_item(a, it);
-        if (im.ntiles == 0) continue;
-        for (uint32_t k = 0; k < im.ntiles && ok; ++k, ++g) {
-          if (k == 0 && item_ord > 0) {
-            // the epilogue has drained the previous item's O and l
-            if (!mbar_wait(bar(B_PV_EMPTY), (item_ord - 1) & 1u, abort_flag, a.status)) {
-              ok = false;
-              break;
-            }
+    // Converged warp, elected issue lane; one wait per 16-token V chunk.
+    uint32_t g = 0, item_ord = 0;
+    bool ok = true;
+    const uint64_t ones_desc = smem_desc(sbase + OFF_ONES, 0, 0, LAYOUT_NONE);
+    for (uint32_t it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+      const Item im = load_item(a, it);
+      if (im.ntiles == 0) continue;
+      for (uint32_t k = 0; k < im.ntiles && ok; ++k, ++g) {
+        if (k == 0 && item_ord > 0) {
+          // the epilogue has drained the previous item's O and l
+          if (!mbar_wait_warp(bar(B_PV_EMPTY), (item_ord - 1) & 1u, abort_flag, a.status)) {
+            ok = false;
+            break;
           }
-          if (!mbar_wait(bar(B_P_FULL), g & 1u, abort_flag, a.status)) {
+        }
+        if (!mbar_wait_warp(bar(B_P_FULL), g & 1u, abort_flag, a.status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        for (uint32_t c = 0; c < NCH; ++c) {
+          const uint32_t v = g * NCH + c, vs = v % V_SLOTS;
+          if (!mbar_wait_warp(bar(B_V_FULL + vs), (v / V_SLOTS) & 1u, abort_flag, a.status)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          for (uint32_t c = 0; c < NCH; ++c) {
-            const uint32_t kv = g * NCH + c, vs = kv & 1u;
-            if (!mbar_wait(bar(B_V_FULL + vs), (kv >> 1) & 1u, abort_flag, a.status)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            const uint32_t vbase = sbase + OFF_VR + vs * VCH_BYTES;
+          if (elect_one()) {
             const uint64_t bdesc = smem_desc(sbase + OFF_P + (c >> 2) * 4096u + (c & 3u) * 32u, 16, 1024,
                                              LAYOUT_SW128);
             const uint32_t acc_flag = (k == 0 && c == 0) ? 0u : 1u;
+            mma_f16(tmem + L_COL, ones_desc, bdesc, IDESC_L, acc_flag);
+            const uint32_t vbase = sbase + OFF_VR + vs * VCH_BYTES;
 #pragma unroll
             for (uint32_t mt = 0; mt < 4; ++mt)
-              mma_f16(tmem + PV_COL + mt * NPV, smem_desc(vbase + mt * 4096u, 2048, 1024, LAYOUT_SW128),
-                      bdesc, IDESC_PV, acc_flag);
-            mma_f16(tmem + L_COL, ones_desc, bdesc, IDESC_L, acc_flag);
+              mma_f16(tmem + PV_COL + mt * NPV, smem_desc(vbase + mt * VU_BYTES, 2048, 1024, LAYOUT_SW128), bdesc,
+                      IDESC_PV, acc_flag);
             mma_commit(bar(B_V_EMPTY + vs));
           }
-          if (!ok) break;
+          __syncwarp();
+        }
+        if (!ok) break;
+        if (elect_one()) {
           mma_commit(bar(B_PV_DONE));
           mma_commit(bar(B_P_EMPTY));
         }
-        ++item_ord;
+        __syncwarp();
       }
-      mma_commit(bar(B_FINAL_PV));
-      mbar_wait(bar(B_FINAL_PV), 0, abort_flag, a.status);
+      ++item_ord;
     }
+    if (elect_one()) mma_commit(bar(B_FINAL_PV));
+    __syncwarp();
+    mbar_wait_drain(bar(B_FINAL_PV), 0, a.status);
   } else if (warp == 3) {
     // spare warp of the issue warpgroup
-  } else if (warp < 8) {
+  } else if (warp < 12) {
     // ================================================================ epilogue
+    const uint32_t ew = warp - 4u;             // 0..7
+    const uint32_t hf = ew >> 2;               // head half
+    const uint32_t h0 = hf * HH;               // first head of this half
     const uint32_t q4 = warp & 3u;             // TMEM lane quarter
     const uint32_t trow = 32u * q4 + lane;     // token row in the tile / latent row in an M-tile
-    const uint32_t ew = warp - 4u;             // 0..3
     const uint32_t lane_addr = (32u * q4) << 16;
     float* qscale = reinterpret_cast<float*>(smem + OFF_QSCALE);
     float* redmax = reinterpret_cast<float*>(smem + OFF_REDMAX);
+    // running reference max per head: a warp-private copy (uniform across the
+    // warp; lane 0 writes between __syncwarp()s)
+    float* m_ref = reinterpret_cast<float*>(smem + OFF_MREF) + ew * 24;
     uint32_t g = 0, esync = 0;
     bool ok = true;
-    // bounded barrier among the 4 epilogue warps (an mbarrier, so a timeout
+    // bounded barrier among the epilogue warps (an mbarrier, so a timeout
     // elsewhere cannot strand a warp in bar.sync)
     auto epi_sync = [&]() -> bool {
       __syncwarp();
@@ -548,7 +642,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const bool single = a.seq_count[im.b] == 1;
       if (im.ntiles == 0) {
         // empty item: zeros, or an empty partial
-        for (uint32_t i = ew * 32 + lane; i < H * (uint32_t)R; i += 128) {
+        for (uint32_t i = ew * 32 + lane; i < H * (uint32_t)R; i += 32 * EPI_WARPS) {
           const uint32_t h = i / R, c = i % R;
           if (single) a.out[((uint64_t)im.b * H + h) * R + c] = 0.f;
           else a.part_o[((uint64_t)it * a.ws_heads + h) * R + c] = 0.f;
@@ -562,7 +656,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       // ---- query -> two int8 digits per element (x = s_h * (d0 + d1/256)), per-head scale
       {
         const float* qb = a.q + (uint64_t)im.b * H * W;
-        for (uint32_t h = ew; h < (uint32_t)HK; h += 4) {
+        for (uint32_t h = ew; h < (uint32_t)HK; h += EPI_WARPS) {
           float amax = 0.f;
           float v[18];
 #pragma unroll
@@ -575,6 +669,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           const float sh = amax > 0.f ? amax / 127.0f : 1.0f;
           const float inv = 1.0f / sh;
 #pragma unroll
+          const uint32_t qrow = (h / HH) * Cfg<HK>::NQH + 2u * (h % HH);  // digit-0 row
           for (int j = 0; j < 18; ++j) {
             const uint32_t kcol = lane + 32u * j;
             const float x = v[j] * inv;
@@ -584,12 +679,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             uint32_t o0, o1;
             if (kcol < 512) {
               base = smem + OFF_QD + (kcol >> 7) * QD_LAT_BYTES;
-              o0 = sw128_off(h, kcol & 127u);
-              o1 = sw128_off(h + HK, kcol & 127u);
+              o0 = sw128_off(qrow, kcol & 127u);
+              o1 = sw128_off(qrow + 1u, kcol & 127u);
             } else {
               base = smem + OFF_QD_ROPE;
-              o0 = sw64_off(h, kcol - 512u);
-              o1 = sw64_off(h + HK, kcol - 512u);
+              o0 = sw64_off(qrow, kcol - 512u);
+              o1 = sw64_off(qrow + 1u, kcol - 512u);
             }
             base[o0] = (uint8_t)(int8_t)(int)d0;
             base[o1] = (uint8_t)(int8_t)(int)d1;
@@ -601,12 +696,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         if (lane == 0) mbar_arrive(bar(B_Q_FULL));
         if (!epi_sync()) break;  // qscale visible to every epilogue thread
       }
-      // running reference max per head: a warp-private copy in shared memory
-      // (uniform across the warp; lane 0 writes between __syncwarp()s)
-      float* m_ref = reinterpret_cast<float*>(smem + OFF_MREF) + ew * 24;
       if (lane == 0)
-        for (int h = 0; h < HK; ++h) m_ref[h] = -INFINITY;
+        for (int h = 0; h < HH; ++h) m_ref[h] = -INFINITY;
       __syncwarp();
+      float qsc[HH];
+#pragma unroll
+      for (int h = 0; h < HH; ++h) qsc[h] = qscale[h0 + h];
       for (uint32_t k = 0; k < im.ntiles && ok; ++k, ++g) {
         const uint32_t s = g & 1u;
         const uint32_t tt0 = im.tok0 + k * TILE;
@@ -618,67 +713,40 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         const uint16_t* scrow =
             reinterpret_cast<const uint16_t*>(smem + s * STAGE_BYTES + ST_SC) + trow * NBLK;
-        float acc[HK];
+        float acc[HH];
 #pragma unroll
-        for (int h = 0; h < HK; ++h) acc[h] = 0.f;
-        // two Q8_0 blocks per TMEM round trip (18 blocks -> 9 rounds)
+        for (int h = 0; h < HH; ++h) acc[h] = 0.f;
+        // two Q8_0 blocks per TMEM round trip (18 blocks -> 9 rounds); this
+        // half reads its 2HH interleaved digit columns of each slot
         for (uint32_t b = 0; b < NBLK; b += 2) {
-          const uint32_t kk = g * NBLK + b;
-          const uint32_t slot0 = kk % QK_SLOTS, slot1 = (kk + 1) % QK_SLOTS;
-          if (!mbar_wait(bar(B_QK_FULL + slot0), (kk / QK_SLOTS) & 1u, abort_flag, a.status) ||
-              !mbar_wait(bar(B_QK_FULL + slot1), ((kk + 1) / QK_SLOTS) & 1u, abort_flag, a.status)) {
+          const uint32_t kk = g * NPAIR + (b >> 1), slot = kk % QK_PAIRS;
+          if (!mbar_wait(bar(B_QK_FULL + slot), (kk / QK_PAIRS) & 1u, abort_flag, a.status)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          // columns [0, HK): digit 0 of each head, [HK, 2HK): digit 1
-          constexpr int NQ = Cfg<HK>::NQK;
-          constexpr int NL = 2 * HK;  // columns actually used
-          uint32_t r0[NL], r1[NL];
-          const uint32_t ta0 = tmem + lane_addr + slot0 * NQ, ta1 = tmem + lane_addr + slot1 * NQ;
-          if constexpr (NL >= 32) {
-            TMEM_LD32(ta0, r0);
-            TMEM_LD32(ta1, r1);
-            if constexpr (NL == 48) {
-              TMEM_LD16(ta0 + 32, (r0 + 32));
-              TMEM_LD16(ta1 + 32, (r1 + 32));
-            }
-            if constexpr (NL == 40) {
-              TMEM_LD8(ta0 + 32, (r0 + 32));
-              TMEM_LD8(ta1 + 32, (r1 + 32));
-            }
-          } else {
-            TMEM_LD16(ta0, r0);
-            TMEM_LD16(ta1, r1);
-          }
+          uint32_t ra[2 * HH], rb[2 * HH];
+          const uint32_t ta = tmem + lane_addr + 2u * slot * NQ + hf * Cfg<HK>::NQH;
+          const uint32_t tb = ta + NQ;
+          tmem_ld<2 * HH>(ta, ra);
+          tmem_ld<2 * HH>(tb, rb);
           tmem_wait_ld();
-          {
-            uint32_t mg[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) mg[i] = MAGIC_I;
-#pragma unroll
-            for (int c = 0; c < NQ; c += 16) {
-              TMEM_ST16(ta0 + (uint32_t)c, mg);
-              TMEM_ST16(ta1 + (uint32_t)c, mg);
-            }
-            tmem_wait_st();
-          }
+          tmem_st_magic<2 * HH>(ta);
+          tmem_st_magic<2 * HH>(tb);
+          tmem_wait_st();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) {
-            mbar_arrive(bar(B_QK_EMPTY + slot0));
-            mbar_arrive(bar(B_QK_EMPTY + slot1));
-          }
+          if (lane == 0) mbar_arrive(bar(B_QK_EMPTY + slot));
           const uint32_t d2 = *reinterpret_cast<const uint32_t*>(scrow + b);  // scales of b, b+1
-          const float d0 = __half2float(__ushort_as_half((uint16_t)(d2 & 0xFFFFu)));
-          const float d1 = __half2float(__ushort_as_half((uint16_t)(d2 >> 16)));
+          const float da = __half2float(__ushort_as_half((uint16_t)(d2 & 0xFFFFu)));
+          const float db = __half2float(__ushort_as_half((uint16_t)(d2 >> 16)));
 #pragma unroll
-          for (int h = 0; h < HK; ++h) {
+          for (int h = 0; h < HH; ++h) {
             // exact int32 -> f32 through the bias: |dot| < 2^22
-            const float x00 = __uint_as_float(r0[h]) - MAGIC_F, x01 = __uint_as_float(r0[h + HK]) - MAGIC_F;
-            const float x10 = __uint_as_float(r1[h]) - MAGIC_F, x11 = __uint_as_float(r1[h + HK]) - MAGIC_F;
-            acc[h] = fmaf(d0, fmaf(x00, 256.f, x01), acc[h]);
-            acc[h] = fmaf(d1, fmaf(x10, 256.f, x11), acc[h]);
+            const float xa0 = __uint_as_float(ra[2 * h]) - MAGIC_F, xa1 = __uint_as_float(ra[2 * h + 1]) - MAGIC_F;
+            const float xb0 = __uint_as_float(rb[2 * h]) - MAGIC_F, xb1 = __uint_as_float(rb[2 * h + 1]) - MAGIC_F;
+            acc[h] = fmaf(da, fmaf(xa0, 256.f, xa1), acc[h]);
+            acc[h] = fmaf(db, fmaf(xb0, 256.f, xb1), acc[h]);
           }
         }
         if (!ok) break;
@@ -686,13 +754,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         if (lane == 0) mbar_arrive(bar(B_KV_EMPTY + s));  // done with the stage's scales
         // ---- online softmax over the tile (log2 domain): scores into acc[]
 #pragma unroll
-        for (int h = 0; h < HK; ++h) {
-          const float v = acc[h] * qscale[h];
-          acc[h] = (valid && h < (int)H && v == v) ? v : -INFINITY;
+        for (int h = 0; h < HH; ++h) {
+          const float v = acc[h] * qsc[h];
+          acc[h] = (valid && h0 + h < H && v == v) ? v : -INFINITY;
         }
-        float* rm = redmax + (g & 1u) * (4 * 24);
+        float* rm = redmax + (g & 1u) * (EPI_WARPS * 24);
 #pragma unroll
-        for (int h = 0; h < HK; ++h) {
+        for (int h = 0; h < HH; ++h) {
           float m = acc[h];
 #pragma unroll
           for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
@@ -704,12 +772,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         // lazy rescale: a head's reference max moves only when the tile max
         // exceeds it by more than 2^8 (so P <= 256 otherwise)
+        const float* rmh = rm + hf * 4 * 24;  // the 4 warps of this half
         auto tile_max = [&](int h) {
-          return fmaxf(fmaxf(rm[h], rm[24 + h]), fmaxf(rm[48 + h], rm[72 + h]));
+          return fmaxf(fmaxf(rmh[h], rmh[24 + h]), fmaxf(rmh[48 + h], rmh[72 + h]));
         };
         bool need_rescale = false;
 #pragma unroll
-        for (int h = 0; h < HK; ++h)
+        for (int h = 0; h < HH; ++h)
           need_rescale |= (m_ref[h] != -INFINITY) && (tile_max(h) > m_ref[h] + RESCALE_LOG2);
         if (need_rescale) {
           // O holds the PV of this item's earlier tiles: retire it, then scale
@@ -718,28 +787,26 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             break;
           }
           tc_fence_after();
-          // the 4 O^T M-tiles and the l columns (index 4) share the head columns
 #pragma unroll 1
-          for (uint32_t mt = 0; mt < 5; ++mt) {
-            uint32_t o[32];
-            const uint32_t ta = tmem + lane_addr + (mt < 4 ? PV_COL + mt * NPV : L_COL);
-            TMEM_LD32(ta, o);
+          for (uint32_t mt = 0; mt < 5; ++mt) {  // 4 O^T M-tiles, then l
+            uint32_t o[HH];
+            const uint32_t ta = tmem + lane_addr + (mt < 4 ? PV_COL + mt * NPV : L_COL) + 16u * hf;
+            tmem_ld<HH>(ta, o);
             tmem_wait_ld();
 #pragma unroll
-            for (int h = 0; h < HK; ++h) {
+            for (int h = 0; h < HH; ++h) {
               const float tm = tile_max(h);
               if (m_ref[h] != -INFINITY && tm > m_ref[h] + RESCALE_LOG2)
                 o[h] = __float_as_uint(__uint_as_float(o[h]) * exp2f(m_ref[h] - tm));
             }
-            TMEM_ST16(ta, o);
-            TMEM_ST16(ta + 16, (o + 16));
+            tmem_st<HH>(ta, o);
             tmem_wait_st();
           }
           tc_fence_before();
         }
         __syncwarp();
         if (lane == 0) {
-          for (int h = 0; h < HK; ++h) {
+          for (int h = 0; h < HH; ++h) {
             const float tm = tile_max(h);
             if (tm > m_ref[h] + RESCALE_LOG2) m_ref[h] = tm;
           }
@@ -754,9 +821,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           uint8_t* pb = smem + OFF_P + (trow >> 6) * 4096u;
           const uint32_t tb = (trow & 63u) * 2u;
 #pragma unroll
-          for (int h = 0; h < HK; ++h) {
+          for (int h = 0; h < HH; ++h) {
             const float p = acc[h] == -INFINITY ? 0.f : exp2f(acc[h] - m_ref[h]);
-            *reinterpret_cast<__half*>(pb + sw128_off((uint32_t)h, tb)) = __float2half_rn(p);
+            *reinterpret_cast<__half*>(pb + sw128_off(16u * hf + (uint32_t)h, tb)) = __float2half_rn(p);
           }
         }
         fence_proxy_async();
@@ -771,40 +838,36 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           break;
         }
         tc_fence_after();
-        float ltot[HK];
+        float ltot[HH];
         {
-          uint32_t lv[32];
-          TMEM_LD32(tmem + lane_addr + L_COL, lv);
+          uint32_t lv[HH];
+          tmem_ld<HH>(tmem + lane_addr + L_COL + 16u * hf, lv);
           tmem_wait_ld();
 #pragma unroll
-          for (int h = 0; h < HK; ++h) ltot[h] = __uint_as_float(lv[h]);
+          for (int h = 0; h < HH; ++h) ltot[h] = __uint_as_float(lv[h]);
         }
 #pragma unroll 1
         for (uint32_t mt = 0; mt < 4; ++mt) {
-          uint32_t o[32];
-          TMEM_LD32(tmem + lane_addr + PV_COL + mt * NPV, o);
+          uint32_t o[HH];
+          tmem_ld<HH>(tmem + lane_addr + PV_COL + mt * NPV + 16u * hf, o);
           tmem_wait_ld();
           const uint32_t c = mt * 128u + trow;
 #pragma unroll
-          for (int h = 0; h < HK; ++h) {
-            if (h >= (int)H) continue;
+          for (int h = 0; h < HH; ++h) {
+            const uint32_t hg = h0 + h;
+            if (hg >= H) continue;
             const float v = __uint_as_float(o[h]);
-            if (single) {
-              a.out[((uint64_t)im.b * H + h) * R + c] = ltot[h] > 0.f ? v / ltot[h] : 0.f;
-            } else {
-              a.part_o[((uint64_t)it * a.ws_heads + h) * R + c] = v;
-            }
+            if (single) a.out[((uint64_t)im.b * H + hg) * R + c] = ltot[h] > 0.f ? v / ltot[h] : 0.f;
+            else a.part_o[((uint64_t)it * a.ws_heads + hg) * R + c] = v;
           }
         }
-        if (!single && ew == 0 && lane < H) {
-          const float ln2 = 0.69314718055994531f;
-          const float mh = m_ref[lane] * ln2;
+        if (!single && q4 == 0 && lane < HH && h0 + lane < H) {
           float lh = 0.f;
 #pragma unroll
-          for (int h = 0; h < HK; ++h)
+          for (int h = 0; h < HH; ++h)
             if ((uint32_t)h == lane) lh = ltot[h];
-          a.part_ml[((uint64_t)it * a.ws_heads + lane) * 2 + 0] = mh;
-          a.part_ml[((uint64_t)it * a.ws_heads + lane) * 2 + 1] = lh;
+          a.part_ml[((uint64_t)it * a.ws_heads + h0 + lane) * 2 + 0] = m_ref[lane] * 0.69314718055994531f;
+          a.part_ml[((uint64_t)it * a.ws_heads + h0 + lane) * 2 + 1] = lh;
         }
         tc_fence_before();
         __syncwarp();
@@ -813,10 +876,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
   } else {
     // ================================================================ converter
-    const uint32_t cw = warp - 8u;                 // 0..3
-    const uint32_t tid = cw * 32u + lane;          // 0..127
-    const uint32_t tl = tid & 15u;                 // token within the chunk
-    const uint32_t gq = tid >> 4;                  // 64-column group (MN atom) 0..7
+    const uint32_t tid = (warp - 12u) * 32u + lane;  // 0..127
+    const uint32_t tl = tid & 15u;                   // token within the 16-token chunk
+    const uint32_t j = tid >> 4;                     // 16-column group within the M-tile, 0..7
     uint32_t g = 0;
     bool ok = true;
     for (uint32_t it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
@@ -830,52 +892,49 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         const uint8_t* stage = smem + s * STAGE_BYTES;
         for (uint32_t c = 0; c < NCH; ++c) {
-          const uint32_t kv = g * NCH + c, vs = kv & 1u;
-          if (!mbar_wait(bar(B_V_EMPTY + vs), ((kv >> 1) & 1u) ^ 1u, abort_flag, a.status)) {
+          const uint32_t t = c * VCH + tl;  // token row in the tile
+          const bool valid = tt0 + t < im.tok1;
+          // dequantize the whole chunk into registers first, so that the wait
+          // for a free slot overlaps this work: this thread covers token t,
+          // latent columns 128mt + 16j .. +15 (one raw 16-byte chunk) of each M-tile mt
+          uint32_t hv[4][8];
+#pragma unroll
+          for (uint32_t mt = 0; mt < 4; ++mt) {
+            if (valid) {
+              const uint4 raw = *reinterpret_cast<const uint4*>(stage + ST_LAT + mt * 16384u + sw128_off(t, j * 16u));
+              const __half2 dd = __half2half2(__ushort_as_half(
+                  *reinterpret_cast<const uint16_t*>(stage + ST_SC + t * 36u + (4u * mt + (j >> 1)) * 2u)));
+              const __half2 bias = __float2half2_rn(1152.0f);
+              const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const uint32_t uu = w[e] ^ 0x80808080u;  // q + 128 per byte
+                const uint32_t lo = __byte_perm(uu, 0x64646464u, 0x4140u);
+                const uint32_t hi = __byte_perm(uu, 0x64646464u, 0x4342u);
+                __half2 a0 = __hmul2(__hsub2(*reinterpret_cast<const __half2*>(&lo), bias), dd);
+                __half2 a1 = __hmul2(__hsub2(*reinterpret_cast<const __half2*>(&hi), bias), dd);
+                hv[mt][2 * e] = *reinterpret_cast<uint32_t*>(&a0);
+                hv[mt][2 * e + 1] = *reinterpret_cast<uint32_t*>(&a1);
+              }
+            } else {
+#pragma unroll
+              for (int e = 0; e < 8; ++e) hv[mt][e] = 0u;
+            }
+          }
+          const uint32_t v = g * NCH + c, vs = v % V_SLOTS;
+          if (!mbar_wait(bar(B_V_EMPTY + vs), ((v / V_SLOTS) & 1u) ^ 1u, abort_flag, a.status)) {
             ok = false;
             break;
           }
-          const uint32_t t = c * VCH + tl;  // token row in the tile
-          const bool valid = tt0 + t < im.tok1;
-          uint8_t* vrow = smem + OFF_VR + vs * VCH_BYTES + gq * 2048u + (tl >> 3) * 1024u + (tl & 7u) * 128u;
-          if (valid) {
-            const uint32_t j = gq >> 1;                  // latent box
-            const uint8_t* src = stage + ST_LAT + j * 16384u;
-            const uint32_t sc2 = *reinterpret_cast<const uint32_t*>(stage + ST_SC + t * 36u + gq * 4u);
-            const __half2 d0 = __half2half2(__ushort_as_half((uint16_t)(sc2 & 0xFFFFu)));
-            const __half2 d1 = __half2half2(__ushort_as_half((uint16_t)(sc2 >> 16)));
-            const __half2 bias = __float2half2_rn(1152.0f);
+          // unit mt of the chunk: MN atom j/4, chunks 2(j%4), 2(j%4)+1 of atom row t%8, K atom t/8
+          uint8_t* vrow = smem + OFF_VR + vs * VCH_BYTES + (j >> 2) * 2048u + (tl >> 3) * 1024u + (tl & 7u) * 128u;
+          const uint32_t ch0 = 2u * (j & 3u);
 #pragma unroll
-            for (uint32_t i = 0; i < 4; ++i) {
-              const uint32_t logical = (gq & 1u) * 4u + i;  // 16-byte chunk within the 128-byte row
-              const uint4 raw = *reinterpret_cast<const uint4*>(src + sw128_off(t, logical * 16u));
-              const __half2 dd = i < 2 ? d0 : d1;
-              uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-              uint32_t hv[8];
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const uint32_t u = w[e] ^ 0x80808080u;  // q + 128 per byte
-                const uint32_t lo = __byte_perm(u, 0x64646464u, 0x4140u);
-                const uint32_t hi = __byte_perm(u, 0x64646464u, 0x4342u);
-                __half2 a0 = __hsub2(*reinterpret_cast<const __half2*>(&lo), bias);
-                __half2 a1 = __hsub2(*reinterpret_cast<const __half2*>(&hi), bias);
-                a0 = __hmul2(a0, dd);
-                a1 = __hmul2(a1, dd);
-                hv[2 * e] = *reinterpret_cast<uint32_t*>(&a0);
-                hv[2 * e + 1] = *reinterpret_cast<uint32_t*>(&a1);
-              }
-              // 16 values = two 8-element (16-byte) chunks of the MN-major atom row
-#pragma unroll
-              for (uint32_t hlf = 0; hlf < 2; ++hlf) {
-                const uint32_t ch = 2u * i + hlf;  // chunk 0..7 along the 64 columns
-                *reinterpret_cast<uint4*>(vrow + (((ch ^ tl) & 7u) << 4)) =
-                    make_uint4(hv[4 * hlf], hv[4 * hlf + 1], hv[4 * hlf + 2], hv[4 * hlf + 3]);
-              }
-            }
-          } else {
-#pragma unroll
-            for (uint32_t ch = 0; ch < 8; ++ch)
-              *reinterpret_cast<uint4*>(vrow + (ch << 4)) = make_uint4(0, 0, 0, 0);
+          for (uint32_t mt = 0; mt < 4; ++mt) {
+            *reinterpret_cast<uint4*>(vrow + mt * VU_BYTES + (((ch0 ^ tl) & 7u) << 4)) =
+                make_uint4(hv[mt][0], hv[mt][1], hv[mt][2], hv[mt][3]);
+            *reinterpret_cast<uint4*>(vrow + mt * VU_BYTES + ((((ch0 + 1u) ^ tl) & 7u) << 4)) =
+                make_uint4(hv[mt][4], hv[mt][5], hv[mt][6], hv[mt][7]);
           }
           fence_proxy_async();
           __syncwarp();
