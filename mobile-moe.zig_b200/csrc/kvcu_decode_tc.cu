@@ -81,15 +81,16 @@ constexpr uint32_t OFF_MISC = OFF_P + 8192;                     // 228352
 // misc: mbarriers, then small words and arrays
 constexpr int B_KV_FULL = 0, B_KV_EMPTY = 2, B_QK_FULL = 4, B_QK_EMPTY = 7, B_V_FULL = 10,
               B_V_EMPTY = 12, B_P_FULL = 14, B_P_EMPTY = 15, B_PV_DONE = 16, B_PV_EMPTY = 17,
-              B_Q_FULL = 18, B_FINAL = 19, B_FINAL_PV = 20, B_EPI = 21, NUM_BARS = 22;
+              B_Q_FULL = 18, B_FINAL = 19, B_FINAL_PV = 20, B_EPI = 21 /* 2: one per head half */,
+              NUM_BARS = 23;
 static_assert(NUM_BARS * 8 <= 352, "mbarriers overlap the misc words");
 constexpr uint32_t OFF_TMEM_BASE = OFF_MISC + 352;            // u32
 constexpr uint32_t OFF_ABORT = OFF_MISC + 356;                // u32
 constexpr uint32_t OFF_ONES = OFF_MISC + 384;                 // 128 B of f16 1.0 (l = ones x P^T)
 constexpr uint32_t OFF_QSCALE = OFF_MISC + 512;               // float[24]
 constexpr uint32_t OFF_REDMAX = OFF_MISC + 640;               // float[2][8 warps][24]
-constexpr uint32_t OFF_MREF = OFF_REDMAX + 2 * EPI_WARPS * 24 * 4;  // float[8 warps][24]
-constexpr uint32_t SMEM_USED = OFF_MREF + EPI_WARPS * 24 * 4;
+constexpr uint32_t OFF_VOTE = OFF_REDMAX + 2 * EPI_WARPS * 24 * 4;  // u32[2][8 warps] rescale votes
+constexpr uint32_t SMEM_USED = OFF_VOTE + 2 * EPI_WARPS * 4;
 constexpr uint32_t SMEM_ALLOC = SMEM_USED + 1024;             // slack for 1024 alignment
 static_assert(SMEM_ALLOC <= 232448, "shared memory budget");
 
@@ -429,7 +430,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     mbar_init(bar(B_Q_FULL), EPI_WARPS);
     mbar_init(bar(B_FINAL), 1);
     mbar_init(bar(B_FINAL_PV), 1);
-    mbar_init(bar(B_EPI), EPI_WARPS);
+    mbar_init(bar(B_EPI + 0), EPI_WARPS / 2);
+    mbar_init(bar(B_EPI + 1), EPI_WARPS / 2);
     *abort_flag = 0u;
     uint32_t* ones = reinterpret_cast<uint32_t*>(smem + OFF_ONES);
     for (int i = 0; i < 32; ++i) ones[i] = 0x3C003C00u;  // f16 1.0 pairs
@@ -623,17 +625,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const uint32_t lane_addr = (32u * q4) << 16;
     float* qscale = reinterpret_cast<float*>(smem + OFF_QSCALE);
     float* redmax = reinterpret_cast<float*>(smem + OFF_REDMAX);
-    // running reference max per head: a warp-private copy (uniform across the
-    // warp; lane 0 writes between __syncwarp()s)
-    float* m_ref = reinterpret_cast<float*>(smem + OFF_MREF) + ew * 24;
     uint32_t g = 0, esync = 0;
     bool ok = true;
-    // bounded barrier among the epilogue warps (an mbarrier, so a timeout
-    // elsewhere cannot strand a warp in bar.sync)
+    // bounded barrier among the 4 epilogue warps of this half (an mbarrier, so
+    // a timeout elsewhere cannot strand a warp in bar.sync)
     auto epi_sync = [&]() -> bool {
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(B_EPI));
-      const bool r = mbar_wait(bar(B_EPI), esync & 1u, abort_flag, a.status);
+      if (lane == 0) mbar_arrive(bar(B_EPI + hf));
+      const bool r = mbar_wait(bar(B_EPI + hf), esync & 1u, abort_flag, a.status);
       ++esync;
       return r;
     };
@@ -653,10 +652,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         continue;
       }
-      // ---- query -> two int8 digits per element (x = s_h * (d0 + d1/256)), per-head scale
+      // ---- query -> two int8 digits per element (x = s_h * (d0 + d1/256)), per-head
+      // scale; each half's 4 warps encode that half's heads
       {
         const float* qb = a.q + (uint64_t)im.b * H * W;
-        for (uint32_t h = ew; h < (uint32_t)HK; h += EPI_WARPS) {
+        for (uint32_t hl = ew & 3u; hl < (uint32_t)HH; hl += 4) {
+          const uint32_t h = h0 + hl;
           float amax = 0.f;
           float v[18];
 #pragma unroll
@@ -668,8 +669,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
           const float sh = amax > 0.f ? amax / 127.0f : 1.0f;
           const float inv = 1.0f / sh;
+          const uint32_t qrow = hf * Cfg<HK>::NQH + 4u * (hl >> 1) + (hl & 1u);  // digit-0 row
 #pragma unroll
-          const uint32_t qrow = (h / HH) * Cfg<HK>::NQH + 2u * (h % HH);  // digit-0 row
           for (int j = 0; j < 18; ++j) {
             const uint32_t kcol = lane + 32u * j;
             const float x = v[j] * inv;
@@ -680,11 +681,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             if (kcol < 512) {
               base = smem + OFF_QD + (kcol >> 7) * QD_LAT_BYTES;
               o0 = sw128_off(qrow, kcol & 127u);
-              o1 = sw128_off(qrow + 1u, kcol & 127u);
+              o1 = sw128_off(qrow + 2u, kcol & 127u);
             } else {
               base = smem + OFF_QD_ROPE;
               o0 = sw64_off(qrow, kcol - 512u);
-              o1 = sw64_off(qrow + 1u, kcol - 512u);
+              o1 = sw64_off(qrow + 2u, kcol - 512u);
             }
             base[o0] = (uint8_t)(int8_t)(int)d0;
             base[o1] = (uint8_t)(int8_t)(int)d1;
@@ -694,14 +695,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         fence_proxy_async();
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(B_Q_FULL));
-        if (!epi_sync()) break;  // qscale visible to every epilogue thread
+        if (!epi_sync()) break;  // this half's qscale visible to its 4 warps
       }
-      if (lane == 0)
-        for (int h = 0; h < HH; ++h) m_ref[h] = -INFINITY;
-      __syncwarp();
-      float qsc[HH];
+      // running reference max per head (log2 domain), identical in the 4 warps of the half
+      float mref[HH];
 #pragma unroll
-      for (int h = 0; h < HH; ++h) qsc[h] = qscale[h0 + h];
+      for (int h = 0; h < HH; ++h) mref[h] = -INFINITY;
+      const float2* qsc2 = reinterpret_cast<const float2*>(qscale + h0);  // h0 is even
       for (uint32_t k = 0; k < im.ntiles && ok; ++k, ++g) {
         const uint32_t s = g & 1u;
         const uint32_t tt0 = im.tok0 + k * TILE;
@@ -713,11 +713,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         const uint16_t* scrow =
             reinterpret_cast<const uint16_t*>(smem + s * STAGE_BYTES + ST_SC) + trow * NBLK;
-        float acc[HH];
+        // per head pair (2p, 2p+1): sum over blocks of d_b * (256 x0 + x1), packed f32x2
+        float2 acc2[HH / 2];
 #pragma unroll
-        for (int h = 0; h < HH; ++h) acc[h] = 0.f;
+        for (int p = 0; p < HH / 2; ++p) acc2[p] = make_float2(0.f, 0.f);
+        const float2 neg_magic = make_float2(-MAGIC_F, -MAGIC_F);
+        const float2 c256 = make_float2(256.f, 256.f);
         // two Q8_0 blocks per TMEM round trip (18 blocks -> 9 rounds); this
-        // half reads its 2HH interleaved digit columns of each slot
+        // half reads its 2HH digit columns of each slot: per head pair
+        // [digit0 h, digit0 h+1, digit1 h, digit1 h+1]
         for (uint32_t b = 0; b < NBLK; b += 2) {
           const uint32_t kk = g * NPAIR + (b >> 1), slot = kk % QK_PAIRS;
           if (!mbar_wait(bar(B_QK_FULL + slot), (kk / QK_PAIRS) & 1u, abort_flag, a.status)) {
@@ -740,78 +744,96 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           const uint32_t d2 = *reinterpret_cast<const uint32_t*>(scrow + b);  // scales of b, b+1
           const float da = __half2float(__ushort_as_half((uint16_t)(d2 & 0xFFFFu)));
           const float db = __half2float(__ushort_as_half((uint16_t)(d2 >> 16)));
+          const float2 da2 = make_float2(da, da), db2 = make_float2(db, db);
 #pragma unroll
-          for (int h = 0; h < HH; ++h) {
-            // exact int32 -> f32 through the bias: |dot| < 2^22
-            const float xa0 = __uint_as_float(ra[2 * h]) - MAGIC_F, xa1 = __uint_as_float(ra[2 * h + 1]) - MAGIC_F;
-            const float xb0 = __uint_as_float(rb[2 * h]) - MAGIC_F, xb1 = __uint_as_float(rb[2 * h + 1]) - MAGIC_F;
-            acc[h] = fmaf(da, fmaf(xa0, 256.f, xa1), acc[h]);
-            acc[h] = fmaf(db, fmaf(xb0, 256.f, xb1), acc[h]);
+          for (int p = 0; p < HH / 2; ++p) {
+            // exact int32 -> f32 through the bias (|dot| < 2^22), then 256 x0 + x1
+            const float2 xa0 = __fadd2_rn(make_float2(__uint_as_float(ra[4 * p]), __uint_as_float(ra[4 * p + 1])),
+                                          neg_magic);
+            const float2 xa1 = __fadd2_rn(
+                make_float2(__uint_as_float(ra[4 * p + 2]), __uint_as_float(ra[4 * p + 3])), neg_magic);
+            const float2 xb0 = __fadd2_rn(make_float2(__uint_as_float(rb[4 * p]), __uint_as_float(rb[4 * p + 1])),
+                                          neg_magic);
+            const float2 xb1 = __fadd2_rn(
+                make_float2(__uint_as_float(rb[4 * p + 2]), __uint_as_float(rb[4 * p + 3])), neg_magic);
+            acc2[p] = __ffma2_rn(da2, __ffma2_rn(xa0, c256, xa1), acc2[p]);
+            acc2[p] = __ffma2_rn(db2, __ffma2_rn(xb0, c256, xb1), acc2[p]);
           }
         }
         if (!ok) break;
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(B_KV_EMPTY + s));  // done with the stage's scales
-        // ---- online softmax over the tile (log2 domain): scores into acc[]
+        // ---- online softmax over the tile (log2 domain)
+        float sc[HH];
 #pragma unroll
-        for (int h = 0; h < HH; ++h) {
-          const float v = acc[h] * qsc[h];
-          acc[h] = (valid && h0 + h < H && v == v) ? v : -INFINITY;
+        for (int p = 0; p < HH / 2; ++p) {
+          const float2 v = __fmul2_rn(acc2[p], qsc2[p]);
+          sc[2 * p] = (valid && h0 + 2 * p < H && v.x == v.x) ? v.x : -INFINITY;
+          sc[2 * p + 1] = (valid && h0 + 2 * p + 1 < H && v.y == v.y) ? v.y : -INFINITY;
         }
-        float* rm = redmax + (g & 1u) * (EPI_WARPS * 24);
+        // lazy rescale: a head's reference max moves only when some score of
+        // the tile exceeds it by more than 2^8 (so P <= 256 otherwise).  Each
+        // warp votes per head; the half combines the 4 votes after one sync.
+        uint32_t bits = 0;
 #pragma unroll
-        for (int h = 0; h < HH; ++h) {
-          float m = acc[h];
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-          if (lane == 0) rm[ew * 24 + h] = m;
-        }
+        for (int h = 0; h < HH; ++h) bits |= (sc[h] > mref[h] + RESCALE_LOG2) ? (1u << h) : 0u;
+        bits = __reduce_or_sync(0xffffffffu, bits);
+        uint32_t* vote = reinterpret_cast<uint32_t*>(smem + OFF_VOTE) + (g & 1u) * EPI_WARPS;
+        if (lane == 0) vote[ew] = bits;
         if (!epi_sync()) {
           ok = false;
           break;
         }
-        // lazy rescale: a head's reference max moves only when the tile max
-        // exceeds it by more than 2^8 (so P <= 256 otherwise)
-        const float* rmh = rm + hf * 4 * 24;  // the 4 warps of this half
-        auto tile_max = [&](int h) {
-          return fmaxf(fmaxf(rmh[h], rmh[24 + h]), fmaxf(rmh[48 + h], rmh[72 + h]));
-        };
-        bool need_rescale = false;
+        const uint4 vw = *reinterpret_cast<const uint4*>(vote + 4 * hf);  // ordered by the mbarrier wait
+        const uint32_t flagged = vw.x | vw.y | vw.z | vw.w;
+        if (flagged) {
+          // exact tile max of the flagged heads over the half's 128 rows
+          float* rm = redmax + (g & 1u) * (EPI_WARPS * 24);
 #pragma unroll
-        for (int h = 0; h < HH; ++h)
-          need_rescale |= (m_ref[h] != -INFINITY) && (tile_max(h) > m_ref[h] + RESCALE_LOG2);
-        if (need_rescale) {
-          // O holds the PV of this item's earlier tiles: retire it, then scale
-          if (!mbar_wait(bar(B_PV_DONE), (g - 1) & 1u, abort_flag, a.status)) {
+          for (int h = 0; h < HH; ++h) {
+            float m = sc[h];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            if (lane == 0) rm[ew * 24 + h] = m;
+          }
+          if (!epi_sync()) {
             ok = false;
             break;
           }
-          tc_fence_after();
-#pragma unroll 1
-          for (uint32_t mt = 0; mt < 5; ++mt) {  // 4 O^T M-tiles, then l
-            uint32_t o[HH];
-            const uint32_t ta = tmem + lane_addr + (mt < 4 ? PV_COL + mt * NPV : L_COL) + 16u * hf;
-            tmem_ld<HH>(ta, o);
-            tmem_wait_ld();
+          const float* rmh = rm + hf * 4 * 24;  // the 4 warps of this half
+          float tmax[HH];
+          bool need_rescale = false;
 #pragma unroll
-            for (int h = 0; h < HH; ++h) {
-              const float tm = tile_max(h);
-              if (m_ref[h] != -INFINITY && tm > m_ref[h] + RESCALE_LOG2)
-                o[h] = __float_as_uint(__uint_as_float(o[h]) * exp2f(m_ref[h] - tm));
-            }
-            tmem_st<HH>(ta, o);
-            tmem_wait_st();
-          }
-          tc_fence_before();
-        }
-        __syncwarp();
-        if (lane == 0) {
           for (int h = 0; h < HH; ++h) {
-            const float tm = tile_max(h);
-            if (tm > m_ref[h] + RESCALE_LOG2) m_ref[h] = tm;
+            tmax[h] = fmaxf(fmaxf(rmh[h], rmh[24 + h]), fmaxf(rmh[48 + h], rmh[72 + h]));
+            need_rescale |= ((flagged >> h) & 1u) && mref[h] != -INFINITY;
           }
+          if (need_rescale) {
+            // O holds the PV of this item's earlier tiles: retire it, then scale
+            if (!mbar_wait(bar(B_PV_DONE), (g - 1) & 1u, abort_flag, a.status)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+#pragma unroll 1
+            for (uint32_t mt = 0; mt < 5; ++mt) {  // 4 O^T M-tiles, then l
+              uint32_t o[HH];
+              const uint32_t ta = tmem + lane_addr + (mt < 4 ? PV_COL + mt * NPV : L_COL) + 16u * hf;
+              tmem_ld<HH>(ta, o);
+              tmem_wait_ld();
+#pragma unroll
+              for (int h = 0; h < HH; ++h)
+                if (((flagged >> h) & 1u) && mref[h] != -INFINITY)
+                  o[h] = __float_as_uint(__uint_as_float(o[h]) * exp2f(mref[h] - tmax[h]));
+              tmem_st<HH>(ta, o);
+              tmem_wait_st();
+            }
+            tc_fence_before();
+          }
+#pragma unroll
+          for (int h = 0; h < HH; ++h)
+            if ((flagged >> h) & 1u) mref[h] = tmax[h];
         }
-        __syncwarp();
         // ---- P (f16) -> shared memory, K-major 128B-swizzled [head][token]
         if (!mbar_wait(bar(B_P_EMPTY), (g & 1u) ^ 1u, abort_flag, a.status)) {
           ok = false;
@@ -822,7 +844,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           const uint32_t tb = (trow & 63u) * 2u;
 #pragma unroll
           for (int h = 0; h < HH; ++h) {
-            const float p = acc[h] == -INFINITY ? 0.f : exp2f(acc[h] - m_ref[h]);
+            const float p = sc[h] == -INFINITY ? 0.f : exp2f(sc[h] - mref[h]);
             *reinterpret_cast<__half*>(pb + sw128_off(16u * hf + (uint32_t)h, tb)) = __float2half_rn(p);
           }
         }
@@ -862,11 +884,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           }
         }
         if (!single && q4 == 0 && lane < HH && h0 + lane < H) {
-          float lh = 0.f;
+          float lh = 0.f, mh = 0.f;
 #pragma unroll
           for (int h = 0; h < HH; ++h)
-            if ((uint32_t)h == lane) lh = ltot[h];
-          a.part_ml[((uint64_t)it * a.ws_heads + h0 + lane) * 2 + 0] = m_ref[lane] * 0.69314718055994531f;
+            if ((uint32_t)h == lane) {
+              lh = ltot[h];
+              mh = mref[h];
+            }
+          a.part_ml[((uint64_t)it * a.ws_heads + h0 + lane) * 2 + 0] = mh * 0.69314718055994531f;
           a.part_ml[((uint64_t)it * a.ws_heads + h0 + lane) * 2 + 1] = lh;
         }
         tc_fence_before();
