@@ -76,7 +76,7 @@ def read_peaks():
 
 def read_traffic_profile():
     """Per-context-token DRAM bytes of the decode kernel from the committed ncu summary."""
-    path = os.path.join(ROOT, "profiles", "decode_config5_ncu.md")
+    path = os.path.join(ROOT, "profiles", "decode_tc_config5_ncu.md")
     try:
         for line in open(path):
             if line.startswith("dram_bytes_per_ctx_token:"):
@@ -436,7 +436,7 @@ def run_ours(args, rank, world, local_rank):
                        "shard_tokens": loads, "l2": "inputs larger than L2 (>=0.4 GB of KV per layer per GPU)"},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
-            "roofline": {"kernel": "mla_decode (k_decode + k_combine), one layer per launch",
+            "roofline": {"kernel": "mla_decode layer call (k_decode_tc + k_combine; 99.3% k_decode_tc)",
                          "bound": "hbm", "achieved": dec_gbs, "peak": peak, "unit": "GB/s",
                          "frac": dec_gbs / peak, "peak_source": peak_kind,
                          "traffic": (traffic_per_tok * avg_ctx_per_launch if traffic_per_tok else None),

@@ -5,8 +5,8 @@
  *
  * It is the drop-in boundary for mobile-moe.zig's KV-cache hot path.  The
  * reference's host code (Zig) would bind these functions with `extern fn`
- * declarations exactly as src/metal_backend.zig:7-26 binds src/metal_bridge.c;
- * INTEGRATION.md shows that binding.  Conventions copied from
+ * declarations exactly as src/metal_backend.zig:7-26 binds src/metal_bridge.c.
+ * Conventions copied from
  * src/metal_bridge.c: a process-wide last-error string (:50-52), `int` return
  * codes (0 = success, negative = error, :54-87), opaque handles with explicit
  * release (:89-96).  No entry point ever falls back to the CPU: without a
@@ -30,6 +30,17 @@
  *
  * Threading: handles are not re-entrant (as KVCache is not, because of its
  * shared dequant scratch, src/kv_cache.zig:59-60); use one host thread per GPU.
+ *
+ * Deliberate differences from the reference, where its behaviour is undefined
+ * or wrong: f32->f16 in the f16-subnormal range rounds to nearest even (the
+ * reference mis-shifts, src/dequant.zig:76-77); a NaN quotient x/d quantizes
+ * to 0; Q8_0 pools start zeroed (src/kv_cache.zig:151-152 leaves them
+ * undefined) and the checkpoint header's padding bytes are written as zeros;
+ * loadFromFile bounds-checks block ids and takes them off the free list
+ * (src/kv_cache.zig:527-533 only retains them); the attention score is
+ * multiplied by `scale` rather than divided by sqrt(head_dim)
+ * (src/inference.zig:613); reusePrefixBlocks retains the cached block before
+ * releasing the one it replaces (src/kv_cache.zig:418-424 releases first).
  */
 #ifndef KVCUDA_H
 #define KVCUDA_H

@@ -10,9 +10,9 @@
 // kvcu_decode.cu.  Sequence 0 is the reference's single sequence; more
 // sequences share the pool (the multi-sequence serving surface).
 //
-// Deviations from the reference, all documented in kvcuda.h / DESIGN.md:
-// Q8_0 pools start zeroed; loadFromFile bounds-checks block ids and takes
-// them off the free list; reusePrefixBlocks retains before it releases.
+// Deviations from the reference (also listed in kvcuda.h): Q8_0 pools start
+// zeroed; loadFromFile bounds-checks block ids and takes them off the free
+// list; reusePrefixBlocks retains before it releases.
 #include <cuda_runtime.h>
 #include <fcntl.h>
 #include <stdio.h>
