@@ -193,6 +193,36 @@ uint32_t kvcu_decode_last_launches(const kvcu_decode_ws* ws);
 int kvcu_decode_ws_set_impl(kvcu_decode_ws* ws, int impl);
 int kvcu_decode_last_impl(const kvcu_decode_ws* ws);
 
+/* Decode without any allocation.  No counterpart in the reference: this is an
+ * extra entry point of this library for callers that must not allocate device
+ * memory at decode time -- a runtime that reserves all of its memory up front
+ * (an allocator that owns the whole device, a hard memory budget), code running
+ * where an allocation would stall or fail (a latency-critical serving loop),
+ * or embedders with no workspace lifetime to manage.  It plans and decodes one
+ * layer in a single call, with the same semantics and kernels as
+ * kvcu_decode_plan + kvcu_mla_decode, but keeps the split-KV scratch (work
+ * items, per-item partial outputs) in a fixed array compiled into the library
+ * (KVCU_NOALLOC_SCRATCH_BYTES of device memory per device, reserved when the
+ * library's device code is loaded) instead of a kvcu_decode_ws.
+ *   Limits: n <= KVCU_NOALLOC_MAX_BATCH, 1 <= n_heads <= KVCU_NOALLOC_MAX_HEADS;
+ *   larger requests return KVCU_ERR_INVALID_ARG and change nothing.  Long
+ *   sequences are split into at most KVCU_NOALLOC_MAX_ITEMS work items in all.
+ *   The first call on a device looks up the array's device address (with that
+ *   device current); make that first call before capturing `stream` into a
+ *   graph.  The scratch is one per device and is not guarded: calls that may
+ *   overlap on the same device (other streams, other host threads) race on it
+ *   and must be serialised by the caller. */
+#define KVCU_NOALLOC_MAX_BATCH 64u
+#define KVCU_NOALLOC_MAX_HEADS 32u
+#define KVCU_NOALLOC_MAX_ITEMS 256u
+#define KVCU_NOALLOC_SCRATCH_BYTES \
+  (KVCU_NOALLOC_MAX_ITEMS * KVCU_NOALLOC_MAX_HEADS * (512u + 2u) * 4u + KVCU_NOALLOC_MAX_ITEMS * 16u + \
+   16u + 2u * KVCU_NOALLOC_MAX_BATCH * 4u)
+int kvcu_mla_decode_noalloc(kvcu_pool* pool, uint32_t layer, uint32_t n, const uint32_t* seq_ids,
+                            uint32_t n_seqs, const uint32_t* table_offsets, const uint32_t* tables,
+                            const uint32_t* lens, const float* q, uint32_t n_heads, float scale,
+                            float* out, void* stream);
+
 /* ------------------------------------------------------------ checkpoint I/O
  * Bytes of the pool section of a v1 checkpoint in the reference's order
  * (src/kv_cache.zig:484-492): Q8_0 -> all [rows][ceil(kv_rank/32)] 34-byte

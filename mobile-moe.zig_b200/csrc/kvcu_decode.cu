@@ -460,6 +460,18 @@ int kvcu_launch_plan(kvcu_decode_ws* ws, const kvcu_pool* p, uint32_t n, const u
   return kvcu_check_cuda(cudaGetLastError(), "plan kernel launch");
 }
 
+// The same plan with an explicit item target, for a workspace that holds fewer
+// items than the default (items <= n + target, so ws->max_items >= n + target + 1
+// keeps every item).
+int kvcu_launch_plan_target(kvcu_decode_ws* ws, const kvcu_pool* p, uint32_t n,
+                            const uint32_t* seq_ids, uint32_t n_seqs, const uint32_t* lens,
+                            uint32_t target, cudaStream_t st) {
+  const uint32_t align = p->block_size > 128u ? p->block_size : 128u;
+  k_plan<<<1, 1024, 0, st>>>(n, seq_ids, n_seqs, lens, target, align, ws->max_items, ws->items,
+                             ws->meta, ws->seq_first, ws->seq_count);
+  return kvcu_check_cuda(cudaGetLastError(), "plan kernel launch");
+}
+
 int kvcu_launch_decode(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint32_t n,
                        const uint32_t* seq_ids, uint32_t n_seqs, const uint32_t* toff,
                        const uint32_t* tables, const uint32_t* lens, const float* q,

@@ -74,6 +74,9 @@ int kvcu_launch_synth(uint64_t seed, uint64_t a, uint32_t n_rows, const uint32_t
 int kvcu_decode_setup(kvcu_decode_ws* ws);
 int kvcu_launch_plan(kvcu_decode_ws* ws, const kvcu_pool* p, uint32_t n, const uint32_t* seq_ids,
                      uint32_t n_seqs, const uint32_t* lens, cudaStream_t st);
+int kvcu_launch_plan_target(kvcu_decode_ws* ws, const kvcu_pool* p, uint32_t n,
+                            const uint32_t* seq_ids, uint32_t n_seqs, const uint32_t* lens,
+                            uint32_t target, cudaStream_t st);
 // ---- tensor-core decode (kvcu_decode_tc.cu) ----
 bool kvcu_decode_tc_supported(const kvcu_pool* p, uint32_t n_heads);
 int kvcu_launch_decode_tc(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint32_t n,

@@ -73,6 +73,7 @@ _SIGS = {
     "kvcu_decode_last_launches": (_u32, [_vp]),
     "kvcu_decode_ws_set_impl": (_i32, [_vp, _i32]),
     "kvcu_decode_last_impl": (_i32, [_vp]),
+    "kvcu_mla_decode_noalloc": (_i32, [_vp, _u32, _u32, _vp, _u32, _vp, _vp, _vp, _vp, _u32, _f32, _vp, _vp]),
     "kvcu_pool_read_checkpoint": (_i32, [_vp, _u64, _u64, _vp, _vp]),
     "kvcu_pool_write_checkpoint": (_i32, [_vp, _u64, _u64, _vp, _vp]),
     "kvcu_synth_rows": (_i32, [_u64, _u64, _u32, _vp, _vp, _u32, _f32, _vp, _vp]),
