@@ -52,16 +52,7 @@ def config5_lengths(seed=SEED, n=N_SEQS):
     return np.minimum(np.floor(np.exp(u)).astype(np.int64), LEN_HI)
 
 
-def lpt_partition(lens, n_parts):
-    """Greedy LPT: longest sequence first to the least-loaded part."""
-    order = np.argsort(-lens, kind="stable")
-    loads = [0] * n_parts
-    parts = [[] for _ in range(n_parts)]
-    for s in order:
-        k = min(range(n_parts), key=lambda i: (loads[i], i))
-        parts[k].append(int(s))
-        loads[k] += int(lens[s])
-    return [sorted(p) for p in parts], loads
+from sharding import aggregate_throughput, lpt_partition  # noqa: E402
 
 
 def read_peaks():
@@ -96,12 +87,13 @@ class ClockSampler:
     def __init__(self, device_index):
         self.dev = device_index
         self.proc = None
-        self.lines = []
+        self.lines = []  # (host arrival time, csv line)
+        self.window = None
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits", "-lms", "200",
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits", "-lms", "50",
                  "-i", str(self.dev)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
@@ -111,7 +103,11 @@ class ClockSampler:
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.perf_counter(), line.strip()))
+
+    def mark(self, t0, t1):
+        """Host-time bounds of the timed region: only samples inside it are summarised."""
+        self.window = (t0, t1)
 
     def __exit__(self, *exc):
         if self.proc:
@@ -125,7 +121,9 @@ class ClockSampler:
     def summary(self):
         sm, smax, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for t, ln in self.lines:
+            if self.window and not (self.window[0] <= t <= self.window[1]):
+                continue
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 9:
                 continue
@@ -329,16 +327,19 @@ def run_ours(args, rank, world, local_rank):
         if world > 1:
             dist.barrier()
 
-    for k in range(args.warmup):
-        step(k, False)
-    st.synchronize()
-    barrier()
-    torch.cuda.synchronize()
-    ev["launches"] = 0
-    ctx_tokens = 0
-    t_start = torch.cuda.Event(enable_timing=True)
-    t_end = torch.cuda.Event(enable_timing=True)
+    # the clock sampler runs from before the warm-up (nvidia-smi takes a moment to
+    # start); only the samples that arrive inside the timed region are kept
     with ClockSampler(physical_gpu(local_rank)) as clk:
+        for k in range(args.warmup):
+            step(k, False)
+        st.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        ev["launches"] = 0
+        ctx_tokens = 0
+        t_start = torch.cuda.Event(enable_timing=True)
+        t_end = torch.cuda.Event(enable_timing=True)
+        h0 = time.perf_counter()
         torch.cuda.nvtx.range_push("timed")
         t_start.record(st)
         for k in range(args.warmup, args.warmup + args.steps):
@@ -347,6 +348,7 @@ def run_ours(args, rank, world, local_rank):
         t_end.record(st)
         torch.cuda.nvtx.range_pop()
         st.synchronize()
+        clk.mark(h0, time.perf_counter())
     barrier()
     torch.cuda.synchronize()
     elapsed = t_start.elapsed_time(t_end) / 1e3
@@ -359,16 +361,9 @@ def run_ours(args, rank, world, local_rank):
     dec_bytes = (avg_ctx_per_launch * Q8_ROW_BYTES + n * H * W * 4 + n * H * R * 4 + tables_bytes)
 
     # ---- cross-rank aggregation (outside the timed region)
-    tot = torch.tensor([float(ctx_tokens), elapsed, dec_bytes / avg_dec], dtype=torch.float64, device=dev)
-    if world > 1:
-        tmax = tot.clone()
-        dist.all_reduce(tot, op=dist.ReduceOp.SUM)
-        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
-        job_tokens, job_time = tot[0].item(), tmax[1].item()
-        dec_gbs = tot[2].item() / world / 1e9
-    else:
-        job_tokens, job_time = ctx_tokens, elapsed
-        dec_gbs = dec_bytes / avg_dec / 1e9
+    job_tokens, job_time = aggregate_throughput(ctx_tokens, elapsed, dist if world > 1 else None, dev)
+    # per-GPU decode bandwidth, averaged over ranks
+    dec_gbs = aggregate_throughput(dec_bytes / avg_dec, 0.0, dist if world > 1 else None, dev)[0] / world / 1e9
     value = job_tokens / job_time
 
     # ---- e2e through the host-buffer API (pinned host memory, copies inside)
@@ -396,14 +391,8 @@ def run_ours(args, rank, world, local_rank):
         e2e_tokens += int((lens0 + base + k + 1).sum()) * NL
     torch.cuda.synchronize()
     e2e_time = time.perf_counter() - t0
-    e = torch.tensor([float(e2e_tokens), e2e_time], dtype=torch.float64, device=dev)
-    if world > 1:
-        emax = e.clone()
-        dist.all_reduce(e, op=dist.ReduceOp.SUM)
-        dist.all_reduce(emax, op=dist.ReduceOp.MAX)
-        e2e_value = e[0].item() / emax[1].item()
-    else:
-        e2e_value = e2e_tokens / e2e_time if e2e_time > 0 else None
+    e_tok, e_time = aggregate_throughput(e2e_tokens, e2e_time, dist if world > 1 else None, dev)
+    e2e_value = e_tok / e_time if e_time > 0 else None
     h2d = NL * n * (W * 4 + 8 + H * W * 4)
     d2h = NL * n * H * R * 4
 
@@ -459,7 +448,7 @@ def run_ours(args, rank, world, local_rank):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--e2e-warmup", type=int, default=1)
