@@ -49,12 +49,13 @@ constexpr int NBLK = 18;             // Q8_0 blocks per row (16 latent + 2 rope)
 constexpr int NQK_MAX = 48;          // QK N: 2 digits x up to 24 heads
 constexpr int HMAX = NQK_MAX / 2;    // heads supported by the tensor-core kernel
 constexpr int NPV = 32;              // PV N: heads padded to 32
-constexpr int QK_PAIRS = 3;          // TMEM ring of QK accumulator pairs (2 blocks each; cols 0..287)
-constexpr int NPAIR = NBLK / 2;      // 9 block pairs per tile
+constexpr int QK_GROUPS = 2;         // TMEM ring of QK accumulator groups (cols 0..287)
+constexpr int GB = 3;                // Q8_0 blocks per group (one TMEM round trip of the epilogue)
+constexpr int NGRP = NBLK / GB;      // 6 block groups per tile
 constexpr int PV_COL = 352;          // O^T accumulator: 4 M-tiles x 32 cols = [352, 480)
 constexpr int L_COL = 480;           // softmax denominators l[h] (ones x P^T) = [480, 512)
 constexpr int TMEM_COLS = 512;
-static_assert(QK_PAIRS * 2 * NQK_MAX <= PV_COL, "TMEM map");
+static_assert(QK_GROUPS * GB * NQK_MAX <= PV_COL && NBLK % GB == 0, "TMEM map");
 constexpr int VCH = 16;              // tokens per V chunk (one f16 MMA K-step)
 constexpr int NCH = TILE / VCH;      // 8 token chunks per tile
 constexpr int V_SLOTS = 2;           // V chunk ring depth
@@ -144,7 +145,8 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
 
 // Bounded wait: gives up after ~2^31 clocks (about a second) or when another
 // role has aborted; any give-up records a timeout in the status word.
-__device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity,
+// (Inlined: a call would have to run under several setmaxnreg budgets.)
+__device__ __forceinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity,
                                             volatile uint32_t* abort_flag, uint32_t* status) {
   const long long t0 = clock64();
   while (true) {
@@ -167,6 +169,20 @@ __device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, vo
   const bool ok = mbar_wait(bar, parity, abort_flag, status);
   return __all_sync(0xffffffffu, ok);
 }
+// Per-warpgroup register budgets (setmaxnreg).  The block launches with 128
+// registers per thread (checked on the host before the first launch); the
+// split below never asks for more than that total, so every .inc completes.
+constexpr uint32_t LAUNCH_REGS = 128, ISSUE_REGS = 64, EPI_REGS = 176, CVT_REGS = 88;
+static_assert(128 * ISSUE_REGS + 256 * EPI_REGS + 128 * CVT_REGS <= NTHREADS * LAUNCH_REGS,
+              "register split exceeds the launch allocation");
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
 // One lane of a converged warp (the lane that issues tcgen05 work).
 __device__ __forceinline__ bool elect_one() {
   uint32_t pred = 0;
@@ -177,7 +193,7 @@ __device__ __forceinline__ bool elect_one() {
 }
 // Wait for this CTA's own asynchronous work (copies, MMAs) to retire: bounded
 // by time only, so it still waits after another role has aborted.
-__device__ __noinline__ void mbar_wait_drain(uint32_t bar, uint32_t parity, uint32_t* status) {
+__device__ __forceinline__ void mbar_wait_drain(uint32_t bar, uint32_t parity, uint32_t* status) {
   const long long t0 = clock64();
   while (!mbar_try(bar, parity)) {
     if (clock64() - t0 > (1ll << 31)) {
@@ -352,6 +368,13 @@ __device__ __forceinline__ void tmem_st_magic(uint32_t ta) {
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
+// Ties registers written by an earlier tcgen05.ld to a point after
+// tcgen05.wait::ld, so no use of them is scheduled before the wait.
+template <int N>
+__device__ __forceinline__ void reg_fence(uint32_t (&r)[N]) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) asm volatile("" : "+r"(r[i]));
+}
 __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
@@ -415,7 +438,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     mbar_init(bar(B_KV_FULL + 1), 1);
     mbar_init(bar(B_KV_EMPTY + 0), 1 + 4 + EPI_WARPS);  // QK issuer commit + converter + epilogue
     mbar_init(bar(B_KV_EMPTY + 1), 1 + 4 + EPI_WARPS);
-    for (int i = 0; i < QK_PAIRS; ++i) {
+    for (int i = 0; i < QK_GROUPS; ++i) {
       mbar_init(bar(B_QK_FULL + i), 1);
       mbar_init(bar(B_QK_EMPTY + i), EPI_WARPS);
     }
@@ -453,13 +476,17 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   if (warp >= 4 && warp < 8) {
     // pre-load every QK slot with the conversion bias (one warp per lane quarter)
     const uint32_t ta = tmem + ((32u * (warp & 3u)) << 16);
-    for (int c = 0; c < QK_PAIRS * 2 * NQ; c += 8) tmem_st_magic<8>(ta + (uint32_t)c);
+    for (int c = 0; c < QK_GROUPS * GB * NQ; c += 8) tmem_st_magic<8>(ta + (uint32_t)c);
     tmem_wait_st();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
 
+  // Register split by warpgroup (set once, with each warpgroup converged): the
+  // issue and converter warpgroups hand registers to the two epilogue ones.
+  if (warp < 4) {
+    setmaxnreg_dec<ISSUE_REGS>();
   if (warp == 0) {
     // ================================================================ producer
     if (lane == 0) {
@@ -522,17 +549,17 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         tc_fence_after();
         const uint32_t stage = sbase + s * STAGE_BYTES;
-        for (uint32_t pr = 0; pr < (uint32_t)NPAIR; ++pr) {
-          const uint32_t kk = g * NPAIR + pr, slot = kk % QK_PAIRS;
-          if (!mbar_wait_warp(bar(B_QK_EMPTY + slot), ((kk / QK_PAIRS) & 1u) ^ 1u, abort_flag, a.status)) {
+        for (uint32_t gi = 0; gi < (uint32_t)NGRP; ++gi) {
+          const uint32_t kk = g * NGRP + gi, slot = kk % QK_GROUPS;
+          if (!mbar_wait_warp(bar(B_QK_EMPTY + slot), ((kk / QK_GROUPS) & 1u) ^ 1u, abort_flag, a.status)) {
             ok = false;
             break;
           }
           tc_fence_after();
           if (elect_one()) {
 #pragma unroll
-            for (uint32_t e = 0; e < 2; ++e) {
-              const uint32_t b = 2u * pr + e;
+            for (uint32_t e = 0; e < (uint32_t)GB; ++e) {
+              const uint32_t b = GB * gi + e;
               uint64_t ad, bd;
               if (b < 16) {
                 ad = smem_desc(stage + ST_LAT + (b >> 2) * 16384u + (b & 3u) * 32u, 16, 1024, LAYOUT_SW128);
@@ -542,7 +569,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 ad = smem_desc(stage + ST_ROPE + (b - 16u) * 32u, 16, 512, LAYOUT_SW64);
                 bd = smem_desc(sbase + OFF_QD_ROPE + (b - 16u) * 32u, 16, 512, LAYOUT_SW64);
               }
-              mma_i8(tmem + (2u * slot + e) * NQ, ad, bd, idesc_qk(NQ), 1u);
+              mma_i8(tmem + (GB * slot + e) * NQ, ad, bd, idesc_qk(NQ), 1u);
             }
             mma_commit(bar(B_QK_FULL + slot));
           }
@@ -613,9 +640,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     if (elect_one()) mma_commit(bar(B_FINAL_PV));
     __syncwarp();
     mbar_wait_drain(bar(B_FINAL_PV), 0, a.status);
-  } else if (warp == 3) {
-    // spare warp of the issue warpgroup
+  }  // warp 3: spare warp of the issue warpgroup
   } else if (warp < 12) {
+    setmaxnreg_inc<EPI_REGS>();
     // ================================================================ epilogue
     const uint32_t ew = warp - 4u;             // 0..7
     const uint32_t hf = ew >> 2;               // head half
@@ -713,52 +740,51 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         const uint16_t* scrow =
             reinterpret_cast<const uint16_t*>(smem + s * STAGE_BYTES + ST_SC) + trow * NBLK;
-        // per head pair (2p, 2p+1): sum over blocks of d_b * (256 x0 + x1), packed f32x2
-        float2 acc2[HH / 2];
+        // per head: sum over blocks of d_b * (256 x0 + x1)
+        float acc[HH];
 #pragma unroll
-        for (int p = 0; p < HH / 2; ++p) acc2[p] = make_float2(0.f, 0.f);
-        const float2 neg_magic = make_float2(-MAGIC_F, -MAGIC_F);
-        const float2 c256 = make_float2(256.f, 256.f);
-        // two Q8_0 blocks per TMEM round trip (18 blocks -> 9 rounds); this
-        // half reads its 2HH digit columns of each slot: per head pair
-        // [digit0 h, digit0 h+1, digit1 h, digit1 h+1]
-        for (uint32_t b = 0; b < NBLK; b += 2) {
-          const uint32_t kk = g * NPAIR + (b >> 1), slot = kk % QK_PAIRS;
-          if (!mbar_wait(bar(B_QK_FULL + slot), (kk / QK_PAIRS) & 1u, abort_flag, a.status)) {
+        for (int h = 0; h < HH; ++h) acc[h] = 0.f;
+        // Three Q8_0 blocks per TMEM round trip (18 blocks -> 6 groups); this
+        // half reads its 2HH digit columns of each slot, per head pair
+        // [digit0 h, digit0 h+1, digit1 h, digit1 h+1].
+        for (uint32_t gi = 0; gi < (uint32_t)NGRP; ++gi) {
+          const uint32_t kk = g * NGRP + gi, slot = kk % QK_GROUPS;
+          if (!mbar_wait(bar(B_QK_FULL + slot), (kk / QK_GROUPS) & 1u, abort_flag, a.status)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          uint32_t ra[2 * HH], rb[2 * HH];
-          const uint32_t ta = tmem + lane_addr + 2u * slot * NQ + hf * Cfg<HK>::NQH;
-          const uint32_t tb = ta + NQ;
-          tmem_ld<2 * HH>(ta, ra);
-          tmem_ld<2 * HH>(tb, rb);
+          uint32_t r0[2 * HH], r1[2 * HH], r2[2 * HH];
+          const uint32_t ta = tmem + lane_addr + GB * slot * NQ + hf * Cfg<HK>::NQH;
+          tmem_ld<2 * HH>(ta, r0);
+          tmem_ld<2 * HH>(ta + NQ, r1);
+          tmem_ld<2 * HH>(ta + 2 * NQ, r2);
           tmem_wait_ld();
+          reg_fence(r0);
+          reg_fence(r1);
+          reg_fence(r2);
+          // re-bias the group for its next use while the values are combined
           tmem_st_magic<2 * HH>(ta);
-          tmem_st_magic<2 * HH>(tb);
+          tmem_st_magic<2 * HH>(ta + NQ);
+          tmem_st_magic<2 * HH>(ta + 2 * NQ);
+          const float d0 = __half2float(__ushort_as_half(scrow[GB * gi]));
+          const float d1 = __half2float(__ushort_as_half(scrow[GB * gi + 1]));
+          const float d2 = __half2float(__ushort_as_half(scrow[GB * gi + 2]));
+#pragma unroll
+          for (int h = 0; h < HH; ++h) {
+            // exact int32 -> f32 through the bias (|dot| < 2^22), then 256 x0 + x1
+            const int c0 = 4 * (h >> 1) + (h & 1), c1 = c0 + 2;
+            const float x00 = __uint_as_float(r0[c0]) - MAGIC_F, x01 = __uint_as_float(r0[c1]) - MAGIC_F;
+            const float x10 = __uint_as_float(r1[c0]) - MAGIC_F, x11 = __uint_as_float(r1[c1]) - MAGIC_F;
+            const float x20 = __uint_as_float(r2[c0]) - MAGIC_F, x21 = __uint_as_float(r2[c1]) - MAGIC_F;
+            acc[h] = fmaf(d0, fmaf(x00, 256.f, x01), acc[h]);
+            acc[h] = fmaf(d1, fmaf(x10, 256.f, x11), acc[h]);
+            acc[h] = fmaf(d2, fmaf(x20, 256.f, x21), acc[h]);
+          }
           tmem_wait_st();
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(bar(B_QK_EMPTY + slot));
-          const uint32_t d2 = *reinterpret_cast<const uint32_t*>(scrow + b);  // scales of b, b+1
-          const float da = __half2float(__ushort_as_half((uint16_t)(d2 & 0xFFFFu)));
-          const float db = __half2float(__ushort_as_half((uint16_t)(d2 >> 16)));
-          const float2 da2 = make_float2(da, da), db2 = make_float2(db, db);
-#pragma unroll
-          for (int p = 0; p < HH / 2; ++p) {
-            // exact int32 -> f32 through the bias (|dot| < 2^22), then 256 x0 + x1
-            const float2 xa0 = __fadd2_rn(make_float2(__uint_as_float(ra[4 * p]), __uint_as_float(ra[4 * p + 1])),
-                                          neg_magic);
-            const float2 xa1 = __fadd2_rn(
-                make_float2(__uint_as_float(ra[4 * p + 2]), __uint_as_float(ra[4 * p + 3])), neg_magic);
-            const float2 xb0 = __fadd2_rn(make_float2(__uint_as_float(rb[4 * p]), __uint_as_float(rb[4 * p + 1])),
-                                          neg_magic);
-            const float2 xb1 = __fadd2_rn(
-                make_float2(__uint_as_float(rb[4 * p + 2]), __uint_as_float(rb[4 * p + 3])), neg_magic);
-            acc2[p] = __ffma2_rn(da2, __ffma2_rn(xa0, c256, xa1), acc2[p]);
-            acc2[p] = __ffma2_rn(db2, __ffma2_rn(xb0, c256, xb1), acc2[p]);
-          }
         }
         if (!ok) break;
         __syncwarp();
@@ -767,9 +793,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         float sc[HH];
 #pragma unroll
         for (int p = 0; p < HH / 2; ++p) {
-          const float2 v = __fmul2_rn(acc2[p], qsc2[p]);
-          sc[2 * p] = (valid && h0 + 2 * p < H && v.x == v.x) ? v.x : -INFINITY;
-          sc[2 * p + 1] = (valid && h0 + 2 * p + 1 < H && v.y == v.y) ? v.y : -INFINITY;
+          const float2 q2 = qsc2[p];
+          const float vx = acc[2 * p] * q2.x, vy = acc[2 * p + 1] * q2.y;
+          sc[2 * p] = (valid && h0 + 2 * p < H && vx == vx) ? vx : -INFINITY;
+          sc[2 * p + 1] = (valid && h0 + 2 * p + 1 < H && vy == vy) ? vy : -INFINITY;
         }
         // lazy rescale: a head's reference max moves only when some score of
         // the tile exceeds it by more than 2^8 (so P <= 256 otherwise).  Each
@@ -900,6 +927,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       }
     }
   } else {
+    setmaxnreg_dec<CVT_REGS>();
     // ================================================================ converter
     const uint32_t tid = (warp - 12u) * 32u + lane;  // 0..127
     const uint32_t tl = tid & 15u;                   // token within the 16-token chunk
@@ -922,28 +950,30 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           // dequantize the whole chunk into registers first, so that the wait
           // for a free slot overlaps this work: this thread covers token t,
           // latent columns 128mt + 16j .. +15 (one raw 16-byte chunk) of each M-tile mt
-          uint32_t hv[4][8];
+          // Branch-free: rows past the sequence end (stale stage bytes) get a
+          // zero scale, so their V is exactly 0 ((1152+q)-1152 is finite).
+          uint4 raw[4];
+          uint16_t dsc[4];
 #pragma unroll
           for (uint32_t mt = 0; mt < 4; ++mt) {
-            if (valid) {
-              const uint4 raw = *reinterpret_cast<const uint4*>(stage + ST_LAT + mt * 16384u + sw128_off(t, j * 16u));
-              const __half2 dd = __half2half2(__ushort_as_half(
-                  *reinterpret_cast<const uint16_t*>(stage + ST_SC + t * 36u + (4u * mt + (j >> 1)) * 2u)));
-              const __half2 bias = __float2half2_rn(1152.0f);
-              const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+            raw[mt] = *reinterpret_cast<const uint4*>(stage + ST_LAT + mt * 16384u + sw128_off(t, j * 16u));
+            dsc[mt] = *reinterpret_cast<const uint16_t*>(stage + ST_SC + t * 36u + (4u * mt + (j >> 1)) * 2u);
+          }
+          uint32_t hv[4][8];
+          const __half2 bias = __float2half2_rn(1152.0f);
 #pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const uint32_t uu = w[e] ^ 0x80808080u;  // q + 128 per byte
-                const uint32_t lo = __byte_perm(uu, 0x64646464u, 0x4140u);
-                const uint32_t hi = __byte_perm(uu, 0x64646464u, 0x4342u);
-                __half2 a0 = __hmul2(__hsub2(*reinterpret_cast<const __half2*>(&lo), bias), dd);
-                __half2 a1 = __hmul2(__hsub2(*reinterpret_cast<const __half2*>(&hi), bias), dd);
-                hv[mt][2 * e] = *reinterpret_cast<uint32_t*>(&a0);
-                hv[mt][2 * e + 1] = *reinterpret_cast<uint32_t*>(&a1);
-              }
-            } else {
+          for (uint32_t mt = 0; mt < 4; ++mt) {
+            const __half2 dd = __half2half2(__ushort_as_half(valid ? dsc[mt] : (uint16_t)0));
+            const uint32_t w[4] = {raw[mt].x, raw[mt].y, raw[mt].z, raw[mt].w};
 #pragma unroll
-              for (int e = 0; e < 8; ++e) hv[mt][e] = 0u;
+            for (int e = 0; e < 4; ++e) {
+              const uint32_t uu = w[e] ^ 0x80808080u;  // q + 128 per byte
+              const uint32_t lo = __byte_perm(uu, 0x64646464u, 0x4140u);
+              const uint32_t hi = __byte_perm(uu, 0x64646464u, 0x4342u);
+              __half2 a0 = __hmul2(__hsub2(*reinterpret_cast<const __half2*>(&lo), bias), dd);
+              __half2 a1 = __hmul2(__hsub2(*reinterpret_cast<const __half2*>(&hi), bias), dd);
+              hv[mt][2 * e] = *reinterpret_cast<uint32_t*>(&a0);
+              hv[mt][2 * e + 1] = *reinterpret_cast<uint32_t*>(&a1);
             }
           }
           const uint32_t v = g * NCH + c, vs = v % V_SLOTS;
@@ -1033,9 +1063,19 @@ template <int HK>
 int launch_tc(int grid, const CUtensorMap& lat, const CUtensorMap& rope, const TcArgs& a, cudaStream_t st) {
   static bool configured = false;
   if (!configured) {
-    int rc = kvcu_check_cuda(cudaFuncSetAttribute(k_decode_tc<HK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                  (int)SMEM_ALLOC),
-                             "cudaFuncSetAttribute(decode_tc)");
+    // the setmaxnreg split assumes exactly LAUNCH_REGS registers per thread at
+    // launch; with fewer, an epilogue .inc could wait forever, so refuse
+    cudaFuncAttributes fa;
+    int rc = kvcu_check_cuda(cudaFuncGetAttributes(&fa, k_decode_tc<HK>), "cudaFuncGetAttributes(decode_tc)");
+    if (rc) return rc;
+    if (fa.numRegs != (int)LAUNCH_REGS) {
+      kvcu_set_error("decode_tc: built with %d registers per thread, the register split needs %u",
+                     fa.numRegs, LAUNCH_REGS);
+      return KVCU_ERR_UNSUPPORTED;
+    }
+    rc = kvcu_check_cuda(cudaFuncSetAttribute(k_decode_tc<HK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              (int)SMEM_ALLOC),
+                         "cudaFuncSetAttribute(decode_tc)");
     if (rc) return rc;
     configured = true;
   }
