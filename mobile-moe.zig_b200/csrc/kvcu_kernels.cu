@@ -134,6 +134,64 @@ __global__ void __launch_bounds__(256) k_append(PoolArgs a, uint32_t n_rows,
   }
 }
 
+// Fast append for the usual shapes (kv_rank and rope_dim multiples of 32,
+// 16-byte aligned source rows): one warp per row, so the row's sequence /
+// table lookups happen once; each 8-lane group owns one 32-element block per
+// step (one float4 per lane, a 3-step shuffle max, one 4-byte store per lane).
+// Same bytes as k_append.
+template <bool QUANT>
+__global__ void __launch_bounds__(256) k_append_rows(PoolArgs a, uint32_t n_rows,
+                                                     const float* __restrict__ latent, uint64_t ls,
+                                                     const float* __restrict__ rope, uint64_t ps,
+                                                     const uint32_t* __restrict__ row_seq,
+                                                     const uint32_t* __restrict__ row_pos,
+                                                     uint32_t n_seqs, const uint32_t* __restrict__ toff,
+                                                     const uint32_t* __restrict__ tables,
+                                                     uint32_t* __restrict__ lens) {
+  const uint32_t lane = threadIdx.x & 31u, grp = lane >> 3, sub = lane & 7u;
+  const uint64_t nwarps = ((uint64_t)gridDim.x * blockDim.x) >> 5;
+  const uint32_t nblk = a.nbk + a.nbp;
+  for (uint64_t r = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < n_rows; r += nwarps) {
+    const uint32_t s = row_seq[r], pos = row_pos[r];
+    uint64_t row;
+    if (!resolve_row(a, s, pos, n_seqs, toff, tables, lane, &row)) continue;
+    // len = max(len, pos + 1), src/kv_cache.zig:358-360
+    if (lens && lane == 0) atomicMax(lens + s, pos + 1u);
+    for (uint32_t b0 = 0; b0 < nblk; b0 += 4) {
+      const uint32_t b = b0 + grp;
+      const bool act = b < nblk;
+      float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (act) {
+        const float* src = b < a.nbk ? latent + r * ls + 32u * b + 4u * sub
+                                     : rope + r * ps + 32u * (b - a.nbk) + 4u * sub;
+        x = __ldg(reinterpret_cast<const float4*>(src));
+      }
+      if (QUANT) {
+        float amax = fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w)));
+#pragma unroll
+        for (int o = 1; o < 8; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        const float d = kvcu::q8_scale(amax);
+        const float inv = d > 0.0f ? __frcp_rn(d) : 0.0f;
+        char4 q = make_char4(0, 0, 0, 0);
+        if (d > 0.0f) {
+          q.x = kvcu::q8_value_fast(x.x, d, inv);
+          q.y = kvcu::q8_value_fast(x.y, d, inv);
+          q.z = kvcu::q8_value_fast(x.z, d, inv);
+          q.w = kvcu::q8_value_fast(x.w, d, inv);
+        }
+        if (act) {
+          *reinterpret_cast<char4*>(a.qs + row * (32u * nblk) + 32u * b + 4u * sub) = q;
+          if (sub == 0) a.sc[row * nblk + b] = kvcu::f32_to_f16(d);
+        }
+      } else if (act) {
+        float* dst = b < a.nbk ? a.kv + row * a.kv_rank + 32u * b + 4u * sub
+                               : a.pe + row * a.rope_dim + 32u * (b - a.nbk) + 4u * sub;
+        *reinterpret_cast<float4*>(dst) = x;
+      }
+    }
+  }
+}
+
 // One warp per (row, 32-element block): out = f16ToF32(d) * q, or the f32 row.
 // Rows come either from one table (table != nullptr, row r = position r) or
 // from (row_seq[r], row_pos[r]) through the CSR tables.
@@ -251,6 +309,19 @@ int kvcu_launch_append(kvcu_pool* p, uint32_t layer, uint32_t n_rows, const floa
                        const uint32_t* tables, uint32_t* lens, cudaStream_t st) {
   if (n_rows == 0) return KVCU_OK;
   PoolArgs a = pool_args(p, layer);
+  const bool rows_ok = p->kv_rank % 32 == 0 && p->rope_dim % 32 == 0 && ls % 4 == 0 && ps % 4 == 0 &&
+                       (reinterpret_cast<uintptr_t>(latent) & 15) == 0 &&
+                       (reinterpret_cast<uintptr_t>(rope) & 15) == 0;
+  if (rows_ok) {
+    const int g = grid_for(n_rows, 256);
+    if (p->quantized)
+      k_append_rows<true><<<g, 256, 0, st>>>(a, n_rows, latent, ls, rope, ps, row_seq, row_pos, n_seqs,
+                                             toff, tables, lens);
+    else
+      k_append_rows<false><<<g, 256, 0, st>>>(a, n_rows, latent, ls, rope, ps, row_seq, row_pos, n_seqs,
+                                              toff, tables, lens);
+    return kvcu_check_cuda(cudaGetLastError(), "append kernel launch");
+  }
   const uint32_t nper = p->quantized ? p->nblk : (p->kv_rank + p->rope_dim + 31) / 32;
   const int g = grid_for((uint64_t)n_rows * nper, 256);
   if (p->quantized)

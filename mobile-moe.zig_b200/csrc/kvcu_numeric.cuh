@@ -110,6 +110,18 @@ __device__ __forceinline__ int8_t q8_value(float x, float d) {
   return (int8_t)(int)r;
 }
 
+// q8_value through a multiply: t = x * inv with inv = RN(1/d) lies within
+// |x/d| * 2^-22 <= 3.1e-5 of RN(x/d) for |x/d| <= 128, so both round to the
+// same integer unless t is within that distance of a half-integer; there (and
+// for NaN / inf) the IEEE quotient decides.  Same results as q8_value.
+__device__ __forceinline__ int8_t q8_value_fast(float x, float d, float inv) {
+  const float t = x * inv;
+  const float fr = fabsf(t - truncf(t));
+  if (!(fabsf(fr - 0.5f) > 1e-4f)) return q8_value(x, d);
+  const float r = fminf(fmaxf(roundf(t), -127.0f), 127.0f);
+  return (int8_t)(int)r;
+}
+
 // Block scale from the block's max |x| (NaN-free max): d = amax/127 or 0.
 __device__ __forceinline__ float q8_scale(float amax) {
   return amax > 0.0f ? __fdiv_rn(amax, 127.0f) : 0.0f;

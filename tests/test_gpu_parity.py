@@ -259,6 +259,38 @@ def test_q8_edge_values_bit_exact(kv, oracle):
     assert c.pool().read_checkpoint() == o.serialize()
 
 
+def test_q8_near_tie_quotients_bit_exact(kv, oracle):
+    """Quotients x/d within a few ulps of half-integers, for many inexact
+    scales: the append kernel's multiply-then-check rounding must agree with
+    roundf(x / d) everywhere, including both sides of every tie."""
+    rng = np.random.default_rng(77)
+    n = 64
+    rows = np.zeros((n, W), np.float32)
+    for r in range(n):
+        for b in range(W // 32):
+            amax = np.float32(np.exp(rng.uniform(-8, 8)))
+            d = np.float32(amax / np.float32(127.0))
+            blk = np.empty(32, np.float32)
+            blk[0] = amax if rng.random() < 0.5 else -amax
+            k = rng.integers(-127, 127, 31).astype(np.float32)
+            x = ((k + np.float32(0.5)) * d).astype(np.float32)
+            step = rng.integers(-3, 4, 31)
+            for i in range(31):
+                v = x[i]
+                for _ in range(abs(int(step[i]))):
+                    v = np.nextafter(v, np.float32(np.inf) if step[i] > 0 else np.float32(-np.inf))
+                x[i] = v
+            blk[1:] = np.clip(x, -amax, amax)
+            rows[r, 32 * b:32 * b + 32] = rng.permutation(blk)
+    c = kv.KVCache.with_blocks(1, R, P, 4, 16, quantized=True)
+    o = oracle.Pool(1, 4, 16, R, P, True)
+    c.ensureCapacity(n)
+    pos = np.arange(n, dtype=np.uint32)
+    c.appendBatch(0, np.zeros(n, np.uint32), pos, rows)
+    o.put_rows(0, np.array(c.seq_block_table(0), np.uint32)[pos // 16], pos % 16, rows)
+    assert c.pool().read_checkpoint() == o.serialize()
+
+
 # ------------------------------------------------------------------ decode parity
 def _decode_case(kv, oracle, lens, bs, quant, n_heads, seed, outlier_p=0.0, n_layers=1, impl=None,
                  expect_impl=None):
