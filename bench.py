@@ -93,7 +93,7 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits", "-lms", "50",
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits", "-lms", "20",
                  "-i", str(self.dev)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
@@ -106,8 +106,9 @@ class ClockSampler:
             self.lines.append((time.perf_counter(), line.strip()))
 
     def mark(self, t0, t1):
-        """Host-time bounds of the timed region: only samples inside it are summarised."""
-        self.window = (t0, t1)
+        """Host-time bounds of the timed region: only samples inside it are summarised
+        (plus one sampling period after it, for a sample taken inside but read late)."""
+        self.window = (t0, t1 + 0.03)
 
     def __exit__(self, *exc):
         if self.proc:
@@ -204,8 +205,8 @@ def run_reference(args, rank, world):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded N(0,1), 1% x20 outliers)",
-        "config": {"workload": "config5_sharded_serving_step (bounded CPU sample)",
-                   "sample": desc},
+        "config": {"workload": "config5_sharded_serving_step", "kv_dtype": "q8_0", "heads": H,
+                   "kv_rank": R, "rope_dim": P, "sample": desc},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": desc},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "the Zig reference cannot be built here (no zig toolchain); its CPU path is timed "
