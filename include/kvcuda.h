@@ -80,6 +80,7 @@ extern "C" {
 #define KVCU_STATUS_BAD_LEN 0x8u     /* lens[s] > table length * block_size */
 #define KVCU_STATUS_TIMEOUT 0x10u    /* a bounded device-side wait gave up */
 #define KVCU_STATUS_MISALIGNED 0x20u /* a decode tile did not start on a block-row boundary */
+#define KVCU_STATUS_BAD_PLAN 0x40u   /* the decode plan has more CTA ranges than the decode grid */
 
 /* metal_get_last_error, src/metal_bridge.c:50-52.  Thread-local. */
 const char* kvcu_get_last_error(void);
@@ -217,7 +218,7 @@ int kvcu_decode_last_impl(const kvcu_decode_ws* ws);
 #define KVCU_NOALLOC_MAX_ITEMS 256u
 #define KVCU_NOALLOC_SCRATCH_BYTES \
   (KVCU_NOALLOC_MAX_ITEMS * KVCU_NOALLOC_MAX_HEADS * (512u + 2u) * 4u + KVCU_NOALLOC_MAX_ITEMS * 16u + \
-   16u + 2u * KVCU_NOALLOC_MAX_BATCH * 4u)
+   16u + (KVCU_NOALLOC_MAX_ITEMS + 1u) * 4u + 2u * KVCU_NOALLOC_MAX_BATCH * 4u)
 int kvcu_mla_decode_noalloc(kvcu_pool* pool, uint32_t layer, uint32_t n, const uint32_t* seq_ids,
                             uint32_t n_seqs, const uint32_t* table_offsets, const uint32_t* tables,
                             const uint32_t* lens, const float* q, uint32_t n_heads, float scale,

@@ -276,11 +276,15 @@ kvcu_decode_ws* kvcu_decode_ws_create(int device, uint32_t max_batch, uint32_t m
   ws->max_batch = max_batch;
   ws->max_heads = max_heads;
   int rc = kvcu_decode_setup(ws);
-  // items <= batch + target items (each sequence adds at most one partial item)
-  ws->max_items = max_batch + (uint32_t)ws->decode_ctas * 4u + 1u;
+  // items <= batch + ranges - 1 (each cut between CTA ranges splits at most one entry)
+  ws->max_ranges = (uint32_t)ws->decode_ctas;
+  ws->max_items = max_batch + ws->max_ranges + 1u;
   const uint64_t mi = ws->max_items;
   if (!rc) rc = kvcu_check_cuda(cudaMalloc(&ws->items, mi * sizeof(kvcu_item)), "cudaMalloc(items)");
   if (!rc) rc = kvcu_check_cuda(cudaMalloc(&ws->meta, 4 * sizeof(uint32_t)), "cudaMalloc(meta)");
+  if (!rc)
+    rc = kvcu_check_cuda(cudaMalloc(&ws->ranges, (ws->max_ranges + 1ull) * sizeof(uint32_t)),
+                         "cudaMalloc(ranges)");
   if (!rc) rc = kvcu_check_cuda(cudaMalloc(&ws->seq_first, max_batch * 4ull), "cudaMalloc");
   if (!rc) rc = kvcu_check_cuda(cudaMalloc(&ws->seq_count, max_batch * 4ull), "cudaMalloc");
   if (!rc) rc = kvcu_check_cuda(cudaMalloc(&ws->part_o, mi * max_heads * 512ull * 4), "cudaMalloc");
@@ -298,6 +302,7 @@ int kvcu_decode_ws_destroy(kvcu_decode_ws* ws) {
   DeviceGuard g(ws->device);
   cudaFree(ws->items);
   cudaFree(ws->meta);
+  cudaFree(ws->ranges);
   cudaFree(ws->seq_first);
   cudaFree(ws->seq_count);
   cudaFree(ws->part_o);

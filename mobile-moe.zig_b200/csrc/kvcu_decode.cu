@@ -8,9 +8,9 @@
 //
 // Structure (one decode = three stream-ordered launches, or two when the plan
 // is reused across layers):
-//   k_plan      one CTA: splits every sequence into work items of at most C
-//               tokens, C chosen so the item count is ~4 waves of the GPU;
-//   k_decode    persistent CTAs (one per SM) stride over the items; each
+//   k_plan      one CTA: cuts the batch into one equal-cost range of work
+//               items per decode CTA, splitting a sequence where a cut falls;
+//   k_decode    persistent CTAs (one per SM) run their range of items; each
 //               streams its KV tile-by-tile through shared memory and keeps
 //               (m, l, o[512]) per head; single-item sequences write the final
 //               output, the others write partials to the workspace;
@@ -31,7 +31,6 @@ constexpr int KS = W + 4;        // padded smem row stride (conflict-free float4
 constexpr int NT = 256;          // threads per CTA
 constexpr int NW = NT / 32;      // warps
 constexpr int KSLICE = W / NW;   // 72 K elements per warp in the QK stage
-constexpr int TARGET_WAVES = 4;  // work items per resident CTA (load balance)
 
 struct DecodeArgs {
   uint32_t layer, num_blocks, block_size, nblk;
@@ -52,6 +51,7 @@ struct DecodeArgs {
   float* out;
   const kvcu_item* items;
   const uint32_t* meta;
+  const uint32_t* ranges;
   const uint32_t* seq_count;
   float* part_o;
   float* part_ml;
@@ -70,47 +70,107 @@ __device__ __forceinline__ float warp_sum(float v) {
 }
 
 // ------------------------------------------------------------------ plan
+// Balanced split-KV plan. Every entry b costs PLAN_UNIT per `align`-token unit
+// of its length plus PLAN_ITEM for finishing an item (draining O, writing the
+// output or a partial). The entries are laid end to end on a cost line of
+// length T in batch order, and the line is cut into G equal ranges, one per
+// decode CTA: range c is [P_c, P_{c+1}) with P_c = floor(c T / G). A cut that
+// falls inside an entry's units splits the entry there (rounded up to a unit),
+// so every CTA gets the same cost within one unit and at most G - 1 entries are
+// split. Items are numbered in batch order; CTA c runs items
+// [ranges[c], ranges[c+1]).
+//
 // Items start at multiples of `align` (= max(128, block size)), so every
 // 128-token tile of the tensor-core kernel covers whole physical blocks (or a
-// 128-row-aligned part of one).
+// 128-row-aligned part of one). An entry's last item is open-ended: decode
+// clips it to the live length, so a plan stays valid while appends grow the
+// sequences.
+constexpr uint32_t PLAN_UNIT = 8;  // cost of one align-token unit
+constexpr uint32_t PLAN_ITEM = 4;  // cost of one item besides its units
+
+__device__ __forceinline__ unsigned long long ceil_div_u64(unsigned long long x, unsigned long long y) {
+  return (x + y - 1) / y;
+}
+
 __global__ void __launch_bounds__(1024) k_plan(uint32_t n, const uint32_t* __restrict__ seq_ids,
                                                uint32_t n_seqs, const uint32_t* __restrict__ lens,
-                                               uint32_t target_items, uint32_t align, uint32_t max_items,
+                                               uint32_t max_ranges, uint32_t align, uint32_t max_items,
                                                kvcu_item* __restrict__ items,
                                                uint32_t* __restrict__ meta,
+                                               uint32_t* __restrict__ ranges,
                                                uint32_t* __restrict__ seq_first,
                                                uint32_t* __restrict__ seq_count) {
   __shared__ unsigned long long s_total;
+  __shared__ unsigned long long s_wcost[32];
   __shared__ uint32_t s_warp[32];
-  __shared__ uint32_t s_carry;
-  const uint32_t tid = threadIdx.x, lane = tid & 31u, wid = tid >> 5;
+  __shared__ uint32_t s_carry;           // items of the earlier chunks
+  __shared__ unsigned long long s_ccarry;  // cost of the earlier chunks
+  const uint32_t tid = threadIdx.x, lane = tid & 31u, wid = tid >> 5, nw = blockDim.x >> 5;
   if (tid == 0) {
     s_total = 0;
     s_carry = 0;
+    s_ccarry = 0;
   }
   __syncthreads();
-  unsigned long long local = 0;
-  for (uint32_t b = tid; b < n; b += blockDim.x) {
+  auto units_of = [&](uint32_t b) -> uint32_t {
     const uint32_t s = seq_ids ? seq_ids[b] : b;
-    local += s < n_seqs ? lens[s] : 0u;
-  }
+    const uint32_t len = s < n_seqs ? lens[s] : 0u;
+    return (uint32_t)ceil_div_u64(len, align);
+  };
+  unsigned long long local = 0;
+  for (uint32_t b = tid; b < n; b += blockDim.x)
+    local += (unsigned long long)PLAN_UNIT * units_of(b) + PLAN_ITEM;
   atomicAdd(&s_total, local);
   __syncthreads();
-  const unsigned long long total = s_total;
-  unsigned long long c = (total + target_items - 1) / (target_items ? target_items : 1);
-  c = (c + align - 1) / align * align;
-  if (c < align) c = align;
-  if (c > 0x40000000ull) c = 0x40000000ull;
-  const uint32_t C = (uint32_t)c;
+  const unsigned long long T = s_total;
+  // ranges at least PLAN_UNIT apart, so two cuts never land in one unit
+  unsigned long long g = T / PLAN_UNIT;
+  if (g > max_ranges) g = max_ranges;
+  if (g < 1) g = 1;
+  const uint32_t G = (uint32_t)g;
   for (uint32_t base = 0; base < n; base += blockDim.x) {
     const uint32_t b = base + tid;
-    uint32_t len = 0, cnt = 0;
-    if (b < n) {
-      const uint32_t s = seq_ids ? seq_ids[b] : b;
-      len = s < n_seqs ? lens[s] : 0u;
-      cnt = len ? (len + C - 1) / C : 1u;
+    const bool valid = b < n;
+    const uint32_t U = valid ? units_of(b) : 0u;
+    const unsigned long long cost = valid ? (unsigned long long)PLAN_UNIT * U + PLAN_ITEM : 0ull;
+    // block-wide exclusive scan of the cost
+    unsigned long long xc = cost;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const unsigned long long y = __shfl_up_sync(0xffffffffu, xc, o);
+      if (lane >= (uint32_t)o) xc += y;
     }
-    // block-wide exclusive scan of cnt
+    if (lane == 31) s_wcost[wid] = xc;
+    __syncthreads();
+    if (wid == 0) {
+      unsigned long long w = lane < nw ? s_wcost[lane] : 0ull;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const unsigned long long y = __shfl_up_sync(0xffffffffu, w, o);
+        if (lane >= (uint32_t)o) w += y;
+      }
+      s_wcost[lane] = w;
+    }
+    __syncthreads();
+    const unsigned long long S = s_ccarry + (wid ? s_wcost[wid - 1] : 0ull) + xc - cost;
+    const unsigned long long E = S + cost;
+    // cuts c with S <= P_c < E (only cuts 1 .. G-1 can split anything)
+    uint32_t c_lo = 1, c_hi = 1;
+    if (valid && T) {
+      c_lo = (uint32_t)max(1ull, ceil_div_u64(S * G, T));
+      c_hi = (uint32_t)min((unsigned long long)G, ceil_div_u64(E * G, T));
+    }
+    // the unit a cut splits at, or 0 when it does not split (cut in the item
+    // cost or in the last unit)
+    auto split_unit = [&](uint32_t c) -> uint32_t {
+      const unsigned long long Pc = (unsigned long long)c * T / G;
+      if (Pc <= S + PLAN_ITEM) return 0u;
+      const unsigned long long u = ceil_div_u64(Pc - S - PLAN_ITEM, PLAN_UNIT);
+      return u < U ? (uint32_t)u : 0u;
+    };
+    uint32_t cnt = valid ? 1u : 0u;
+    for (uint32_t c = c_lo; c < c_hi; ++c) cnt += split_unit(c) ? 1u : 0u;
+    // block-wide exclusive scan of the item counts
     uint32_t x = cnt;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -120,7 +180,7 @@ __global__ void __launch_bounds__(1024) k_plan(uint32_t n, const uint32_t* __res
     if (lane == 31) s_warp[wid] = x;
     __syncthreads();
     if (wid == 0) {
-      uint32_t w = lane < (blockDim.x >> 5) ? s_warp[lane] : 0u;
+      uint32_t w = lane < nw ? s_warp[lane] : 0u;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
         const uint32_t y = __shfl_up_sync(0xffffffffu, w, o);
@@ -129,30 +189,47 @@ __global__ void __launch_bounds__(1024) k_plan(uint32_t n, const uint32_t* __res
       s_warp[lane] = w;  // inclusive per-warp totals
     }
     __syncthreads();
-    const uint32_t warp_prefix = wid ? s_warp[wid - 1] : 0u;
-    const uint32_t first = s_carry + warp_prefix + x - cnt;
-    if (b < n) {
+    const uint32_t first = s_carry + (wid ? s_warp[wid - 1] : 0u) + x - cnt;
+    if (valid) {
       seq_first[b] = first;
       seq_count[b] = cnt;
-      for (uint32_t k = 0; k < cnt; ++k) {
-        if (first + k >= max_items) break;
-        kvcu_item it;
-        it.b = b;
-        it.start = k * C;
-        // The last item is open-ended: decode clips it to the live length, so
-        // a plan stays valid while appends grow the sequences.
-        it.end = (k + 1 == cnt) ? 0xFFFFFFFFu : min(len, (k + 1) * C);
-        it.pad = 0;
-        items[first + k] = it;
+      // item k covers units [u_k, u_{k+1}); u_0 = 0, the last one is open
+      uint32_t k = 0, u_start = 0;
+      for (uint32_t c = c_lo; c <= c_hi; ++c) {
+        const uint32_t u = c < c_hi ? split_unit(c) : 0u;
+        if (c < c_hi) {
+          // range c starts after the entry's items that begin before the cut;
+          // the first item counts as beginning after its item cost, so a cut
+          // that lands in that cost hands the whole first item to range c
+          const unsigned long long Pc = (unsigned long long)c * T / G;
+          ranges[c] = first + (Pc > S + PLAN_ITEM ? 1u : 0u) + k;
+        }
+        if (c < c_hi && !u) continue;
+        if (first + k < max_items) {
+          kvcu_item it;
+          it.b = b;
+          it.start = u_start * align;
+          it.end = (c == c_hi) ? 0xFFFFFFFFu : u * align;
+          it.pad = 0;
+          items[first + k] = it;
+        }
+        ++k;
+        u_start = u;
       }
     }
     __syncthreads();
-    if (tid == 0) s_carry += s_warp[(blockDim.x >> 5) - 1];
+    if (tid == 0) {
+      s_carry += s_warp[nw - 1];
+      s_ccarry += s_wcost[nw - 1];
+    }
     __syncthreads();
   }
   if (tid == 0) {
-    meta[0] = min(s_carry, max_items);
-    meta[1] = C;
+    const uint32_t n_items = min(s_carry, max_items);
+    meta[0] = n_items;
+    meta[1] = G;
+    ranges[0] = 0;
+    ranges[G] = n_items;
   }
 }
 
@@ -189,10 +266,13 @@ __global__ void __launch_bounds__(NT, 1) k_decode(DecodeArgs a) {
   constexpr int HH = NH / 2;             // heads per PV thread group
   const uint32_t c4 = tid & 127u;        // PV: output columns 4*c4 .. +3
   const uint32_t hg = tid >> 7;          // PV: head group
-  const uint32_t n_items = a.meta[0];
+  const uint32_t n_items = a.meta[0], n_ranges = a.meta[1];
   const uint32_t H = a.n_heads;
+  if (blockIdx.x == 0 && tid == 0 && n_ranges > gridDim.x) atomicOr(a.status, KVCU_STATUS_BAD_PLAN);
+  const uint32_t it0 = blockIdx.x < n_ranges ? min(a.ranges[blockIdx.x], n_items) : n_items;
+  const uint32_t it1 = blockIdx.x < n_ranges ? min(a.ranges[blockIdx.x + 1], n_items) : n_items;
 
-  for (uint32_t it = blockIdx.x; it < n_items; it += gridDim.x) {
+  for (uint32_t it = it0; it < it1; ++it) {
     const kvcu_item item = a.items[it];
     const uint32_t b = item.b;
     const uint32_t s = a.seq_ids ? a.seq_ids[b] : b;
@@ -426,7 +506,7 @@ int launch_decode_t(kvcu_decode_ws* ws, const DecodeArgs& a, cudaStream_t st) {
     if (rc) return rc;
     configured = true;
   }
-  k_decode<QUANT, NH><<<ws->num_sms, NT, smem, st>>>(a);
+  k_decode<QUANT, NH><<<ws->decode_ctas, NT, smem, st>>>(a);
   return kvcu_check_cuda(cudaGetLastError(), "decode kernel launch");
 }
 
@@ -453,22 +533,21 @@ int kvcu_decode_setup(kvcu_decode_ws* ws) {
 
 int kvcu_launch_plan(kvcu_decode_ws* ws, const kvcu_pool* p, uint32_t n, const uint32_t* seq_ids,
                      uint32_t n_seqs, const uint32_t* lens, cudaStream_t st) {
-  const uint32_t target = (uint32_t)ws->decode_ctas * TARGET_WAVES;
-  const uint32_t align = p->block_size > 128u ? p->block_size : 128u;
-  k_plan<<<1, 1024, 0, st>>>(n, seq_ids, n_seqs, lens, target, align, ws->max_items, ws->items,
-                             ws->meta, ws->seq_first, ws->seq_count);
-  return kvcu_check_cuda(cudaGetLastError(), "plan kernel launch");
+  return kvcu_launch_plan_target(ws, p, n, seq_ids, n_seqs, lens, (uint32_t)ws->decode_ctas, st);
 }
 
-// The same plan with an explicit item target, for a workspace that holds fewer
-// items than the default (items <= n + target, so ws->max_items >= n + target + 1
-// keeps every item).
+// The plan with at most `ranges` CTA ranges. It makes at most n + ranges - 1
+// items, so ws->max_items >= n + ranges keeps every item; the decode grid
+// (ws->decode_ctas) must be >= ranges.
 int kvcu_launch_plan_target(kvcu_decode_ws* ws, const kvcu_pool* p, uint32_t n,
                             const uint32_t* seq_ids, uint32_t n_seqs, const uint32_t* lens,
-                            uint32_t target, cudaStream_t st) {
+                            uint32_t ranges, cudaStream_t st) {
   const uint32_t align = p->block_size > 128u ? p->block_size : 128u;
-  k_plan<<<1, 1024, 0, st>>>(n, seq_ids, n_seqs, lens, target, align, ws->max_items, ws->items,
-                             ws->meta, ws->seq_first, ws->seq_count);
+  if (ranges > ws->max_ranges) ranges = ws->max_ranges;
+  if (ranges > (uint32_t)ws->decode_ctas) ranges = (uint32_t)ws->decode_ctas;
+  if (ranges < 1) ranges = 1;
+  k_plan<<<1, 1024, 0, st>>>(n, seq_ids, n_seqs, lens, ranges, align, ws->max_items, ws->items,
+                             ws->meta, ws->ranges, ws->seq_first, ws->seq_count);
   return kvcu_check_cuda(cudaGetLastError(), "plan kernel launch");
 }
 
@@ -536,6 +615,7 @@ int kvcu_launch_decode(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint32_
   a.out = out;
   a.items = ws->items;
   a.meta = ws->meta;
+  a.ranges = ws->ranges;
   a.seq_count = ws->seq_count;
   a.part_o = ws->part_o;
   a.part_ml = ws->part_ml;

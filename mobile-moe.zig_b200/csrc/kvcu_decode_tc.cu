@@ -111,6 +111,7 @@ struct TcArgs {
   float* out;
   const kvcu_item* items;
   const uint32_t* meta;
+  const uint32_t* ranges;
   const uint32_t* seq_count;
   float* part_o;
   float* part_ml;
@@ -429,7 +430,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
   auto bar = [&](int i) { return sbase + OFF_MISC + 8u * (uint32_t)i; };
   volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + OFF_ABORT);
-  const uint32_t n_items = a.meta[0];
+  // this CTA's range of work items (the plan cuts the batch into equal-cost
+  // ranges, one per CTA)
+  const uint32_t n_items = a.meta[0], n_ranges = a.meta[1];
+  const uint32_t it_begin = blockIdx.x < n_ranges ? min(a.ranges[blockIdx.x], n_items) : n_items;
+  const uint32_t it_end = blockIdx.x < n_ranges ? min(a.ranges[blockIdx.x + 1], n_items) : n_items;
+  if (blockIdx.x == 0 && threadIdx.x == 0 && n_ranges > gridDim.x) atomicOr(a.status, KVCU_STATUS_BAD_PLAN);
   const uint32_t H = a.n_heads;
 
   // ---- set-up: barriers, constant operands, TMEM
@@ -492,7 +498,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     if (lane == 0) {
       uint32_t g = 0;
       const uint32_t br = a.box_rows;
-      for (uint32_t it = blockIdx.x; it < n_items && !*abort_flag; it += gridDim.x) {
+      for (uint32_t it = it_begin; it < it_end && !*abort_flag; ++it) {
         const Item im = load_item(a, it);
         for (uint32_t k = 0; k < im.ntiles && !*abort_flag; ++k, ++g) {
           const uint32_t s = g & 1u;
@@ -536,7 +542,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     // issues each MMA / commit.  One wait per pair of Q8_0 blocks.
     uint32_t g = 0, item_no = 0;
     bool ok = true;
-    for (uint32_t it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+    for (uint32_t it = it_begin; it < it_end && ok; ++it) {
       const Item im = load_item(a, it);
       if (im.ntiles == 0) continue;
       if (!mbar_wait_warp(bar(B_Q_FULL), item_no & 1u, abort_flag, a.status)) break;
@@ -591,7 +597,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     uint32_t g = 0, item_ord = 0;
     bool ok = true;
     const uint64_t ones_desc = smem_desc(sbase + OFF_ONES, 0, 0, LAYOUT_NONE);
-    for (uint32_t it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+    for (uint32_t it = it_begin; it < it_end && ok; ++it) {
       const Item im = load_item(a, it);
       if (im.ntiles == 0) continue;
       for (uint32_t k = 0; k < im.ntiles && ok; ++k, ++g) {
@@ -663,7 +669,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       ++esync;
       return r;
     };
-    for (uint32_t it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+    for (uint32_t it = it_begin; it < it_end && ok; ++it) {
       const Item im = load_item(a, it);
       const bool single = a.seq_count[im.b] == 1;
       if (im.ntiles == 0) {
@@ -934,7 +940,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const uint32_t j = tid >> 4;                     // 16-column group within the M-tile, 0..7
     uint32_t g = 0;
     bool ok = true;
-    for (uint32_t it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+    for (uint32_t it = it_begin; it < it_end && ok; ++it) {
       const Item im = load_item(a, it);
       for (uint32_t k = 0; k < im.ntiles && ok; ++k, ++g) {
         const uint32_t s = g & 1u;
@@ -1123,12 +1129,13 @@ int kvcu_launch_decode_tc(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint
   a.out = out;
   a.items = ws->items;
   a.meta = ws->meta;
+  a.ranges = ws->ranges;
   a.seq_count = ws->seq_count;
   a.part_o = ws->part_o;
   a.part_ml = ws->part_ml;
   a.ws_heads = ws->max_heads;
-  if (n_heads <= 8) return launch_tc<8>(ws->num_sms, lat, rope, a, st);
-  if (n_heads <= 16) return launch_tc<16>(ws->num_sms, lat, rope, a, st);
-  if (n_heads <= 20) return launch_tc<20>(ws->num_sms, lat, rope, a, st);
-  return launch_tc<24>(ws->num_sms, lat, rope, a, st);
+  if (n_heads <= 8) return launch_tc<8>(ws->decode_ctas, lat, rope, a, st);
+  if (n_heads <= 16) return launch_tc<16>(ws->decode_ctas, lat, rope, a, st);
+  if (n_heads <= 20) return launch_tc<20>(ws->decode_ctas, lat, rope, a, st);
+  return launch_tc<24>(ws->decode_ctas, lat, rope, a, st);
 }

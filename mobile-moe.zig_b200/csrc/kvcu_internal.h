@@ -30,9 +30,10 @@ struct kvcu_item {
 
 struct kvcu_decode_ws {
   int device;
-  uint32_t max_batch, max_heads, max_items;
+  uint32_t max_batch, max_heads, max_items, max_ranges;
   kvcu_item* items;          // [max_items]
-  uint32_t* meta;            // [0] n_items, [1] chunk tokens
+  uint32_t* meta;            // [0] n_items, [1] CTA ranges G
+  uint32_t* ranges;          // [max_ranges + 1] first item of each CTA range
   uint32_t* seq_first;       // [max_batch] first item of entry b
   uint32_t* seq_count;       // [max_batch] items of entry b
   float* part_o;             // [max_items][max_heads][512]

@@ -6,11 +6,12 @@
 // fixed array compiled into this translation unit, one per device, reserved
 // when the library's device code is loaded.  The call plans and decodes with
 // the same kernels as kvcu_decode_plan + kvcu_mla_decode; only where the
-// scratch lives, and the plan's item target (bounded by the array), differ.
+// scratch lives, and the plan's range count (bounded by the array), differ.
 //
 // Nothing in the scratch needs clearing between calls: the plan kernel writes
-// every field the decode reads (item list, item count, per-entry first item and
-// item count), and the decode writes every partial before the combine reads it.
+// every field the decode reads (item list, item count, CTA ranges, per-entry
+// first item and item count), and the decode writes every partial before the
+// combine reads it.
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -30,12 +31,13 @@ constexpr size_t kPartO = 0;                                                  //
 constexpr size_t kPartMl = align256(kPartO + (size_t)kMaxItems * kMaxHeads * 512 * 4);  // f32 [items][heads][2]
 constexpr size_t kItems = align256(kPartMl + (size_t)kMaxItems * kMaxHeads * 2 * 4);   // kvcu_item [items]
 constexpr size_t kMeta = align256(kItems + (size_t)kMaxItems * sizeof(kvcu_item));     // u32 [4]
-constexpr size_t kSeqFirst = align256(kMeta + 4 * 4);                                 // u32 [batch]
+constexpr size_t kRanges = align256(kMeta + 4 * 4);                                   // u32 [items + 1]
+constexpr size_t kSeqFirst = align256(kRanges + ((size_t)kMaxItems + 1) * 4);         // u32 [batch]
 constexpr size_t kSeqCount = align256(kSeqFirst + (size_t)kMaxBatch * 4);            // u32 [batch]
 constexpr size_t kScratchBytes = align256(kSeqCount + (size_t)kMaxBatch * 4);
 static_assert(sizeof(kvcu_item) == 16, "item layout");
 static_assert(kScratchBytes >= (size_t)KVCU_NOALLOC_SCRATCH_BYTES &&
-                  kScratchBytes <= (size_t)KVCU_NOALLOC_SCRATCH_BYTES + 6 * 256,
+                  kScratchBytes <= (size_t)KVCU_NOALLOC_SCRATCH_BYTES + 7 * 256,
               "the header's stated scratch size");
 
 }  // namespace
@@ -106,8 +108,10 @@ extern "C" int kvcu_mla_decode_noalloc(kvcu_pool* p, uint32_t layer, uint32_t n,
     ws.max_batch = kMaxBatch;
     ws.max_heads = kMaxHeads;
     ws.max_items = kMaxItems;
+    ws.max_ranges = kMaxItems;
     ws.items = reinterpret_cast<kvcu_item*>(base + kItems);
     ws.meta = reinterpret_cast<uint32_t*>(base + kMeta);
+    ws.ranges = reinterpret_cast<uint32_t*>(base + kRanges);
     ws.seq_first = reinterpret_cast<uint32_t*>(base + kSeqFirst);
     ws.seq_count = reinterpret_cast<uint32_t*>(base + kSeqCount);
     ws.part_o = reinterpret_cast<float*>(base + kPartO);
@@ -115,11 +119,11 @@ extern "C" int kvcu_mla_decode_noalloc(kvcu_pool* p, uint32_t layer, uint32_t n,
     ws.impl = KVCU_DECODE_AUTO;
     rc = kvcu_decode_setup(&ws);
     if (!rc && n) {
-      // at most n + target items: keep them within the array
-      uint32_t target = (uint32_t)ws.decode_ctas * 4u;
-      if (target > kMaxItems - n - 1u) target = kMaxItems - n - 1u;
+      // at most n + ranges - 1 items: keep them within the array
+      uint32_t ranges = (uint32_t)ws.decode_ctas;
+      if (ranges > kMaxItems - n) ranges = kMaxItems - n;
       const cudaStream_t st = (cudaStream_t)stream;
-      rc = kvcu_launch_plan_target(&ws, p, n, seq_ids, n_seqs, lens, target, st);
+      rc = kvcu_launch_plan_target(&ws, p, n, seq_ids, n_seqs, lens, ranges, st);
       if (!rc)
         rc = kvcu_launch_decode(&ws, p, layer, n, seq_ids, n_seqs, table_offsets, tables, lens, q,
                                 n_heads, scale, out, st);

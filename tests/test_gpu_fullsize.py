@@ -5,8 +5,8 @@ properties that do not depend on the size:
 - decode of a sample of sequences (the shortest, median ones and the longest,
   which the plan splits across many work items) against the oracle, <= 1e-3;
 - permutation invariance: decoding the batch in another order permutes the
-  outputs bit for bit (each sequence's work items depend only on its length
-  and the batch total);
+  outputs (<= 1e-3: the plan cuts the batch into per-CTA ranges in batch
+  order, so a sequence may be split at other points);
 - a sequence decoded alone matches its row of the full batch (<= 1e-3: the
   split points differ, so partial sums are combined in another order).
 """
@@ -90,7 +90,8 @@ def test_fullsize_permutation_invariance(full):
     cache.mlaDecode_dev(0, perm, q[torch.from_numpy(perm.astype(np.int64)).cuda()], SCALE, out_p)
     torch.cuda.synchronize()
     assert cache.pool().status() == 0
-    assert torch.equal(out_p, out[torch.from_numpy(perm.astype(np.int64)).cuda()])
+    want = out[torch.from_numpy(perm.astype(np.int64)).cuda()]
+    assert rel_err_rows(out_p.cpu().numpy(), want.cpu().numpy()) <= REL_TOL
 
 
 def test_fullsize_single_sequence_matches_batch_row(full):

@@ -429,14 +429,17 @@ def test_decode_device_api_plan_reuse_with_growth(kv, oracle, torch_mod):
 
 def test_decode_split_matches_unsplit(kv, oracle):
     """A long sequence decoded alone (split across CTAs) equals the same sequence
-    decoded inside a batch of short ones (different split) to 1e-5."""
+    decoded inside a batch of short ones (different split) to 2e-4: the
+    tensor-core kernel rounds P to f16 against each item's running maximum, so
+    other split points round other values (each side is within 1e-3 of the
+    oracle)."""
     lens = [20000, 3, 3, 3]
     c = _decode_case(kv, oracle, lens, 64, True, 20, 21)
     q = np.random.default_rng(22).standard_normal((1, 20, W)).astype(np.float32)
     a = c.mlaDecode(0, q, np.array([0], np.uint32), SCALE)
     qq = np.concatenate([q, q, q], axis=0)
     b = c.mlaDecode(0, qq, np.array([1, 0, 2], np.uint32), SCALE)
-    assert rel_err_rows(b[1:2], a) <= 1e-5
+    assert rel_err_rows(b[1:2], a) <= 2e-4
 
 
 # ------------------------------------------------------------------ checkpoint v2
