@@ -63,8 +63,6 @@ constexpr uint32_t VU_BYTES = 4096;  // one V unit: 16 tokens x 128 columns (one
 constexpr uint32_t VCH_BYTES = 4 * VU_BYTES;  // one V chunk: 16 tokens x 512 columns
 constexpr int NTHREADS = 512;        // 4 warpgroups: issue, epilogue x2, converter
 constexpr int EPI_WARPS = 8;
-constexpr uint32_t MAGIC_I = 0x4B400000u;    // float 12582912 = 1.5 * 2^23
-constexpr float MAGIC_F = 12582912.0f;
 constexpr float RESCALE_LOG2 = 8.0f;         // lazy rescale threshold (factor 256)
 constexpr uint32_t STATUS_TIMEOUT = KVCU_STATUS_TIMEOUT;
 
@@ -347,25 +345,6 @@ __device__ __forceinline__ void tmem_st(uint32_t ta, const uint32_t* r) {
     tst1(ta, r);
   }
 }
-// N columns of the conversion bias
-template <int N>
-__device__ __forceinline__ void tmem_st_magic(uint32_t ta) {
-  uint32_t m[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) m[i] = MAGIC_I;
-  if constexpr (N >= 8) {
-    tst8(ta, m);
-    tmem_st_magic<N - 8>(ta + 8);
-  } else if constexpr (N >= 4) {
-    tst4(ta, m);
-    tmem_st_magic<N - 4>(ta + 4);
-  } else if constexpr (N >= 2) {
-    tst2(ta, m);
-    tmem_st_magic<N - 2>(ta + 2);
-  } else if constexpr (N == 1) {
-    tst1(ta, m);
-  }
-}
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -479,16 +458,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + OFF_TMEM_BASE);
 
-  if (warp >= 4 && warp < 8) {
-    // pre-load every QK slot with the conversion bias (one warp per lane quarter)
-    const uint32_t ta = tmem + ((32u * (warp & 3u)) << 16);
-    for (int c = 0; c < QK_GROUPS * GB * NQ; c += 8) tmem_st_magic<8>(ta + (uint32_t)c);
-    tmem_wait_st();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-
   // Register split by warpgroup (set once, with each warpgroup converged): the
   // issue and converter warpgroups hand registers to the two epilogue ones.
   if (warp < 4) {
@@ -575,7 +544,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 ad = smem_desc(stage + ST_ROPE + (b - 16u) * 32u, 16, 512, LAYOUT_SW64);
                 bd = smem_desc(sbase + OFF_QD_ROPE + (b - 16u) * 32u, 16, 512, LAYOUT_SW64);
               }
-              mma_i8(tmem + (GB * slot + e) * NQ, ad, bd, idesc_qk(NQ), 1u);
+              mma_i8(tmem + (GB * slot + e) * NQ, ad, bd, idesc_qk(NQ), 0u);  // fresh int32 dots
             }
             mma_commit(bar(B_QK_FULL + slot));
           }
@@ -769,25 +738,21 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           reg_fence(r0);
           reg_fence(r1);
           reg_fence(r2);
-          // re-bias the group for its next use while the values are combined
-          tmem_st_magic<2 * HH>(ta);
-          tmem_st_magic<2 * HH>(ta + NQ);
-          tmem_st_magic<2 * HH>(ta + 2 * NQ);
           const float d0 = __half2float(__ushort_as_half(scrow[GB * gi]));
           const float d1 = __half2float(__ushort_as_half(scrow[GB * gi + 1]));
           const float d2 = __half2float(__ushort_as_half(scrow[GB * gi + 2]));
 #pragma unroll
           for (int h = 0; h < HH; ++h) {
-            // exact int32 -> f32 through the bias (|dot| < 2^22), then 256 x0 + x1
+            // 256 x0 + x1 exactly in int32 (|x0| <= 32 * 127^2 < 2^19), one
+            // rounding to f32, then the block scale
             const int c0 = 4 * (h >> 1) + (h & 1), c1 = c0 + 2;
-            const float x00 = __uint_as_float(r0[c0]) - MAGIC_F, x01 = __uint_as_float(r0[c1]) - MAGIC_F;
-            const float x10 = __uint_as_float(r1[c0]) - MAGIC_F, x11 = __uint_as_float(r1[c1]) - MAGIC_F;
-            const float x20 = __uint_as_float(r2[c0]) - MAGIC_F, x21 = __uint_as_float(r2[c1]) - MAGIC_F;
-            acc[h] = fmaf(d0, fmaf(x00, 256.f, x01), acc[h]);
-            acc[h] = fmaf(d1, fmaf(x10, 256.f, x11), acc[h]);
-            acc[h] = fmaf(d2, fmaf(x20, 256.f, x21), acc[h]);
+            const int v0 = (int)r0[c0] * 256 + (int)r0[c1];
+            const int v1 = (int)r1[c0] * 256 + (int)r1[c1];
+            const int v2 = (int)r2[c0] * 256 + (int)r2[c1];
+            acc[h] = fmaf(d0, __int2float_rn(v0), acc[h]);
+            acc[h] = fmaf(d1, __int2float_rn(v1), acc[h]);
+            acc[h] = fmaf(d2, __int2float_rn(v2), acc[h]);
           }
-          tmem_wait_st();
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(bar(B_QK_EMPTY + slot));
