@@ -392,6 +392,7 @@ def run_ours(args, rank, world, local_rank):
         e2e_tokens += int((lens0 + base + k + 1).sum()) * NL
     torch.cuda.synchronize()
     e2e_time = time.perf_counter() - t0
+    e2e_mapped = cache.last_decode_mapped
     e_tok, e_time = aggregate_throughput(e2e_tokens, e2e_time, dist if world > 1 else None, dev)
     e2e_value = e_tok / e_time if e_time > 0 else None
     h2d = NL * n * (W * 4 + 8 + H * W * 4)
@@ -425,7 +426,9 @@ def run_ours(args, rank, world, local_rank):
                        "parallelism": f"sequence-sharded x{world} (LPT by tokens), no collective",
                        "shard_tokens": loads, "l2": "inputs larger than L2 (>=0.4 GB of KV per layer per GPU)"},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h},
+                    "d2h_bytes_per_step": d2h,
+                    "host_buffers": ("pinned; q read and out written over PCIe by the kernels"
+                                     if e2e_mapped else "copied in and out around the kernels")},
             "roofline": {"kernel": "mla_decode layer call (k_decode_tc + k_combine; 99.3% k_decode_tc)",
                          "bound": "hbm", "achieved": dec_gbs, "peak": peak, "unit": "GB/s",
                          "frac": dec_gbs / peak, "peak_source": peak_kind,

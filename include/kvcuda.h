@@ -309,9 +309,17 @@ int kvcache_append_batch_dev(kvcache* c, uint32_t layer, uint32_t n, const uint3
 /* gather(layer, seq): out[len][kv_rank + rope_dim] (HOST buffer). */
 int kvcache_gather(kvcache* c, uint32_t layer, uint32_t seq, float* out);
 /* mlaDecode (the call replacing src/inference.zig:518-660): HOST q
- * [n][n_heads][R+P] and out [n][n_heads][R]; copies in and out inside. */
+ * [n][n_heads][R+P] and out [n][n_heads][R]; returns when out is complete.
+ * Pageable buffers are copied in and out around the kernels.  When both are
+ * pinned and mapped (cudaHostAlloc / cudaHostRegister) and their allocations
+ * hold the whole arrays, the kernels read q and write out in host memory
+ * directly, so the transfers overlap the decode instead of preceding and
+ * following it. */
 int kvcache_mla_decode(kvcache* c, uint32_t layer, uint32_t n, const uint32_t* seq_ids,
                        const float* q, uint32_t n_heads, float scale, float* out);
+/* 1 when the last kvcache_mla_decode used its buffers in place (pinned,
+ * mapped), 0 when it copied. */
+int kvcache_last_decode_mapped(const kvcache* c);
 /* Device variant: q/out device pointers, no host copies; plans once per step
  * (a plan is reused until a sequence length or the batch changes). */
 int kvcache_mla_decode_dev(kvcache* c, uint32_t layer, uint32_t n, const uint32_t* seq_ids,

@@ -13,6 +13,7 @@
 // Deviations from the reference (also listed in kvcuda.h): Q8_0 pools start
 // zeroed; loadFromFile bounds-checks block ids and takes them off the free
 // list; reusePrefixBlocks retains before it releases.
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <fcntl.h>
 #include <stdio.h>
@@ -141,6 +142,37 @@ int ensure_dev(T** ptr, size_t* cap, size_t n) {
   return KVCU_OK;
 }
 
+// The device address of host buffer [p, p + bytes) when it is pinned, mapped
+// into the device's address space and its allocation covers all `bytes`; null
+// otherwise (pageable memory, an unmapped or shorter allocation, or a failed
+// query), and the caller copies instead.
+typedef CUresult (*PointerAttrFn)(void*, CUpointer_attribute, CUdeviceptr);
+void* mapped_host_range(const void* p, size_t bytes) {
+  static PointerAttrFn attr_fn = []() -> PointerAttrFn {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuPointerGetAttribute", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    return reinterpret_cast<PointerAttrFn>(f);
+  }();
+  if (!attr_fn || !p || !bytes) return nullptr;
+  cudaPointerAttributes at;
+  if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+    cudaGetLastError();  // a failed query leaves a (non-sticky) error behind: clear it
+    return nullptr;
+  }
+  if (at.type != cudaMemoryTypeHost || !at.devicePointer) return nullptr;
+  const CUdeviceptr dp = reinterpret_cast<CUdeviceptr>(at.devicePointer);
+  CUdeviceptr start = 0;
+  size_t size = 0;
+  if (attr_fn(&start, CU_POINTER_ATTRIBUTE_RANGE_START_ADDR, dp) != CUDA_SUCCESS ||
+      attr_fn(&size, CU_POINTER_ATTRIBUTE_RANGE_SIZE, dp) != CUDA_SUCCESS)
+    return nullptr;
+  if (dp < start || bytes > size || dp - start > size - bytes) return nullptr;
+  return at.devicePointer;
+}
+
 }  // namespace
 
 struct kvcache {
@@ -179,6 +211,7 @@ struct kvcache {
   uint64_t plan_tokens = 0;
   uint32_t last_launches = 0;
   int decode_impl = KVCU_DECODE_AUTO;
+  int last_mapped = 0;  // the last host-buffer decode read q / wrote out in place (pinned, mapped)
 
   bool quantized() const { return pool && pool->quantized; }
   uint32_t row_width() const { return kv_rank + rope_dim; }
@@ -762,6 +795,17 @@ int kvcache_mla_decode(kvcache* c, uint32_t layer, uint32_t n, const uint32_t* s
   if (!n) return KVCU_OK;
   DevScope d(c->device);
   const size_t qn = (size_t)n * n_heads * c->row_width(), on = (size_t)n * n_heads * c->kv_rank;
+  // Pinned, mapped host buffers that hold the whole q / out: the kernels read
+  // q and write out over the bus themselves, overlapped with the decode.
+  const void* q_map = mapped_host_range(q, qn * 4);
+  void* out_map = q_map ? mapped_host_range(out, on * 4) : nullptr;
+  c->last_mapped = (q_map && out_map) ? 1 : 0;
+  if (c->last_mapped) {
+    int rc = decode_impl(c, layer, n, seq_ids, static_cast<const float*>(q_map), n_heads, scale,
+                         static_cast<float*>(out_map), c->stream);
+    if (rc) return rc;
+    return check_status(c);  // synchronises: out is complete in host memory
+  }
   int rc = ensure_dev(&c->d_f, &c->d_f_cap, qn);
   if (!rc) rc = ensure_dev(&c->d_f2, &c->d_f2_cap, on);
   if (rc) return rc;
@@ -782,6 +826,8 @@ int kvcache_mla_decode_dev(kvcache* c, uint32_t layer, uint32_t n, const uint32_
 }
 
 uint32_t kvcache_last_launches(const kvcache* c) { return c ? c->last_launches : 0; }
+
+int kvcache_last_decode_mapped(const kvcache* c) { return c ? c->last_mapped : 0; }
 
 int kvcache_set_decode_impl(kvcache* c, int impl) {
   if (!c || impl < KVCU_DECODE_AUTO || impl > KVCU_DECODE_TENSOR_CORE) return KVCU_ERR_INVALID_ARG;

@@ -117,6 +117,7 @@ _SIGS = {
     "kvcache_mla_decode": (_i32, [_vp, _u32, _u32, _vp, _vp, _u32, _f32, _vp]),
     "kvcache_mla_decode_dev": (_i32, [_vp, _u32, _u32, _vp, _vp, _u32, _f32, _vp, _vp]),
     "kvcache_last_launches": (_u32, [_vp]),
+    "kvcache_last_decode_mapped": (_i32, [_vp]),
     "kvcache_set_decode_impl": (_i32, [_vp, _i32]),
     "kvcache_last_decode_impl": (_i32, [_vp]),
     "kvcache_save_to_file_v2": (_i32, [_vp, _cp]),
@@ -565,6 +566,11 @@ class KVCache:
     @property
     def last_launches(self):
         return lib().kvcache_last_launches(self._h)
+
+    @property
+    def last_decode_mapped(self):
+        """True when the last host-buffer decode used pinned, mapped q / out in place."""
+        return bool(lib().kvcache_last_decode_mapped(self._h))
 
     def set_decode_impl(self, impl):
         check(lib().kvcache_set_decode_impl(self._h, impl), "set_decode_impl")

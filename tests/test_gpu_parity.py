@@ -427,6 +427,45 @@ def test_decode_device_api_plan_reuse_with_growth(kv, oracle, torch_mod):
     assert [c.seq_len(s) for s in range(len(lens))] == cur
 
 
+def test_decode_host_api_pinned_buffers_in_place(kv, oracle, torch_mod):
+    """Pinned, mapped q / out are read and written in place by the kernels; the
+    outputs equal the copy path's and the device API's bit for bit, and match
+    the oracle."""
+    torch = torch_mod
+    lens = [1, 300, 2500, 70, 9000]
+    bs, H = 64, 20
+    nb = sum((L + bs - 1) // bs for L in lens) + 2
+    c, o, _ = _multi_seq_cache(kv, oracle, lens, bs, nb, 41, True, 0.01)
+    ids = np.arange(len(lens), dtype=np.uint32)
+    q = np.random.default_rng(41).standard_normal((len(lens), H, W)).astype(np.float32)
+    # pageable: copied
+    out_copy = c.mlaDecode(0, q, ids, SCALE)
+    assert not c.last_decode_mapped
+    # pinned q and out: used in place
+    q_pin = torch.from_numpy(q).pin_memory()
+    out_pin = torch.full((len(lens), H, R), float("nan")).pin_memory()
+    c.mlaDecode_ptr(0, len(lens), ids, q_pin.data_ptr(), H, SCALE, out_pin.data_ptr())
+    assert c.last_decode_mapped
+    # pinned q, pageable out: copied
+    out_mixed = np.full((len(lens), H, R), np.nan, np.float32)
+    c.mlaDecode_ptr(0, len(lens), ids, q_pin.data_ptr(), H, SCALE, out_mixed.ctypes.data)
+    assert not c.last_decode_mapped
+    out_dev = torch.empty((len(lens), H, R), device="cuda")
+    c.mlaDecode_dev(0, ids, torch.from_numpy(q).cuda(), SCALE, out_dev)
+    torch.cuda.synchronize()
+    assert np.array_equal(out_pin.numpy(), out_copy)
+    assert np.array_equal(out_mixed, out_copy)
+    assert np.array_equal(out_dev.cpu().numpy(), out_copy)
+    offs = [0]
+    tabs = []
+    for s in range(len(lens)):
+        tabs.extend(c.seq_block_table(s))
+        offs.append(len(tabs))
+    want = o.attention_batch(0, np.array(offs, np.uint32), np.array(tabs, np.uint32),
+                             np.array(lens, np.uint32), q, SCALE, n_threads=8)
+    assert rel_err_rows(out_copy, want) <= REL_TOL
+
+
 def test_decode_split_matches_unsplit(kv, oracle):
     """A long sequence decoded alone (split across CTAs) equals the same sequence
     decoded inside a batch of short ones (different split) to 2e-4: the
