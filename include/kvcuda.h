@@ -181,6 +181,34 @@ int kvcu_mla_decode(kvcu_decode_ws* ws, kvcu_pool* pool, uint32_t layer, uint32_
                     const uint32_t* seq_ids, uint32_t n_seqs, const uint32_t* table_offsets,
                     const uint32_t* tables, const uint32_t* lens, const float* q,
                     uint32_t n_heads, float scale, float* out, void* stream);
+/* kvcu_mla_decode that also writes lse[b][h] = log(sum_p exp(s_p)) of the
+ * scaled scores (natural log; -inf for an empty context), so that further
+ * positions can be merged into out (kvcu_mla_finish does this for the newest
+ * token of a step). */
+int kvcu_mla_decode_lse(kvcu_decode_ws* ws, kvcu_pool* pool, uint32_t layer, uint32_t n,
+                        const uint32_t* seq_ids, uint32_t n_seqs, const uint32_t* table_offsets,
+                        const uint32_t* tables, const uint32_t* lens, const float* q,
+                        uint32_t n_heads, float scale, float* out, float* lse, void* stream);
+/* The MLA decode step around the cache, in absorbed form (src/inference.zig:
+ * 492-513 and 518-660).  Step = kvcu_mla_prepare, kvcu_append(rows) at the
+ * positions, kvcu_mla_decode_lse over the history (lens = positions), then
+ * kvcu_mla_finish.  All pointers are device pointers; weights are row-major as
+ * the reference's matVecMul reads them (src/math.zig:79-99).
+ * prepare: q [n][H][qk_nope + P] (after q_b_proj), kv_a [n][R + P] (after
+ *   kv_a_proj), positions [n], norm_w [R] (kv_a_norm), k_b [H*qk_nope][R] ->
+ *   rows [n][R + P] = [RMSNorm(kv_a[0:R]) * norm_w, RoPE(kv_a[R:], pos)]
+ *   (src/math.zig:7-35, 197-240) and q_abs [n][H][R + P] =
+ *   [k_b_h^T q_nope_h, RoPE(q_rope_h, pos)].
+ * finish: merges the newest token (its unquantized latent rows[b][0:R] and its
+ *   k_pe as the cache stores it) into the history's out / lse (latent is the
+ *   decode's out, updated in place), then attn [n][H][v_dim] = v_b_h latent_h
+ *   with v_b [H*v_dim][R]. */
+int kvcu_mla_prepare(kvcu_pool* pool, uint32_t n, uint32_t n_heads, uint32_t qk_nope, const float* q,
+                     const float* kv_a, const uint32_t* positions, const float* norm_w, float eps,
+                     float rope_base, const float* k_b, float* q_abs, float* rows, void* stream);
+int kvcu_mla_finish(kvcu_pool* pool, uint32_t n, uint32_t n_heads, uint32_t v_dim, const float* q_abs,
+                    const float* rows, float* latent, const float* lse, float scale, const float* v_b,
+                    float* attn, void* stream);
 /* Kernel launches the last kvcu_mla_decode issued (for launch accounting). */
 uint32_t kvcu_decode_last_launches(const kvcu_decode_ws* ws);
 /* Decode kernel selection.  AUTO uses the tcgen05 tensor-core kernel for Q8_0
@@ -320,6 +348,19 @@ int kvcache_mla_decode(kvcache* c, uint32_t layer, uint32_t n, const uint32_t* s
 /* 1 when the last kvcache_mla_decode used its buffers in place (pinned,
  * mapped), 0 when it copied. */
 int kvcache_last_decode_mapped(const kvcache* c);
+/* One MLA decode step of layer `layer` for a batch of sequences (the batched
+ * form of src/inference.zig:492-660): each entry b appends its new token at
+ * positions[b] (host array; each sequence at most once) and attends over
+ * positions <= positions[b].  Device inputs as for kvcu_mla_prepare /
+ * kvcu_mla_finish (q [n][H][qk_nope + rope_dim], kv_a [n][kv_rank + rope_dim],
+ * norm_w [kv_rank], k_b [H*qk_nope][kv_rank], v_b [H*v_dim][kv_rank]); output
+ * attn [n][H][v_dim] (before o_proj).  scale = 1/sqrt(qk_nope + rope_dim) as
+ * in the reference.  Stream-ordered; the call returns before the kernels end. */
+int kvcache_mla_step_dev(kvcache* c, uint32_t layer, uint32_t n, const uint32_t* seq_ids,
+                         const uint32_t* positions, const float* q_dev, const float* kv_a_dev,
+                         const float* norm_w_dev, float eps, float rope_base, const float* k_b_dev,
+                         const float* v_b_dev, uint32_t n_heads, uint32_t qk_nope, uint32_t v_dim,
+                         float scale, float* attn_dev, void* stream);
 /* Device variant: q/out device pointers, no host copies; plans once per step
  * (a plan is reused until a sequence length or the batch changes). */
 int kvcache_mla_decode_dev(kvcache* c, uint32_t layer, uint32_t n, const uint32_t* seq_ids,

@@ -201,6 +201,11 @@ struct kvcache {
   size_t d_f2_cap = 0;
   uint32_t* d_u = nullptr;
   size_t d_u_cap = 0;
+  // scratch of the MLA step: q_abs, rows, latent, lse / seq ids, positions, history lengths
+  float* d_step = nullptr;
+  size_t d_step_cap = 0;
+  uint32_t* d_stepu = nullptr;
+  size_t d_stepu_cap = 0;
   // decode
   kvcu_decode_ws* ws = nullptr;
   uint32_t ws_batch = 0, ws_heads = 0;
@@ -555,6 +560,8 @@ void kvcache_deinit(kvcache* c) {
   cudaFree(c->d_f);
   cudaFree(c->d_f2);
   cudaFree(c->d_u);
+  cudaFree(c->d_step);
+  cudaFree(c->d_stepu);
   cudaFree(c->d_seq_ids);
   if (c->stream) cudaStreamDestroy(c->stream);
   delete c;
@@ -823,6 +830,71 @@ int kvcache_mla_decode_dev(kvcache* c, uint32_t layer, uint32_t n, const uint32_
   if (!n) return KVCU_OK;
   DevScope d(c->device);
   return decode_impl(c, layer, n, seq_ids, q_dev, n_heads, scale, out_dev, (cudaStream_t)stream);
+}
+
+int kvcache_mla_step_dev(kvcache* c, uint32_t layer, uint32_t n, const uint32_t* seq_ids,
+                         const uint32_t* positions, const float* q_dev, const float* kv_a_dev,
+                         const float* norm_w_dev, float eps, float rope_base, const float* k_b_dev,
+                         const float* v_b_dev, uint32_t n_heads, uint32_t qk_nope, uint32_t v_dim,
+                         float scale, float* attn_dev, void* stream) {
+  if (!c || (n && (!seq_ids || !positions || !q_dev || !kv_a_dev || !norm_w_dev || !k_b_dev ||
+                   !v_b_dev || !attn_dev)))
+    return KVCU_ERR_INVALID_ARG;
+  if (!n) return KVCU_OK;
+  DevScope d(c->device);
+  const cudaStream_t st = (cudaStream_t)stream;
+  int rc = validate_positions(c, layer, n, seq_ids, positions);
+  if (rc) return rc;
+  const uint32_t R = c->kv_rank, Wd = c->row_width(), n_seqs = (uint32_t)c->seqs.size();
+  // scratch: q_abs [n][H][W], rows [n][W], latent [n][H][R], lse [n][H]
+  const size_t q_abs_n = (size_t)n * n_heads * Wd, rows_n = (size_t)n * Wd, lat_n = (size_t)n * n_heads * R;
+  rc = ensure_dev(&c->d_step, &c->d_step_cap, q_abs_n + rows_n + lat_n + (size_t)n * n_heads);
+  if (!rc) rc = ensure_dev(&c->d_stepu, &c->d_stepu_cap, 2 * (size_t)n + n_seqs);
+  if (!rc) rc = sync_tables(c);
+  if (!rc) rc = sync_lens(c);
+  if (!rc) rc = ensure_ws(c, n, n_heads);
+  if (rc) return rc;
+  float* q_abs = c->d_step;
+  float* rows = q_abs + q_abs_n;
+  float* latent = rows + rows_n;
+  float* lse = latent + lat_n;
+  uint32_t* d_ids = c->d_stepu;
+  uint32_t* d_pos = d_ids + n;
+  uint32_t* d_hist = d_pos + n;
+  // the decode covers each entry's history, positions < pos (the newest token
+  // is merged by kvcu_mla_finish as the reference treats it)
+  std::vector<uint32_t> hist(n_seqs, 0);
+  std::vector<char> seen(n_seqs, 0);
+  for (uint32_t b = 0; b < n; ++b) {
+    if (seen[seq_ids[b]]) {
+      kvcu_set_error("kvcache_mla_step_dev: sequence %u appears twice in the batch", seq_ids[b]);
+      return KVCU_ERR_INVALID_ARG;
+    }
+    seen[seq_ids[b]] = 1;
+    hist[seq_ids[b]] = positions[b];
+  }
+  KVCU_CUDA(cudaMemcpyAsync(d_ids, seq_ids, (size_t)n * 4, cudaMemcpyHostToDevice, st));
+  KVCU_CUDA(cudaMemcpyAsync(d_pos, positions, (size_t)n * 4, cudaMemcpyHostToDevice, st));
+  KVCU_CUDA(cudaMemcpyAsync(d_hist, hist.data(), (size_t)n_seqs * 4, cudaMemcpyHostToDevice, st));
+  rc = kvcu_mla_prepare(c->pool, n, n_heads, qk_nope, q_dev, kv_a_dev, d_pos, norm_w_dev, eps, rope_base,
+                        k_b_dev, q_abs, rows, st);
+  if (!rc)
+    rc = kvcu_append(c->pool, layer, n, rows, Wd, rows + R, Wd, d_ids, d_pos, n_seqs, c->d_toff, c->d_tables,
+                     c->d_lens, st);
+  if (rc) return rc;
+  bump_lens(c, n, seq_ids, positions);  // the append kernel advanced d_lens identically
+  rc = kvcu_decode_plan(c->ws, c->pool, n, d_ids, n_seqs, d_hist, st);
+  c->plan_epoch = ~0ull;  // the cached decode plan no longer matches the workspace
+  if (!rc)
+    rc = kvcu_mla_decode_lse(c->ws, c->pool, layer, n, d_ids, n_seqs, c->d_toff, c->d_tables, d_hist, q_abs,
+                             n_heads, scale, latent, lse, st);
+  if (!rc) rc = kvcu_mla_finish(c->pool, n, n_heads, v_dim, q_abs, rows, latent, lse, scale, v_b_dev, attn_dev, st);
+  if (rc) return rc;
+  // rows, gemm (prepare) + append + plan + decode + merge, gemm (finish). The
+  // three host arrays above are pageable: each cudaMemcpyAsync returned only
+  // after staging them, so they may go out of scope now.
+  c->last_launches = 2 + 1 + 1 + kvcu_decode_last_launches(c->ws) + 2;
+  return KVCU_OK;
 }
 
 uint32_t kvcache_last_launches(const kvcache* c) { return c ? c->last_launches : 0; }

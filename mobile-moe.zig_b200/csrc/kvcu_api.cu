@@ -339,7 +339,24 @@ int kvcu_mla_decode(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint32_t n
   DeviceGuard g(p->device);
   if (g.rc) return g.rc;
   return kvcu_launch_decode(ws, p, layer, n, seq_ids, n_seqs, table_offsets, tables, lens, q,
-                            n_heads, scale, out, (cudaStream_t)stream);
+                            n_heads, scale, out, nullptr, (cudaStream_t)stream);
+}
+
+int kvcu_mla_decode_lse(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint32_t n,
+                        const uint32_t* seq_ids, uint32_t n_seqs, const uint32_t* table_offsets,
+                        const uint32_t* tables, const uint32_t* lens, const float* q,
+                        uint32_t n_heads, float scale, float* out, float* lse, void* stream) {
+  if (!ws || !valid_pool(p)) return KVCU_ERR_INVALID_ARG;
+  if (ws->device != p->device) return KVCU_ERR_INVALID_ARG;
+  if (layer >= p->n_layers) {
+    kvcu_set_error("kvcu_mla_decode_lse: layer %u >= n_layers %u", layer, p->n_layers);
+    return KVCU_ERR_LAYER_OOB;
+  }
+  if (n && (!table_offsets || !tables || !lens || !q || !out || !lse)) return KVCU_ERR_INVALID_ARG;
+  DeviceGuard g(p->device);
+  if (g.rc) return g.rc;
+  return kvcu_launch_decode(ws, p, layer, n, seq_ids, n_seqs, table_offsets, tables, lens, q,
+                            n_heads, scale, out, lse, (cudaStream_t)stream);
 }
 
 uint32_t kvcu_decode_last_launches(const kvcu_decode_ws* ws) { return ws ? ws->last_launches : 0; }

@@ -56,6 +56,7 @@ struct DecodeArgs {
   float* part_o;
   float* part_ml;
   uint32_t ws_heads;
+  float* lse;  // optional [n][H] log-sum-exp of the scaled scores (natural log)
 };
 
 __device__ __forceinline__ float warp_max(float v) {
@@ -445,6 +446,7 @@ __global__ void __launch_bounds__(NT, 1) k_decode(DecodeArgs a) {
         float4 o = make_float4(acc[j][0] * inv, acc[j][1] * inv, acc[j][2] * inv, acc[j][3] * inv);
         if (!(l > 0.f)) o = make_float4(0.f, 0.f, 0.f, 0.f);
         reinterpret_cast<float4*>(a.out + ((uint64_t)b * H + h) * R)[c4] = o;
+        if (a.lse && c4 == 0) a.lse[(uint64_t)b * H + h] = l > 0.f ? m + logf(l) : -INFINITY;
       } else {
         reinterpret_cast<float4*>(a.part_o + ((uint64_t)it * a.ws_heads + h) * R)[c4] =
             make_float4(acc[j][0], acc[j][1], acc[j][2], acc[j][3]);
@@ -465,7 +467,7 @@ __global__ void __launch_bounds__(128) k_combine(uint32_t n, uint32_t H, uint32_
                                                  const uint32_t* __restrict__ seq_count,
                                                  const float* __restrict__ part_o,
                                                  const float* __restrict__ part_ml,
-                                                 float* __restrict__ out) {
+                                                 float* __restrict__ out, float* __restrict__ lse) {
   const uint32_t b = blockIdx.x / H, h = blockIdx.x % H;
   if (b >= n) return;
   const uint32_t cnt = seq_count[b];
@@ -490,6 +492,7 @@ __global__ void __launch_bounds__(128) k_combine(uint32_t n, uint32_t H, uint32_
   float4 r = make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv);
   if (!(l > 0.f)) r = make_float4(0.f, 0.f, 0.f, 0.f);
   reinterpret_cast<float4*>(out + ((uint64_t)b * H + h) * R)[threadIdx.x] = r;
+  if (lse && threadIdx.x == 0) lse[(uint64_t)b * H + h] = l > 0.f ? m + logf(l) : -INFINITY;
 }
 
 size_t decode_smem(int nh) {
@@ -557,7 +560,7 @@ int kvcu_launch_plan_target(kvcu_decode_ws* ws, const kvcu_pool* p, uint32_t n,
 int kvcu_launch_decode(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint32_t n,
                        const uint32_t* seq_ids, uint32_t n_seqs, const uint32_t* toff,
                        const uint32_t* tables, const uint32_t* lens, const float* q,
-                       uint32_t n_heads, float scale, float* out, cudaStream_t st) {
+                       uint32_t n_heads, float scale, float* out, float* lse, cudaStream_t st) {
   const bool tc_ok = kvcu_decode_tc_supported(p, n_heads) && n_heads <= ws->max_heads &&
                      n <= ws->max_batch;
   if (ws->impl == KVCU_DECODE_TENSOR_CORE && !tc_ok) {
@@ -569,10 +572,10 @@ int kvcu_launch_decode(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint32_
     ws->last_launches = 0;
     if (n == 0) return KVCU_OK;
     int rc = kvcu_launch_decode_tc(ws, p, layer, n, seq_ids, n_seqs, toff, tables, lens, q, n_heads,
-                                   scale, out, st);
+                                   scale, out, lse, st);
     if (rc) return rc;
     k_combine<<<n * n_heads, 128, 0, st>>>(n, n_heads, ws->max_heads, ws->seq_first, ws->seq_count,
-                                           ws->part_o, ws->part_ml, out);
+                                           ws->part_o, ws->part_ml, out, lse);
     rc = kvcu_check_cuda(cudaGetLastError(), "combine kernel launch");
     if (rc) return rc;
     ws->last_launches = 2;
@@ -622,11 +625,12 @@ int kvcu_launch_decode(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint32_
   a.seq_count = ws->seq_count;
   a.part_o = ws->part_o;
   a.part_ml = ws->part_ml;
+  a.lse = lse;
   a.ws_heads = ws->max_heads;
   int rc = p->quantized ? launch_decode_q<true>(ws, a, st) : launch_decode_q<false>(ws, a, st);
   if (rc) return rc;
   k_combine<<<n * n_heads, 128, 0, st>>>(n, n_heads, ws->max_heads, ws->seq_first, ws->seq_count,
-                                         ws->part_o, ws->part_ml, out);
+                                         ws->part_o, ws->part_ml, out, lse);
   rc = kvcu_check_cuda(cudaGetLastError(), "combine kernel launch");
   if (rc) return rc;
   ws->last_launches = 2;

@@ -114,6 +114,7 @@ struct TcArgs {
   float* part_o;
   float* part_ml;
   uint32_t ws_heads;
+  float* lse;  // optional [n][H] log-sum-exp (natural log) of single-item entries
 };
 
 // ------------------------------------------------------------------ PTX helpers
@@ -652,6 +653,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           a.part_ml[((uint64_t)it * a.ws_heads + lane) * 2 + 0] = -INFINITY;
           a.part_ml[((uint64_t)it * a.ws_heads + lane) * 2 + 1] = 0.f;
         }
+        if (single && a.lse && ew == 0 && lane < H) a.lse[(uint64_t)im.b * H + lane] = -INFINITY;
         continue;
       }
       // ---- query -> two int8 digits per element (x = s_h * (d0 + d1/256)), per-head
@@ -892,6 +894,17 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           a.part_ml[((uint64_t)it * a.ws_heads + h0 + lane) * 2 + 0] = mh * 0.69314718055994531f;
           a.part_ml[((uint64_t)it * a.ws_heads + h0 + lane) * 2 + 1] = lh;
         }
+        if (single && a.lse && q4 == 0 && lane < HH && h0 + lane < H) {
+          float lh = 0.f, mh = 0.f;
+#pragma unroll
+          for (int h = 0; h < HH; ++h)
+            if ((uint32_t)h == lane) {
+              lh = ltot[h];
+              mh = mref[h];
+            }
+          // mref is in log2 units of the scaled score, l = sum 2^(s - mref)
+          a.lse[(uint64_t)im.b * H + h0 + lane] = lh > 0.f ? (mh + log2f(lh)) * 0.69314718055994531f : -INFINITY;
+        }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(B_PV_EMPTY));
@@ -1070,7 +1083,7 @@ bool kvcu_decode_tc_supported(const kvcu_pool* p, uint32_t n_heads) {
 int kvcu_launch_decode_tc(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint32_t n,
                           const uint32_t* seq_ids, uint32_t n_seqs, const uint32_t* toff,
                           const uint32_t* tables, const uint32_t* lens, const float* q,
-                          uint32_t n_heads, float scale, float* out, cudaStream_t st) {
+                          uint32_t n_heads, float scale, float* out, float* lse, cudaStream_t st) {
   const uint32_t box_rows = p->block_size < (uint32_t)TILE ? p->block_size : (uint32_t)TILE;
   CUtensorMap lat, rope;
   int rc = make_maps(p, box_rows, &lat, &rope);
@@ -1099,6 +1112,7 @@ int kvcu_launch_decode_tc(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint
   a.part_o = ws->part_o;
   a.part_ml = ws->part_ml;
   a.ws_heads = ws->max_heads;
+  a.lse = lse;
   if (n_heads <= 8) return launch_tc<8>(ws->decode_ctas, lat, rope, a, st);
   if (n_heads <= 16) return launch_tc<16>(ws->decode_ctas, lat, rope, a, st);
   if (n_heads <= 20) return launch_tc<20>(ws->decode_ctas, lat, rope, a, st);

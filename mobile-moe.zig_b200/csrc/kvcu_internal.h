@@ -83,8 +83,10 @@ bool kvcu_decode_tc_supported(const kvcu_pool* p, uint32_t n_heads);
 int kvcu_launch_decode_tc(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint32_t n,
                           const uint32_t* seq_ids, uint32_t n_seqs, const uint32_t* toff,
                           const uint32_t* tables, const uint32_t* lens, const float* q,
-                          uint32_t n_heads, float scale, float* out, cudaStream_t st);
+                          uint32_t n_heads, float scale, float* out, float* lse, cudaStream_t st);
+// `lse` (nullable): [n][n_heads] log-sum-exp of the scaled scores, natural log
+// (-inf for an empty context), for merging further terms into `out`.
 int kvcu_launch_decode(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint32_t n,
                        const uint32_t* seq_ids, uint32_t n_seqs, const uint32_t* table_offsets,
                        const uint32_t* tables, const uint32_t* lens, const float* q,
-                       uint32_t n_heads, float scale, float* out, cudaStream_t st);
+                       uint32_t n_heads, float scale, float* out, float* lse, cudaStream_t st);

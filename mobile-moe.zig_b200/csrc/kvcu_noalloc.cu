@@ -126,7 +126,7 @@ extern "C" int kvcu_mla_decode_noalloc(kvcu_pool* p, uint32_t layer, uint32_t n,
       rc = kvcu_launch_plan_target(&ws, p, n, seq_ids, n_seqs, lens, ranges, st);
       if (!rc)
         rc = kvcu_launch_decode(&ws, p, layer, n, seq_ids, n_seqs, table_offsets, tables, lens, q,
-                                n_heads, scale, out, st);
+                                n_heads, scale, out, nullptr, st);
     }
   }
   if (prev >= 0 && prev != p->device) cudaSetDevice(prev);

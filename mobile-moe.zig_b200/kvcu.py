@@ -70,6 +70,10 @@ _SIGS = {
     "kvcu_decode_ws_destroy": (_i32, [_vp]),
     "kvcu_decode_plan": (_i32, [_vp, _vp, _u32, _vp, _u32, _vp, _vp]),
     "kvcu_mla_decode": (_i32, [_vp, _vp, _u32, _u32, _vp, _u32, _vp, _vp, _vp, _vp, _u32, _f32, _vp, _vp]),
+    "kvcu_mla_decode_lse": (_i32, [_vp, _vp, _u32, _u32, _vp, _u32, _vp, _vp, _vp, _vp, _u32, _f32, _vp, _vp,
+                                   _vp]),
+    "kvcu_mla_prepare": (_i32, [_vp, _u32, _u32, _u32, _vp, _vp, _vp, _vp, _f32, _f32, _vp, _vp, _vp, _vp]),
+    "kvcu_mla_finish": (_i32, [_vp, _u32, _u32, _u32, _vp, _vp, _vp, _vp, _f32, _vp, _vp, _vp]),
     "kvcu_decode_last_launches": (_u32, [_vp]),
     "kvcu_decode_ws_set_impl": (_i32, [_vp, _i32]),
     "kvcu_decode_last_impl": (_i32, [_vp]),
@@ -116,6 +120,8 @@ _SIGS = {
     "kvcache_gather": (_i32, [_vp, _u32, _u32, _vp]),
     "kvcache_mla_decode": (_i32, [_vp, _u32, _u32, _vp, _vp, _u32, _f32, _vp]),
     "kvcache_mla_decode_dev": (_i32, [_vp, _u32, _u32, _vp, _vp, _u32, _f32, _vp, _vp]),
+    "kvcache_mla_step_dev": (_i32, [_vp, _u32, _u32, _vp, _vp, _vp, _vp, _vp, _f32, _f32, _vp, _vp, _u32,
+                                    _u32, _u32, _f32, _vp, _vp]),
     "kvcache_last_launches": (_u32, [_vp]),
     "kvcache_last_decode_mapped": (_i32, [_vp]),
     "kvcache_set_decode_impl": (_i32, [_vp, _i32]),
@@ -562,6 +568,17 @@ class KVCache:
         n, H = q_dev.shape[0], q_dev.shape[1]
         check(lib().kvcache_mla_decode_dev(self._h, layer, n, _np_ptr(s), _dptr(q_dev), H, scale,
                                            _dptr(out_dev), _stream(stream)), "mlaDecode_dev")
+
+    def mla_step_dev(self, layer, seq_ids, positions, q, kv_a, norm_w, eps, rope_base, k_b, v_b, qk_nope, v_dim,
+                     scale, attn, stream=None):
+        """One MLA decode step (kvcache_mla_step_dev): device tensors q [n][H][qk_nope+P],
+        kv_a [n][R+P], norm_w [R], k_b [H*qk_nope][R], v_b [H*v_dim][R] -> attn [n][H][v_dim]."""
+        s = np.ascontiguousarray(seq_ids, np.uint32)
+        p = np.ascontiguousarray(positions, np.uint32)
+        n, H = q.shape[0], q.shape[1]
+        check(lib().kvcache_mla_step_dev(self._h, layer, n, _np_ptr(s), _np_ptr(p), _dptr(q), _dptr(kv_a),
+                                         _dptr(norm_w), eps, rope_base, _dptr(k_b), _dptr(v_b), H, qk_nope,
+                                         v_dim, scale, _dptr(attn), _stream(stream)), "mla_step_dev")
 
     @property
     def last_launches(self):

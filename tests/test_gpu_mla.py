@@ -1,0 +1,113 @@
+"""The MLA decode step on the GPU (kvcache_mla_step_dev: kvcu_mla_prepare,
+append, kvcu_mla_decode_lse over the history, kvcu_mla_finish) against the
+reference's non-absorbed step restated on the CPU (oracle/mla_ref.py, one
+oracle KVCache per sequence holding the same history), <= 1e-3 relative."""
+import numpy as np
+import pytest
+
+from kvdata import REL_TOL, rel_err_rows
+
+pytestmark = pytest.mark.gpu
+
+R, P, H, QK_NOPE, V_DIM = 512, 64, 20, 128, 128
+EPS, BASE = 1e-6, 10000.0
+SCALE = float(np.float32(1.0 / np.sqrt(QK_NOPE + P)))
+
+
+@pytest.fixture(scope="module")
+def kv():
+    import torch
+
+    import kvcu
+
+    if not torch.cuda.is_available():
+        pytest.fail("GPU tests need a CUDA device")
+    kvcu.init(0)
+    return kvcu
+
+
+def _run_step(kv, oracle, hist, bs, quant, seed, n_heads=H, layers=1, layer=0):
+    import torch
+
+    import mla_ref
+
+    rng = np.random.default_rng(seed)
+    n = len(hist)
+    cap = [L + 1 for L in hist]
+    nb = sum((c + bs - 1) // bs for c in cap) + 2
+    cache = kv.KVCache.with_blocks(layers, R, P, nb, bs, quantized=quant)
+    for _ in range(n - 1):
+        cache.seq_create()
+    refs = []
+    for s, L in enumerate(hist):
+        cache.seq_ensure_capacity(s, cap[s])
+        oc = oracle.KVCache(layers, R, P, cap[s] + bs, bs)
+        if quant:
+            oc.enableQuantization()
+        assert oc.ensureCapacity(cap[s]) == 0
+        if L:
+            rows = rng.standard_normal((L, R + P)).astype(np.float32)
+            cache.appendBatch(layer, np.full(L, s, np.uint32), np.arange(L, dtype=np.uint32), rows)
+            for p in range(L):
+                assert oc.put(layer, p, rows[p, :R], rows[p, R:]) == 0
+        refs.append(oc)
+    q = rng.standard_normal((n, n_heads, QK_NOPE + P)).astype(np.float32)
+    kv_a = rng.standard_normal((n, R + P)).astype(np.float32)
+    w = (1.0 + 0.1 * rng.standard_normal(R)).astype(np.float32)
+    k_b = (rng.standard_normal((n_heads * QK_NOPE, R)) / np.sqrt(R)).astype(np.float32)
+    v_b = (rng.standard_normal((n_heads * V_DIM, R)) / np.sqrt(R)).astype(np.float32)
+    dev = torch.device("cuda", 0)
+    t = lambda a: torch.from_numpy(a).to(dev)
+    attn = torch.full((n, n_heads, V_DIM), float("nan"), device=dev)
+    ids = np.arange(n, dtype=np.uint32)
+    pos = np.array(hist, np.uint32)
+    cache.mla_step_dev(layer, ids, pos, t(q), t(kv_a), t(w), EPS, BASE, t(k_b), t(v_b), QK_NOPE, V_DIM, SCALE,
+                       attn)
+    torch.cuda.synchronize()
+    assert cache.pool().status() == 0
+    got = attn.cpu().numpy()
+    want = np.stack([mla_ref.mla_attention(refs[b], layer, hist[b], q[b], kv_a[b], w, EPS, BASE, k_b, v_b,
+                                           QK_NOPE, P, V_DIM) for b in range(n)])
+    return cache, refs, got, want
+
+
+@pytest.mark.parametrize("quant", [True, False])
+def test_mla_step_matches_reference(kv, oracle, quant):
+    # empty history, one token, block edges, a long sequence that the plan splits
+    hist = [0, 1, 63, 64, 65, 300, 1500]
+    cache, refs, got, want = _run_step(kv, oracle, hist, 64, quant, 31)
+    assert np.isfinite(got).all()
+    assert rel_err_rows(got, want) <= REL_TOL
+    assert [cache.seq_len(s) for s in range(len(hist))] == [L + 1 for L in hist]
+
+
+def test_mla_step_appends_the_normalised_roped_row(kv, oracle):
+    # the step's append stores RMSNorm(latent) and RoPE(k_pe) as the reference's put does (f32 cache)
+    hist = [5, 130]
+    cache, refs, got, want = _run_step(kv, oracle, hist, 16, False, 32)
+    for s, L in enumerate(hist):
+        row = cache.gather(0, s)[L]
+        c_ref = refs[s].getKVCompressed(0, L)[1]
+        k_ref = refs[s].getKPe(0, L)[1]
+        assert np.allclose(row[:R], c_ref, rtol=1e-5, atol=1e-6)
+        assert np.allclose(row[R:], k_ref, rtol=1e-5, atol=1e-5)
+
+
+def test_mla_step_cuda_core_heads_and_large_positions(kv, oracle):
+    # 28 heads take the CUDA-core decode; positions past 4096 exercise RoPE's large angles
+    hist = [4100, 17, 0]
+    cache, refs, got, want = _run_step(kv, oracle, hist, 16, True, 33, n_heads=28)
+    assert cache.last_decode_impl == kv.DECODE_CUDA_CORE
+    assert rel_err_rows(got, want) <= REL_TOL
+
+
+def test_mla_step_rejects_repeated_sequence(kv):
+    import torch
+
+    cache = kv.KVCache.with_blocks(1, R, P, 8, 16, quantized=True)
+    cache.seq_ensure_capacity(0, 4)
+    dev = torch.device("cuda", 0)
+    z = lambda *s: torch.zeros(s, device=dev)
+    with pytest.raises(kv.KVCudaError):
+        cache.mla_step_dev(0, [0, 0], [0, 1], z(2, H, QK_NOPE + P), z(2, R + P), z(R), EPS, BASE,
+                           z(H * QK_NOPE, R), z(H * V_DIM, R), QK_NOPE, V_DIM, SCALE, z(2, H, V_DIM))
