@@ -218,6 +218,42 @@ def run_reference(args, rank, world):
 
 # ------------------------------------------------------------------ GPU arm
 APPEND_ROWS = 1 << 17
+QK_NOPE, V_DIM = 128, 128  # DeepSeek2-Lite head dims (head_dim 192 = 128 + 64 rope)
+
+
+def measure_mla_step(cache, ids, lens_before, NL, steps, torch, dev, st):
+    """Whole MLA decode steps (kvcache_mla_step_dev) on the same cache, all layers:
+    RMSNorm + RoPE + k_b absorption, the append, a plan, the decode with LSE over
+    the history, the newest-token merge and v_b. One untimed step, then `steps`
+    timed with CUDA events per layer. Random f32 weights of the model's shapes."""
+    n = ids.size
+    g = torch.Generator(device=dev).manual_seed(SEED + 7)
+    with torch.cuda.stream(st):
+        q = torch.randn((NL, n, H, QK_NOPE + P), device=dev, generator=g)
+        kv_a = torch.randn((NL, n, W), device=dev, generator=g)
+        norm_w = 1.0 + 0.1 * torch.randn((NL, R), device=dev, generator=g)
+        k_b = torch.randn((NL, H * QK_NOPE, R), device=dev, generator=g) / R ** 0.5
+        v_b = torch.randn((NL, H * V_DIM, R), device=dev, generator=g) / R ** 0.5
+        attn = torch.empty((NL, n, H, V_DIM), device=dev)
+    st.synchronize()
+    times, tokens = [], 0
+    for k in range(1 + steps):
+        pos = (lens_before + k).astype(np.uint32)
+        for layer in range(NL):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            cache.mla_step_dev(layer, ids, pos, q[layer], kv_a[layer], norm_w[layer], 1e-6, 10000.0, k_b[layer],
+                               v_b[layer], QK_NOPE, V_DIM, SCALE, attn[layer], st)
+            e1.record(st)
+            if k:
+                times.append((e0, e1))
+                tokens += int((pos.astype(np.int64) + 1).sum())
+    st.synchronize()
+    ms = sum(a.elapsed_time(b) for a, b in times) / len(times)
+    return {"ms_per_layer": ms, "ctx_tokens_per_s": tokens / (ms * 1e-3 * len(times)), "layers": NL,
+            "steps": steps, "what": "kvcache_mla_step_dev per layer: RMSNorm, RoPE, k_b absorption, append, "
+                                    "plan, decode with LSE over the history, newest-token merge, v_b "
+                                    "(q, kv_a after their projections; random f32 weights)"}
 
 
 def measure_append(kvcu, torch, dev, local_rank, reps=5):
@@ -270,7 +306,7 @@ def run_ours(args, rank, world, local_rank):
     mine = np.array(parts[rank], np.int64)
     lens0 = lens_all[mine]
     n = mine.size
-    total_steps = args.warmup + args.steps + args.e2e_warmup + args.e2e_steps
+    total_steps = args.warmup + args.steps + args.e2e_warmup + args.e2e_steps + 1 + args.mla_steps
     nb = int(sum((int(L) + total_steps + BS - 1) // BS for L in lens0)) + 8
     cache = kvcu.KVCache.with_blocks(NL, R, P, nb, BS, quantized=True, device=local_rank)
     for _ in range(n - 1):
@@ -398,6 +434,8 @@ def run_ours(args, rank, world, local_rank):
     h2d = NL * n * (W * 4 + 8 + H * W * 4)
     d2h = NL * n * H * R * 4
 
+    mla = measure_mla_step(cache, ids, lens0 + base + args.e2e_warmup + args.e2e_steps, NL, args.mla_steps,
+                           torch, dev, st)
     append_gbs = measure_append(kvcu, torch, dev, local_rank)
     clk_sum = clk.summary()
 
@@ -440,6 +478,7 @@ def run_ours(args, rank, world, local_rank):
             "append": {"GB/s": append_gbs, "rows": APPEND_ROWS,
                        "bytes_per_row": 2304 + Q8_ROW_BYTES + 8,
                        "what": "one batched f32->Q8_0 append through the block table (prefill-sized)"},
+            "mla_step": mla,
             "prefill_s": t_pre,
         }
         if cpu:
@@ -456,6 +495,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--e2e-warmup", type=int, default=1)
+    ap.add_argument("--mla-steps", type=int, default=2, help="timed whole-MLA-step passes (after one untimed)")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-sample-tokens", type=int, default=400_000)
     ap.add_argument("--no-cpu-baseline", action="store_true")
