@@ -718,9 +718,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const uint16_t* scrow =
             reinterpret_cast<const uint16_t*>(smem + s * STAGE_BYTES + ST_SC) + trow * NBLK;
         // per head: sum over blocks of d_b * (256 x0 + x1)
-        float acc[HH];
+        float2 acc2[HH / 2];  // heads (2p, 2p+1)
 #pragma unroll
-        for (int h = 0; h < HH; ++h) acc[h] = 0.f;
+        for (int p = 0; p < HH / 2; ++p) acc2[p] = make_float2(0.f, 0.f);
         // Three Q8_0 blocks per TMEM round trip (18 blocks -> 6 groups); this
         // half reads its 2HH digit columns of each slot, per head pair
         // [digit0 h, digit0 h+1, digit1 h, digit1 h+1].
@@ -743,17 +743,23 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           const float d0 = __half2float(__ushort_as_half(scrow[GB * gi]));
           const float d1 = __half2float(__ushort_as_half(scrow[GB * gi + 1]));
           const float d2 = __half2float(__ushort_as_half(scrow[GB * gi + 2]));
+          // Per head: 256 x0 + x1 exactly in int32 (|x0| <= 32 * 127^2 < 2^19),
+          // one rounding to f32, then the block scale, two heads per packed
+          // f32x2 FMA (each lane is one fused multiply-add, as fmaf). Head pair p
+          // has digit-0 columns 4p, 4p+1 and digit-1 columns 4p+2, 4p+3.
+          const float2 dd0 = make_float2(d0, d0), dd1 = make_float2(d1, d1), dd2 = make_float2(d2, d2);
 #pragma unroll
-          for (int h = 0; h < HH; ++h) {
-            // 256 x0 + x1 exactly in int32 (|x0| <= 32 * 127^2 < 2^19), one
-            // rounding to f32, then the block scale
-            const int c0 = 4 * (h >> 1) + (h & 1), c1 = c0 + 2;
-            const int v0 = (int)r0[c0] * 256 + (int)r0[c1];
-            const int v1 = (int)r1[c0] * 256 + (int)r1[c1];
-            const int v2 = (int)r2[c0] * 256 + (int)r2[c1];
-            acc[h] = fmaf(d0, __int2float_rn(v0), acc[h]);
-            acc[h] = fmaf(d1, __int2float_rn(v1), acc[h]);
-            acc[h] = fmaf(d2, __int2float_rn(v2), acc[h]);
+          for (int p = 0; p < HH / 2; ++p) {
+            const int c = 4 * p;
+            const float2 f0 = make_float2(__int2float_rn((int)r0[c] * 256 + (int)r0[c + 2]),
+                                          __int2float_rn((int)r0[c + 1] * 256 + (int)r0[c + 3]));
+            const float2 f1 = make_float2(__int2float_rn((int)r1[c] * 256 + (int)r1[c + 2]),
+                                          __int2float_rn((int)r1[c + 1] * 256 + (int)r1[c + 3]));
+            const float2 f2 = make_float2(__int2float_rn((int)r2[c] * 256 + (int)r2[c + 2]),
+                                          __int2float_rn((int)r2[c + 1] * 256 + (int)r2[c + 3]));
+            acc2[p] = __ffma2_rn(dd0, f0, acc2[p]);
+            acc2[p] = __ffma2_rn(dd1, f1, acc2[p]);
+            acc2[p] = __ffma2_rn(dd2, f2, acc2[p]);
           }
           tc_fence_before();
           __syncwarp();
@@ -767,7 +773,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
         for (int p = 0; p < HH / 2; ++p) {
           const float2 q2 = qsc2[p];
-          const float vx = acc[2 * p] * q2.x, vy = acc[2 * p + 1] * q2.y;
+          const float2 v2 = __fmul2_rn(acc2[p], q2);
+          const float vx = v2.x, vy = v2.y;
           sc[2 * p] = (valid && h0 + 2 * p < H && vx == vx) ? vx : -INFINITY;
           sc[2 * p + 1] = (valid && h0 + 2 * p + 1 < H && vy == vy) ? vy : -INFINITY;
         }
