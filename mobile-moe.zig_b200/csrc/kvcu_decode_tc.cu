@@ -740,6 +740,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           reg_fence(r0);
           reg_fence(r1);
           reg_fence(r2);
+          // the values are in registers: the slot can take the next group's MMAs now
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(B_QK_EMPTY + slot));
           const float d0 = __half2float(__ushort_as_half(scrow[GB * gi]));
           const float d1 = __half2float(__ushort_as_half(scrow[GB * gi + 1]));
           const float d2 = __half2float(__ushort_as_half(scrow[GB * gi + 2]));
@@ -761,9 +765,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             acc2[p] = __ffma2_rn(dd1, f1, acc2[p]);
             acc2[p] = __ffma2_rn(dd2, f2, acc2[p]);
           }
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(bar(B_QK_EMPTY + slot));
         }
         if (!ok) break;
         __syncwarp();

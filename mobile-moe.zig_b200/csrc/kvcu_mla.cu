@@ -75,33 +75,35 @@ __global__ void __launch_bounds__(ROWS_THREADS)
 }
 
 // Per-head f32 GEMM C[m][n] = sum_k A[m][k] * B(k, n) for head z = blockIdx.z,
-// B(k, n) = TRANS_B ? Bm[n * ldb + k] : Bm[k * ldb + n]. 64 x 64 output tile
-// per CTA, 16-deep K slices through shared memory, 4 x 4 outputs per thread.
-constexpr int GM = 64, GN = 64, GK = 16;
+// B(k, n) = TRANS_B ? Bm[n * ldb + k] : Bm[k * ldb + n]. 128 x 64 output tile
+// per CTA, 16-deep K slices through shared memory; each thread owns 8 rows x 4
+// columns and reads its operands from shared memory as float4.
+constexpr int GM = 128, GN = 64, GK = 16;
 template <bool TRANS_B>
 __global__ void __launch_bounds__(256)
     k_head_gemm(uint32_t M, uint32_t N, uint32_t K, const float* __restrict__ A, uint32_t lda,
                 uint64_t a_hs, const float* __restrict__ B, uint32_t ldb, uint64_t b_hs,
                 float* __restrict__ C, uint32_t ldc, uint64_t c_hs) {
-  __shared__ float As[GK][GM + 4];
-  __shared__ float Bs[GK][GN + 4];
+  __shared__ __align__(16) float As[GK][GM + 4];
+  __shared__ __align__(16) float Bs[GK][GN + 4];
   const uint32_t z = blockIdx.z, tid = threadIdx.x;
   A += z * a_hs;
   B += z * b_hs;
   C += z * c_hs;
   const uint32_t m0 = blockIdx.y * GM, n0 = blockIdx.x * GN;
-  const uint32_t tx = tid % 16, ty = tid / 16;
-  float acc[4][4] = {};
+  const uint32_t tx = tid % 16, ty = tid / 16;  // columns tx*4.., rows ty*8..
+  float acc[8][4] = {};
   for (uint32_t k0 = 0; k0 < K; k0 += GK) {
-    // A tile [GM][GK] -> As[k][m]; each thread 4 elements
+    // A tile [GM][GK] -> As[k][m]
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {
+    for (int r = 0; r < (GM * GK) / 256; ++r) {
       const uint32_t e = tid + 256u * r, mm = e / GK, kk = e % GK;
       const uint32_t gm = m0 + mm, gk = k0 + kk;
       As[kk][mm] = (gm < M && gk < K) ? A[(uint64_t)gm * lda + gk] : 0.f;
     }
+    // B tile [GK][GN] -> Bs[k][n]
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {
+    for (int r = 0; r < (GN * GK) / 256; ++r) {
       const uint32_t e = tid + 256u * r;
       uint32_t kk, nn;
       if (TRANS_B) {
@@ -119,21 +121,21 @@ __global__ void __launch_bounds__(256)
     __syncthreads();
 #pragma unroll
     for (int kk = 0; kk < GK; ++kk) {
-      float a[4], bv[4];
+      const float4 a0 = *reinterpret_cast<const float4*>(&As[kk][ty * 8]);
+      const float4 a1 = *reinterpret_cast<const float4*>(&As[kk][ty * 8 + 4]);
+      const float4 b4 = *reinterpret_cast<const float4*>(&Bs[kk][tx * 4]);
+      const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      const float bv[4] = {b4.x, b4.y, b4.z, b4.w};
 #pragma unroll
-      for (int i = 0; i < 4; ++i) a[i] = As[kk][ty * 4 + i];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) bv[j] = Bs[kk][tx * 4 + j];
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
+      for (int i = 0; i < 8; ++i)
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], bv[j], acc[i][j]);
     }
     __syncthreads();
   }
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const uint32_t gm = m0 + ty * 4 + i;
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t gm = m0 + ty * 8 + i;
     if (gm >= M) continue;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
