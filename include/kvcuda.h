@@ -123,6 +123,9 @@ int kvcu_pool_describe(const kvcu_pool* pool, kvcu_pool_desc* out);
 int kvcu_pool_zero(kvcu_pool* pool, void* stream);
 /* Read and clear the device status word (synchronises `stream`). */
 int kvcu_pool_status(kvcu_pool* pool, uint32_t* status_out, void* stream);
+/* Copy physical block `src` to `dst` in every layer, device to device
+ * (stream-ordered): the copy of a copy-on-write of a shared prefix block. */
+int kvcu_pool_copy_block(kvcu_pool* pool, uint32_t src, uint32_t dst, void* stream);
 
 /* ------------------------------------------------------------ append / gather
  * Sequences are described by device arrays indexed by sequence id s:
@@ -314,6 +317,17 @@ void kvcache_cache_block(kvcache* c, uint32_t block_idx, const uint32_t* token_i
 uint32_t kvcache_find_prefix_blocks(kvcache* c, const uint32_t* tokens, uint32_t n);
 int kvcache_reuse_prefix_blocks(kvcache* c, const uint32_t* tokens, uint32_t n, uint32_t n_blocks);
 uint64_t kvcache_compute_hash(const uint32_t* token_ids, uint32_t n, uint64_t prefix_hash);
+/* The same for any sequence of the pool, so that sequences share cached prefix
+ * blocks on the device (the hash map, and so kvcache_find_prefix_blocks, is
+ * pool-wide).  reuse makes `seq`'s first n_blocks blocks the cached ones
+ * (retained) and sets its len to n_blocks * block_size.  A shared block is never
+ * written: every write path (put, append_batch(_dev), the MLA step) first copies
+ * a block held by more than one owner to a fresh block for the writing sequence
+ * (copy-on-write). */
+int kvcache_seq_cache_block(kvcache* c, uint32_t seq, uint32_t block_idx, const uint32_t* token_ids,
+                            uint32_t n_tokens, uint64_t prefix_hash);
+int kvcache_seq_reuse_prefix_blocks(kvcache* c, uint32_t seq, const uint32_t* tokens, uint32_t n,
+                                    uint32_t n_blocks);
 
 /* ---- many sequences on one pool (sequence 0 always exists) ---- */
 /* New empty sequence; returns its id or a negative error. */

@@ -433,6 +433,36 @@ int validate_positions(kvcache* c, uint32_t layer, uint32_t n, const uint32_t* s
   return KVCU_OK;
 }
 
+// Copy-on-write before writing (seq, pos): a block that is also held elsewhere
+// (refcount > 1: another sequence reused it as a cached prefix) is first copied,
+// all layers, to a fresh block that this sequence then owns alone, so shared
+// prefix blocks stay read-only. The reference never writes into a shared
+// block, because only full blocks are cached and reusePrefixBlocks moves len past
+// them; this keeps that true after a truncate into a shared prefix as well.
+// Runs after validate_positions, on the stream of the write that follows.
+int cow_for_write(kvcache* c, uint32_t n, const uint32_t* seq_ids, const uint32_t* positions,
+                  cudaStream_t st) {
+  for (uint32_t r = 0; r < n; ++r) {
+    Seq& q = c->seqs[seq_ids[r]];
+    const uint32_t bi = positions[r] / c->block_size;
+    const uint32_t old = q.table[bi];
+    if (c->ref_count[old] <= 1) continue;
+    uint32_t fresh;
+    int rc = allocate_block(c, &fresh);
+    if (rc) return rc;
+    rc = kvcu_pool_copy_block(c->pool, old, fresh, st);
+    if (rc) {
+      release_block(c, fresh);
+      return rc;
+    }
+    release_block(c, old);
+    q.table[bi] = fresh;
+    c->tables_dirty = true;
+    c->epoch++;
+  }
+  return KVCU_OK;
+}
+
 void bump_lens(kvcache* c, uint32_t n, const uint32_t* seq_ids, const uint32_t* positions) {
   for (uint32_t r = 0; r < n; ++r) {
     Seq& q = c->seqs[seq_ids[r]];
@@ -598,6 +628,7 @@ int kvcache_put(kvcache* c, uint32_t layer, uint32_t pos, const float* kv_comp, 
   DevScope d(c->device);
   const uint32_t s0 = 0;
   int rc = validate_positions(c, layer, 1, &s0, &pos);
+  if (!rc) rc = cow_for_write(c, 1, &s0, &pos, c->stream);
   if (rc) return rc;
   std::vector<float> row(c->row_width());
   memcpy(row.data(), kv_comp, c->kv_rank * 4);
@@ -655,17 +686,23 @@ uint64_t kvcache_compute_hash(const uint32_t* token_ids, uint32_t n, uint64_t pr
   return xxh64(buf.data(), buf.size(), 0);
 }
 
-void kvcache_cache_block(kvcache* c, uint32_t block_idx, const uint32_t* token_ids,
-                         uint32_t n_tokens, uint64_t prefix_hash) {
-  if (!c) return;
-  Seq& q = c->seqs[0];
-  if (block_idx >= q.table.size() || n_tokens != c->block_size) return;
+int kvcache_seq_cache_block(kvcache* c, uint32_t seq, uint32_t block_idx, const uint32_t* token_ids,
+                            uint32_t n_tokens, uint64_t prefix_hash) {
+  if (!c || seq >= c->seqs.size() || (n_tokens && !token_ids)) return KVCU_ERR_INVALID_ARG;
+  Seq& q = c->seqs[seq];
+  if (block_idx >= q.table.size() || n_tokens != c->block_size) return KVCU_OK;  // full blocks only
   const uint32_t id = q.table[block_idx];
   const uint64_t h = kvcache_compute_hash(token_ids, n_tokens, prefix_hash);
   auto it = c->hash_map.find(h);
-  if (it != c->hash_map.end() && it->second != id) return;  // collision: skip
+  if (it != c->hash_map.end() && it->second != id) return KVCU_OK;  // collision: skip
   c->hash[id] = h;
   c->hash_map[h] = id;
+  return KVCU_OK;
+}
+
+void kvcache_cache_block(kvcache* c, uint32_t block_idx, const uint32_t* token_ids,
+                         uint32_t n_tokens, uint64_t prefix_hash) {
+  if (c) kvcache_seq_cache_block(c, 0, block_idx, token_ids, n_tokens, prefix_hash);
 }
 
 uint32_t kvcache_find_prefix_blocks(kvcache* c, const uint32_t* tokens, uint32_t n) {
@@ -683,11 +720,16 @@ uint32_t kvcache_find_prefix_blocks(kvcache* c, const uint32_t* tokens, uint32_t
 }
 
 int kvcache_reuse_prefix_blocks(kvcache* c, const uint32_t* tokens, uint32_t n, uint32_t n_blocks) {
-  if (!c) return KVCU_ERR_INVALID_ARG;
+  return kvcache_seq_reuse_prefix_blocks(c, 0, tokens, n, n_blocks);
+}
+
+int kvcache_seq_reuse_prefix_blocks(kvcache* c, uint32_t seq, const uint32_t* tokens, uint32_t n,
+                                    uint32_t n_blocks) {
+  if (!c || seq >= c->seqs.size()) return KVCU_ERR_INVALID_ARG;
   if (n_blocks == 0) return KVCU_OK;
   const uint32_t bs = c->block_size;
-  if ((uint64_t)n_blocks * bs > n) return KVCU_ERR_INVALID_ARG;
-  Seq& q = c->seqs[0];
+  if ((uint64_t)n_blocks * bs > n || !tokens) return KVCU_ERR_INVALID_ARG;
+  Seq& q = c->seqs[seq];
   uint64_t prefix = kNoHash;
   for (uint32_t bi = 0; bi < n_blocks; ++bi) {
     const uint64_t h = kvcache_compute_hash(tokens + (uint64_t)bi * bs, bs, prefix);
@@ -749,6 +791,7 @@ int kvcache_append_batch(kvcache* c, uint32_t layer, uint32_t n, const uint32_t*
   if (!n) return KVCU_OK;
   DevScope d(c->device);
   int rc = validate_positions(c, layer, n, seq_ids, positions);
+  if (!rc) rc = cow_for_write(c, n, seq_ids, positions, c->stream);
   if (rc) return rc;
   rc = append_host_rows(c, layer, n, seq_ids, positions, rows);
   if (rc) return rc;
@@ -764,6 +807,7 @@ int kvcache_append_batch_dev(kvcache* c, uint32_t layer, uint32_t n, const uint3
   if (!n) return KVCU_OK;
   DevScope d(c->device);
   int rc = validate_positions(c, layer, n, seq_ids, positions);
+  if (!rc) rc = cow_for_write(c, n, seq_ids, positions, (cudaStream_t)stream);
   if (!rc) rc = sync_tables(c);
   if (!rc) rc = sync_lens(c);
   if (rc) return rc;
@@ -844,6 +888,7 @@ int kvcache_mla_step_dev(kvcache* c, uint32_t layer, uint32_t n, const uint32_t*
   DevScope d(c->device);
   const cudaStream_t st = (cudaStream_t)stream;
   int rc = validate_positions(c, layer, n, seq_ids, positions);
+  if (!rc) rc = cow_for_write(c, n, seq_ids, positions, st);
   if (rc) return rc;
   const uint32_t R = c->kv_rank, Wd = c->row_width(), n_seqs = (uint32_t)c->seqs.size();
   // scratch: q_abs [n][H][W], rows [n][W], latent [n][H][R], lse [n][H]

@@ -207,6 +207,32 @@ int kvcu_pool_status(kvcu_pool* p, uint32_t* status_out, void* stream) {
   return KVCU_OK;
 }
 
+int kvcu_pool_copy_block(kvcu_pool* p, uint32_t src, uint32_t dst, void* stream) {
+  if (!valid_pool(p) || src >= p->num_blocks || dst >= p->num_blocks) return KVCU_ERR_INVALID_ARG;
+  if (src == dst) return KVCU_OK;
+  DeviceGuard g(p->device);
+  if (g.rc) return g.rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  // one block of one array is BS contiguous rows per layer; layers are NB*BS rows apart
+  auto copy = [&](void* base, size_t row_bytes) -> int {
+    if (!base) return KVCU_OK;
+    char* b = static_cast<char*>(base);
+    const size_t width = (size_t)p->block_size * row_bytes, pitch = (size_t)p->num_blocks * width;
+    return kvcu_check_cuda(cudaMemcpy2DAsync(b + dst * width, pitch, b + src * width, pitch, width, p->n_layers,
+                                             cudaMemcpyDeviceToDevice, st),
+                           "cudaMemcpy2DAsync(block copy)");
+  };
+  int rc;
+  if (p->quantized) {
+    rc = copy(p->qs, 32ull * p->nblk);
+    if (!rc) rc = copy(p->sc, 2ull * p->nblk);
+  } else {
+    rc = copy(p->kv, 4ull * p->kv_rank);
+    if (!rc) rc = copy(p->pe, 4ull * p->rope_dim);
+  }
+  return rc;
+}
+
 int kvcu_append(kvcu_pool* p, uint32_t layer, uint32_t n_rows, const float* latent,
                 uint64_t latent_stride, const float* rope, uint64_t rope_stride,
                 const uint32_t* row_seq, const uint32_t* row_pos, uint32_t n_seqs,

@@ -63,6 +63,7 @@ _SIGS = {
     "kvcu_pool_describe": (_i32, [_vp, C.POINTER(PoolDesc)]),
     "kvcu_pool_zero": (_i32, [_vp, _vp]),
     "kvcu_pool_status": (_i32, [_vp, C.POINTER(_u32), _vp]),
+    "kvcu_pool_copy_block": (_i32, [_vp, _u32, _u32, _vp]),
     "kvcu_append": (_i32, [_vp, _u32, _u32, _vp, _u64, _vp, _u64, _vp, _vp, _u32, _vp, _vp, _vp, _vp]),
     "kvcu_gather": (_i32, [_vp, _u32, _vp, _u32, _u32, _vp, _vp]),
     "kvcu_gather_rows": (_i32, [_vp, _u32, _u32, _vp, _vp, _u32, _vp, _vp, _vp, _vp]),
@@ -107,6 +108,8 @@ _SIGS = {
     "kvcache_cache_block": (None, [_vp, _u32, _vp, _u32, _u64]),
     "kvcache_find_prefix_blocks": (_u32, [_vp, _vp, _u32]),
     "kvcache_reuse_prefix_blocks": (_i32, [_vp, _vp, _u32, _u32]),
+    "kvcache_seq_cache_block": (_i32, [_vp, _u32, _u32, _vp, _u32, _u64]),
+    "kvcache_seq_reuse_prefix_blocks": (_i32, [_vp, _u32, _vp, _u32, _u32]),
     "kvcache_compute_hash": (_u64, [_vp, _u32, _u64]),
     "kvcache_seq_create": (_i64, [_vp]),
     "kvcache_num_seqs": (_u32, [_vp]),
@@ -487,6 +490,16 @@ class KVCache:
         t = np.ascontiguousarray(tokens, np.uint32)
         check(lib().kvcache_reuse_prefix_blocks(self._h, _np_ptr(t), t.size, n_blocks),
               "reusePrefixBlocks")
+
+    def seq_cache_block(self, seq, block_idx, token_ids, prefix_hash):
+        t = np.ascontiguousarray(token_ids, np.uint32)
+        check(lib().kvcache_seq_cache_block(self._h, seq, block_idx, _np_ptr(t), t.size, prefix_hash),
+              "seq_cache_block")
+
+    def seq_reuse_prefix_blocks(self, seq, tokens, n_blocks):
+        t = np.ascontiguousarray(tokens, np.uint32)
+        check(lib().kvcache_seq_reuse_prefix_blocks(self._h, seq, _np_ptr(t), t.size, n_blocks),
+              "seq_reuse_prefix_blocks")
 
     @staticmethod
     def computeHash(token_ids, prefix_hash=NO_HASH):
