@@ -391,6 +391,47 @@ int kvcache_last_decode_impl(const kvcache* c);
 int kvcache_save_to_file_v2(kvcache* c, const char* path);
 int kvcache_load_from_file_v2(kvcache* c, const char* path);
 
+/* ---- continuous batching over one pool (BatchScheduler, src/batch_queue.zig:75-232) ----
+ * Each request is a sequence of the kvcache (instead of owning a KVCache,
+ * src/batch_queue.zig:33-52); ids start at 1.  collect returns up to
+ * max_batch_size requests that are running or waiting and not finished
+ * (completed, max_tokens generated, or last token == eos), highest priority
+ * first, then in arrival order, with their pool sequences.  reap_completed
+ * drops completed requests and resets their sequences (blocks back to the
+ * pool); the sequences are reused by later requests.  reclaim_blocks resets
+ * the sequences of paused and completed requests and returns the blocks freed.
+ * Host-only; not thread-safe (one scheduler per host thread, as in the
+ * reference). */
+#define KVCU_SEQ_WAITING 0
+#define KVCU_SEQ_RUNNING 1
+#define KVCU_SEQ_PAUSED 2
+#define KVCU_SEQ_COMPLETED 3
+#define KVCU_PRIORITY_LOW 0
+#define KVCU_PRIORITY_NORMAL 1
+#define KVCU_PRIORITY_HIGH 2
+#define KVCU_PRIORITY_CRITICAL 3
+typedef struct kvcu_batch kvcu_batch;
+kvcu_batch* kvcu_batch_create(kvcache* c, uint32_t max_batch_size);
+int kvcu_batch_destroy(kvcu_batch* b);
+/* addRequest / addRequestWithPriority: the new id, or a negative error. */
+int64_t kvcu_batch_add_request(kvcu_batch* b, uint32_t max_tokens, int priority);
+/* collectBatchIndices: writes ids and pool sequences; returns how many. */
+uint32_t kvcu_batch_collect(kvcu_batch* b, uint32_t eos_token, uint64_t* ids_out, uint32_t* seqs_out,
+                            uint32_t cap);
+int kvcu_batch_mark_running(kvcu_batch* b, const uint64_t* ids, uint32_t n);
+int kvcu_batch_mark_completed(kvcu_batch* b, uint64_t id);
+int kvcu_batch_set_status(kvcu_batch* b, uint64_t id, int status);
+int kvcu_batch_status(const kvcu_batch* b, uint64_t id);
+/* Record a generated token (Sequence.tokens); is_finished returns 1 / 0. */
+int kvcu_batch_push_token(kvcu_batch* b, uint64_t id, uint32_t token);
+int kvcu_batch_is_finished(kvcu_batch* b, uint64_t id, uint32_t eos_token);
+uint32_t kvcu_batch_reap_completed(kvcu_batch* b);
+uint32_t kvcu_batch_reclaim_blocks(kvcu_batch* b);
+uint32_t kvcu_batch_running_count(const kvcu_batch* b);
+uint32_t kvcu_batch_size(const kvcu_batch* b);
+/* The request's pool sequence, or a negative error. */
+int64_t kvcu_batch_seq(const kvcu_batch* b, uint64_t id);
+
 #ifdef __cplusplus
 }
 #endif

@@ -131,6 +131,21 @@ _SIGS = {
     "kvcache_last_decode_impl": (_i32, [_vp]),
     "kvcache_save_to_file_v2": (_i32, [_vp, _cp]),
     "kvcache_load_from_file_v2": (_i32, [_vp, _cp]),
+    "kvcu_batch_create": (_vp, [_vp, _u32]),
+    "kvcu_batch_destroy": (_i32, [_vp]),
+    "kvcu_batch_add_request": (_i64, [_vp, _u32, _i32]),
+    "kvcu_batch_collect": (_u32, [_vp, _u32, _vp, _vp, _u32]),
+    "kvcu_batch_mark_running": (_i32, [_vp, _vp, _u32]),
+    "kvcu_batch_mark_completed": (_i32, [_vp, _u64]),
+    "kvcu_batch_set_status": (_i32, [_vp, _u64, _i32]),
+    "kvcu_batch_status": (_i32, [_vp, _u64]),
+    "kvcu_batch_push_token": (_i32, [_vp, _u64, _u32]),
+    "kvcu_batch_is_finished": (_i32, [_vp, _u64, _u32]),
+    "kvcu_batch_reap_completed": (_u32, [_vp]),
+    "kvcu_batch_reclaim_blocks": (_u32, [_vp]),
+    "kvcu_batch_running_count": (_u32, [_vp]),
+    "kvcu_batch_size": (_u32, [_vp]),
+    "kvcu_batch_seq": (_i64, [_vp, _u64]),
 }
 
 
@@ -646,3 +661,80 @@ class KVCache:
             synth_rows(seed, layer, t_d, p_d, W, rows[:n], outlier_p, stream)
             self.appendBatch_dev(layer, s_h, p_h, s_d, p_d, rows[:n], stream)
         return total
+
+
+SEQ_WAITING, SEQ_RUNNING, SEQ_PAUSED, SEQ_COMPLETED = 0, 1, 2, 3
+PRIORITY_LOW, PRIORITY_NORMAL, PRIORITY_HIGH, PRIORITY_CRITICAL = 0, 1, 2, 3
+
+
+class BatchScheduler:
+    """BatchScheduler (src/batch_queue.zig:75-232) over one KVCache's shared pool
+    (kvcu_batch_*): each request is a sequence of `cache`."""
+
+    def __init__(self, cache: "KVCache", max_batch_size: int):
+        self._cache = cache  # keeps the cache alive while the scheduler uses it
+        self._h = lib().kvcu_batch_create(cache._h, max_batch_size)
+        if not self._h:
+            raise KVCudaError(-11, "kvcu_batch_create", last_error())
+        self.max_batch_size = max_batch_size
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().kvcu_batch_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+    def addRequest(self, max_tokens, priority=PRIORITY_NORMAL) -> int:
+        rc = lib().kvcu_batch_add_request(self._h, max_tokens, priority)
+        if rc < 0:
+            check(int(rc), "addRequest")
+        return int(rc)
+
+    def collectBatch(self, eos_token=0):
+        """(ids, pool sequences) of the next batch, in priority then arrival order."""
+        ids = np.zeros(self.max_batch_size, np.uint64)
+        seqs = np.zeros(self.max_batch_size, np.uint32)
+        n = lib().kvcu_batch_collect(self._h, eos_token, _np_ptr(ids), _np_ptr(seqs), self.max_batch_size)
+        return ids[:n].copy(), seqs[:n].copy()
+
+    def markRunning(self, ids):
+        a = np.ascontiguousarray(ids, np.uint64)
+        check(lib().kvcu_batch_mark_running(self._h, _np_ptr(a), a.size), "markRunning")
+
+    def markCompleted(self, rid):
+        check(lib().kvcu_batch_mark_completed(self._h, rid), "markCompleted")
+
+    def setStatus(self, rid, status):
+        check(lib().kvcu_batch_set_status(self._h, rid, status), "setStatus")
+
+    def status(self, rid) -> int:
+        return lib().kvcu_batch_status(self._h, rid)
+
+    def pushToken(self, rid, token):
+        check(lib().kvcu_batch_push_token(self._h, rid, token), "pushToken")
+
+    def isFinished(self, rid, eos_token=0) -> bool:
+        rc = lib().kvcu_batch_is_finished(self._h, rid, eos_token)
+        if rc < 0:
+            check(rc, "isFinished")
+        return bool(rc)
+
+    def reapCompleted(self) -> int:
+        return lib().kvcu_batch_reap_completed(self._h)
+
+    def reclaimBlocks(self) -> int:
+        return lib().kvcu_batch_reclaim_blocks(self._h)
+
+    def runningCount(self) -> int:
+        return lib().kvcu_batch_running_count(self._h)
+
+    def __len__(self):
+        return lib().kvcu_batch_size(self._h)
+
+    def seq(self, rid) -> int:
+        rc = lib().kvcu_batch_seq(self._h, rid)
+        if rc < 0:
+            check(int(rc), "seq")
+        return int(rc)
