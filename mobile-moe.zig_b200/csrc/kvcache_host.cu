@@ -23,6 +23,7 @@
 #include <algorithm>
 #include <errno.h>
 #include <new>
+#include <thread>
 #include <unordered_map>
 #include <vector>
 
@@ -959,30 +960,80 @@ namespace {
 
 constexpr size_t kIoChunk = 64ull << 20;
 
+// Two host buffers for the pool section of a checkpoint, pinned so that the
+// device copies run at full bus speed (pageable ones if pinning fails).
+struct IoBuffers {
+  uint8_t* pinned[2] = {nullptr, nullptr};
+  std::vector<uint8_t> pageable[2];
+  explicit IoBuffers(size_t n) {
+    for (int i = 0; i < 2; ++i)
+      if (cudaHostAlloc(reinterpret_cast<void**>(&pinned[i]), n, cudaHostAllocDefault) != cudaSuccess) {
+        cudaGetLastError();
+        pinned[i] = nullptr;
+        pageable[i].resize(n);
+      }
+  }
+  ~IoBuffers() {
+    for (int i = 0; i < 2; ++i)
+      if (pinned[i]) cudaFreeHost(pinned[i]);
+  }
+  uint8_t* operator[](int i) { return pinned[i] ? pinned[i] : pageable[i].data(); }
+};
+
+// Save: while a helper thread writes chunk k to the file, the device packs and
+// copies chunk k+1 into the other buffer.
 int write_pool(kvcache* c, int fd) {
   kvcu_pool_desc desc;
   int rc = kvcu_pool_describe(c->pool, &desc);
   if (rc) return rc;
-  std::vector<uint8_t> buf(std::min<uint64_t>(kIoChunk, std::max<uint64_t>(desc.checkpoint_bytes, 1)));
-  for (uint64_t off = 0; off < desc.checkpoint_bytes; off += buf.size()) {
-    const uint64_t n = std::min<uint64_t>(buf.size(), desc.checkpoint_bytes - off);
-    rc = kvcu_pool_read_checkpoint(c->pool, off, n, buf.data(), c->stream);
-    if (!rc) rc = write_all(fd, buf.data(), n);
-    if (rc) return rc;
+  const uint64_t total = desc.checkpoint_bytes;
+  const size_t chunk = (size_t)std::min<uint64_t>(kIoChunk, std::max<uint64_t>(total, 1));
+  IoBuffers bufs(chunk);
+  std::thread writer;
+  int wrc = KVCU_OK;
+  uint64_t k = 0;
+  for (uint64_t off = 0; off < total; off += chunk, ++k) {
+    const uint64_t n = std::min<uint64_t>(chunk, total - off);
+    uint8_t* b = bufs[(int)(k & 1)];
+    rc = kvcu_pool_read_checkpoint(c->pool, off, n, b, c->stream);  // returns with b filled
+    if (writer.joinable()) writer.join();  // chunk k-1, in the other buffer, is written
+    if (rc || wrc) break;
+    writer = std::thread([&wrc, fd, b, n]() { wrc = write_all(fd, b, n); });
   }
-  return KVCU_OK;
+  if (writer.joinable()) writer.join();
+  if (!rc && wrc) kvcu_set_error("checkpoint write failed");
+  return rc ? rc : wrc;
 }
 
+// Load: while chunk k goes to the device, a helper thread reads chunk k+1 from
+// the file into the other buffer.
 int read_pool(kvcache* c, int fd) {
   kvcu_pool_desc desc;
   int rc = kvcu_pool_describe(c->pool, &desc);
   if (rc) return rc;
-  std::vector<uint8_t> buf(std::min<uint64_t>(kIoChunk, std::max<uint64_t>(desc.checkpoint_bytes, 1)));
-  for (uint64_t off = 0; off < desc.checkpoint_bytes; off += buf.size()) {
-    const uint64_t n = std::min<uint64_t>(buf.size(), desc.checkpoint_bytes - off);
-    rc = read_no_eof(fd, buf.data(), n);
-    if (!rc) rc = kvcu_pool_write_checkpoint(c->pool, off, n, buf.data(), c->stream);
+  const uint64_t total = desc.checkpoint_bytes;
+  if (!total) return KVCU_OK;
+  const size_t chunk = (size_t)std::min<uint64_t>(kIoChunk, total);
+  IoBuffers bufs(chunk);
+  rc = read_no_eof(fd, bufs[0], (size_t)std::min<uint64_t>(chunk, total));
+  if (rc) return rc;
+  int rrc = KVCU_OK;
+  uint64_t k = 0;
+  for (uint64_t off = 0; off < total; off += chunk, ++k) {
+    const uint64_t n = std::min<uint64_t>(chunk, total - off);
+    std::thread reader;
+    if (off + chunk < total) {
+      uint8_t* nb = bufs[(int)((k + 1) & 1)];
+      const uint64_t nn = std::min<uint64_t>(chunk, total - off - chunk);
+      reader = std::thread([&rrc, fd, nb, nn]() { rrc = read_no_eof(fd, nb, nn); });
+    }
+    rc = kvcu_pool_write_checkpoint(c->pool, off, n, bufs[(int)(k & 1)], c->stream);
+    if (reader.joinable()) reader.join();
     if (rc) return rc;
+    if (rrc) {
+      kvcu_set_error("checkpoint truncated or unreadable");
+      return rrc;
+    }
   }
   return KVCU_OK;
 }

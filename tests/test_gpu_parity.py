@@ -499,6 +499,27 @@ def test_checkpoint_v2_roundtrip(kv, oracle, tmp_path):
     assert np.array_equal(c.mlaDecode(0, q, ids, SCALE), d.mlaDecode(0, q, ids, SCALE))
 
 
+@pytest.mark.parametrize("quant,nb,bs,lens", [(True, 4096, 64, [60000, 70000, 50000]),
+                                              (False, 2048, 16, [12000, 9000, 9000])])
+def test_checkpoint_v2_roundtrip_multi_chunk(kv, tmp_path, quant, nb, bs, lens):
+    """Pools larger than the 64 MB I/O chunk (160 MB Q8_0, 75 MB f32): the pipelined save
+    and load give back the same bytes."""
+    c = kv.KVCache.with_blocks(1, R, P, nb, bs, quantized=quant)
+    for _ in range(len(lens) - 1):
+        c.seq_create()
+    ids = np.arange(len(lens), dtype=np.uint32)
+    for s, L in enumerate(lens):
+        c.seq_ensure_capacity(s, L)
+    c.prefill_synthetic(0, ids, np.array(lens), 3, 0.01)
+    path = tmp_path / "big.kvck"
+    c.saveToFileV2(path)
+    d = kv.KVCache.with_blocks(1, R, P, nb, bs, quantized=quant)
+    d.loadFromFileV2(path)
+    assert [d.seq_len(s) for s in range(len(lens))] == lens
+    assert d.pool().read_checkpoint() == c.pool().read_checkpoint()
+    assert np.array_equal(d.gather(0, 2), c.gather(0, 2))
+
+
 # ------------------------------------------------------------------ bad indices set the status word
 def test_bad_table_entries_set_status_without_fault(kv, torch_mod):
     torch = torch_mod
