@@ -11,6 +11,7 @@
 // one warp owns one 32-element Q8_0 block (one 128-byte coalesced f32 read,
 // one 32-byte int8 write, a 5-step shuffle max), grids are sized in multiples
 // of the SM count and loop grid-stride.
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include "kvcu_internal.h"
@@ -181,7 +182,9 @@ __global__ void __launch_bounds__(256) k_append_rows(PoolArgs a, uint32_t n_rows
         }
         if (act) {
           *reinterpret_cast<char4*>(a.qs + row * (32u * nblk) + 32u * b + 4u * sub) = q;
-          if (sub == 0) a.sc[row * nblk + b] = kvcu::f32_to_f16(d);
+          // the hardware RNE conversion gives the same bits as f32_to_f16 for
+          // every non-NaN d (normal, subnormal, overflow to inf)
+          if (sub == 0) a.sc[row * nblk + b] = d == d ? __half_as_ushort(__float2half_rn(d)) : kvcu::f32_to_f16(d);
         }
       } else if (act) {
         float* dst = b < a.nbk ? a.kv + row * a.kv_rank + 32u * b + 4u * sub

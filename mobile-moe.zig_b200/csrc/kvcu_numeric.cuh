@@ -112,13 +112,15 @@ __device__ __forceinline__ int8_t q8_value(float x, float d) {
 
 // q8_value through a multiply: t = x * inv with inv = RN(1/d) lies within
 // |x/d| * 2^-22 <= 3.1e-5 of RN(x/d) for |x/d| <= 128, so both round to the
-// same integer unless t is within that distance of a half-integer; there (and
-// for NaN / inf) the IEEE quotient decides.  Same results as q8_value.
+// same integer unless t is within 1e-4 of a half-integer; there (and for NaN /
+// inf) the IEEE quotient decides.  Away from half-integers, round-half-even
+// (rintf) and the reference's round-half-away agree.  For |x| <= amax of its
+// block (d = RN(amax/127)), |t| <= 127 * (1 + 3 * 2^-24), so the result needs
+// no clamp.  Same results as q8_value for such x.
 __device__ __forceinline__ int8_t q8_value_fast(float x, float d, float inv) {
   const float t = x * inv;
-  const float fr = fabsf(t - truncf(t));
-  if (!(fabsf(fr - 0.5f) > 1e-4f)) return q8_value(x, d);
-  const float r = fminf(fmaxf(roundf(t), -127.0f), 127.0f);
+  const float r = rintf(t);
+  if (!(fabsf(t - r) < 0.4999f)) return q8_value(x, d);
   return (int8_t)(int)r;
 }
 
