@@ -78,10 +78,21 @@ constexpr uint32_t OFF_VR = OFF_QD + 4 * QD_LAT_BYTES + 3072;  // 187392: V chun
 constexpr uint32_t OFF_P = OFF_VR + V_SLOTS * VCH_BYTES;        // P^T: 2 regions x [32][128 B]
 constexpr uint32_t OFF_MISC = OFF_P + 8192;                     // 228352
 // misc: mbarriers, then small words and arrays
-constexpr int B_KV_FULL = 0, B_KV_EMPTY = 2, B_QK_FULL = 4, B_QK_EMPTY = 7, B_V_FULL = 10,
-              B_V_EMPTY = 12, B_P_FULL = 14, B_P_EMPTY = 15, B_PV_DONE = 16, B_PV_EMPTY = 17,
-              B_Q_FULL = 18, B_FINAL = 19, B_FINAL_PV = 20, B_EPI = 21 /* 2: one per head half */,
-              NUM_BARS = 23;
+// The raw stage is loaded and handed back in slices of whole V chunks.
+// Measured on config 5 (block size 64): 64-row slices with early hand-back
+// 3.78 G ctx-tok/s, one 128-row slice 3.74 G, 32-row 3.59 G, 16-row 2.19 G
+// (TMA boxes under 32 rows cost more per byte than they save in waiting).
+constexpr uint32_t SLICE = 64;
+constexpr int NSL = TILE / SLICE;
+constexpr uint32_t CPS = SLICE / VCH;  // V chunks per slice
+constexpr uint32_t ROW_BYTES = 4u * 128u + 64u + 36u;  // latent + rope + scales
+static_assert(SLICE % VCH == 0 && TILE % SLICE == 0, "a slice is a whole number of V chunks");
+constexpr int B_KV_FULL = 0, B_SL_EMPTY = 2 /* 2 stages x NSL slices */, B_QK_FULL = 2 + 2 * NSL,
+              B_QK_EMPTY = B_QK_FULL + QK_GROUPS, B_V_FULL = B_QK_EMPTY + QK_GROUPS,
+              B_V_EMPTY = B_V_FULL + V_SLOTS, B_P_FULL = B_V_EMPTY + V_SLOTS, B_P_EMPTY = B_P_FULL + 1,
+              B_PV_DONE = B_P_EMPTY + 1, B_PV_EMPTY = B_PV_DONE + 1, B_Q_FULL = B_PV_EMPTY + 1,
+              B_FINAL = B_Q_FULL + 1, B_FINAL_PV = B_FINAL + 1, B_EPI = B_FINAL_PV + 1 /* 2: one per head half */,
+              NUM_BARS = B_EPI + 2;
 static_assert(NUM_BARS * 8 <= 352, "mbarriers overlap the misc words");
 constexpr uint32_t OFF_TMEM_BASE = OFF_MISC + 352;            // u32
 constexpr uint32_t OFF_ABORT = OFF_MISC + 356;                // u32
@@ -420,10 +431,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 
   // ---- set-up: barriers, constant operands, TMEM
   if (threadIdx.x == 0) {
-    mbar_init(bar(B_KV_FULL + 0), 1);
-    mbar_init(bar(B_KV_FULL + 1), 1);
-    mbar_init(bar(B_KV_EMPTY + 0), 1 + 4 + EPI_WARPS);  // QK issuer commit + converter + epilogue
-    mbar_init(bar(B_KV_EMPTY + 1), 1 + 4 + EPI_WARPS);
+    mbar_init(bar(B_KV_FULL + 0), NSL);  // one arrival per slice, loaded or not
+    mbar_init(bar(B_KV_FULL + 1), NSL);
+    for (int i = 0; i < 2 * NSL; ++i) mbar_init(bar(B_SL_EMPTY + i), 4);  // the 4 converter warps
     for (int i = 0; i < QK_GROUPS; ++i) {
       mbar_init(bar(B_QK_FULL + i), 1);
       mbar_init(bar(B_QK_EMPTY + i), EPI_WARPS);
@@ -465,41 +475,57 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     setmaxnreg_dec<ISSUE_REGS>();
   if (warp == 0) {
     // ================================================================ producer
+    // Slice i of a tile is refilled as soon as the converter hands back the
+    // same slice of the tile two earlier, so the next tile streams in while
+    // this one's PV runs.  Every slice arrives once on the stage's full
+    // barrier, with its bytes, or with none past the item end.
     if (lane == 0) {
-      uint32_t g = 0;
+      uint32_t g = 0;  // tiles whose NSL arrivals are all made
+      bool live = true;
       const uint32_t br = a.box_rows;
-      for (uint32_t it = it_begin; it < it_end && !*abort_flag; ++it) {
+      for (uint32_t it = it_begin; it < it_end && live; ++it) {
         const Item im = load_item(a, it);
-        for (uint32_t k = 0; k < im.ntiles && !*abort_flag; ++k, ++g) {
+        for (uint32_t k = 0; k < im.ntiles && live; ++k) {
           const uint32_t s = g & 1u;
-          if (!mbar_wait(bar(B_KV_EMPTY + s), ((g >> 1) & 1u) ^ 1u, abort_flag, a.status)) break;
           const uint32_t tt0 = im.tok0 + k * TILE;
           const uint32_t tt1 = min(tt0 + TILE, im.tok1);
-          // every segment is one box of br rows inside one physical block (the
-          // plan aligns items to max(128, block size); anything else is refused)
-          uint32_t bytes = 0;
-          for (uint32_t off = 0; tt0 + off < tt1; off += br) {
-            const uint32_t pos = tt0 + off;
-            const uint32_t blk = a.tables[im.t0 + pos / a.block_size];
-            if (blk >= a.num_blocks) atomicOr(a.status, KVCU_STATUS_BAD_BLOCK);
-            else if (pos % a.block_size + br > a.block_size) atomicOr(a.status, KVCU_STATUS_MISALIGNED);
-            else bytes += br * (4u * 128u + 64u + 36u);
-          }
           const uint32_t stage = sbase + s * STAGE_BYTES;
-          mbar_arrive_tx(bar(B_KV_FULL + s), bytes);
-          for (uint32_t off = 0; tt0 + off < tt1; off += br) {
-            const uint32_t pos = tt0 + off;
-            const uint32_t blk = a.tables[im.t0 + pos / a.block_size];
-            if (blk >= a.num_blocks || pos % a.block_size + br > a.block_size) continue;
-            const uint64_t row =
-                ((uint64_t)a.layer * a.num_blocks + blk) * a.block_size + pos % a.block_size;
+          const uint32_t full = bar(B_KV_FULL + s);
+          bool started = false;
+#pragma unroll 1
+          for (uint32_t i = 0; i < (uint32_t)NSL; ++i) {
+            if (live && !mbar_wait(bar(B_SL_EMPTY + NSL * s + i), ((g >> 1) & 1u) ^ 1u, abort_flag, a.status))
+              live = false;
+            // Stop before the first slice; after it, the remaining slices still
+            // arrive (without bytes) so that the drain below sees the phase end.
+            if (!live && !started) break;
+            started = true;
+            // every segment is one box of br rows inside one physical block (the
+            // plan aligns items to max(128, block size); anything else is refused)
+            uint32_t bytes = 0;
+            for (uint32_t off = i * SLICE; live && off < (i + 1) * SLICE && tt0 + off < tt1; off += br) {
+              const uint32_t pos = tt0 + off;
+              const uint32_t blk = a.tables[im.t0 + pos / a.block_size];
+              if (blk >= a.num_blocks) atomicOr(a.status, KVCU_STATUS_BAD_BLOCK);
+              else if (pos % a.block_size + br > a.block_size) atomicOr(a.status, KVCU_STATUS_MISALIGNED);
+              else bytes += br * ROW_BYTES;
+            }
+            mbar_arrive_tx(full, bytes);
+            for (uint32_t off = i * SLICE; bytes && off < (i + 1) * SLICE && tt0 + off < tt1; off += br) {
+              const uint32_t pos = tt0 + off;
+              const uint32_t blk = a.tables[im.t0 + pos / a.block_size];
+              if (blk >= a.num_blocks || pos % a.block_size + br > a.block_size) continue;
+              const uint64_t row =
+                  ((uint64_t)a.layer * a.num_blocks + blk) * a.block_size + pos % a.block_size;
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-              tma_load_2d(stage + ST_LAT + (uint32_t)j * 16384u + off * 128u, &map_lat, j * 128, (int)row,
-                          bar(B_KV_FULL + s));
-            tma_load_2d(stage + ST_ROPE + off * 64u, &map_rope, 512, (int)row, bar(B_KV_FULL + s));
-            bulk_load(stage + ST_SC + off * 36u, a.sc + row * NBLK, br * 36u, bar(B_KV_FULL + s));
+              for (int j = 0; j < 4; ++j)
+                tma_load_2d(stage + ST_LAT + (uint32_t)j * 16384u + off * 128u, &map_lat, j * 128, (int)row,
+                            full);
+              tma_load_2d(stage + ST_ROPE + off * 64u, &map_rope, 512, (int)row, full);
+              bulk_load(stage + ST_SC + off * 36u, a.sc + row * NBLK, br * 36u, full);
+            }
           }
+          if (started) ++g;
         }
       }
       // wait (bounded) for the copies of the last two stages to land
@@ -552,8 +578,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           __syncwarp();
         }
         if (!ok) break;
-        if (elect_one()) mma_commit(bar(B_KV_EMPTY + s));  // the raw stage's int8 rows are no longer read
-        __syncwarp();
       }
       ++item_no;
     }
@@ -710,7 +734,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const uint32_t s = g & 1u;
         const uint32_t tt0 = im.tok0 + k * TILE;
         const bool valid = tt0 + trow < im.tok1;
-        // raw stage s holds this tile's block scales
+        // raw stage s holds this tile's block scales (read before this tile's P
+        // is published; the converter hands the stage back after that)
         if (!mbar_wait(bar(B_KV_FULL + s), (g >> 1) & 1u, abort_flag, a.status)) {
           ok = false;
           break;
@@ -767,8 +792,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           }
         }
         if (!ok) break;
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(B_KV_EMPTY + s));  // done with the stage's scales
         // ---- online softmax over the tile (log2 domain)
         float sc[HH];
 #pragma unroll
@@ -973,6 +996,17 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             ok = false;
             break;
           }
+          // From chunk 2 on, this slot was freed by a PV MMA of this tile, so
+          // the epilogue has published the tile's P: it has read the stage's
+          // scales and waited for the QK MMAs.  The raw rows of the chunks read
+          // so far (into registers) go back to the producer.
+          // Slices [lo, hi) are whole after chunk c and were not handed back yet.
+          const uint32_t lo = c == 2 ? 0u : c / CPS, hi = c >= 2 ? (c + 1) / CPS : 0u;
+          if (hi > lo) {
+            __syncwarp();
+            if (lane == 0)
+              for (uint32_t j = lo; j < hi; ++j) mbar_arrive(bar(B_SL_EMPTY + NSL * s + j));
+          }
           // unit mt of the chunk: MN atom j/4, chunks 2(j%4), 2(j%4)+1 of atom row t%8, K atom t/8
           uint8_t* vrow = smem + OFF_VR + vs * VCH_BYTES + (j >> 2) * 2048u + (tl >> 3) * 1024u + (tl & 7u) * 128u;
           const uint32_t ch0 = 2u * (j & 3u);
@@ -988,8 +1022,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           if (lane == 0) mbar_arrive(bar(B_V_FULL + vs));
         }
         if (!ok) break;
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(B_KV_EMPTY + s));
       }
     }
   }
@@ -1092,7 +1124,8 @@ int kvcu_launch_decode_tc(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint
                           const uint32_t* seq_ids, uint32_t n_seqs, const uint32_t* toff,
                           const uint32_t* tables, const uint32_t* lens, const float* q,
                           uint32_t n_heads, float scale, float* out, float* lse, cudaStream_t st) {
-  const uint32_t box_rows = p->block_size < (uint32_t)TILE ? p->block_size : (uint32_t)TILE;
+  // one box per slice, or per block where blocks are smaller than a slice
+  const uint32_t box_rows = p->block_size < SLICE ? p->block_size : SLICE;
   CUtensorMap lat, rope;
   int rc = make_maps(p, box_rows, &lat, &rope);
   if (rc) return rc;
