@@ -67,7 +67,8 @@ constexpr float RESCALE_LOG2 = 8.0f;         // lazy rescale threshold (factor 2
 constexpr uint32_t STATUS_TIMEOUT = KVCU_STATUS_TIMEOUT;
 
 // ---- shared memory map (offsets from a 1024-aligned base) ----
-constexpr uint32_t ST_LAT = 0;                   // 4 x [128 rows][128 B], SW128
+constexpr uint32_t ST_LAT = 0;                   // [16 row groups][4 column chunks][8 rows][128 B], SW128
+constexpr uint32_t LAT_GROUP = 4096;             // bytes per 8-row group (the QK A operand's SBO)
 constexpr uint32_t ST_ROPE = 4 * 16384;          // [128 rows][64 B], SW64
 constexpr uint32_t ST_SC = ST_ROPE + 8192;       // [128][18] u16 scales
 constexpr uint32_t STAGE_BYTES = 79872;          // 78,336 rounded up to 1024
@@ -230,6 +231,15 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+// 4-D tile: coordinates innermost first
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int x, int y, int z, int w,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(bar)
       : "memory");
 }
 __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
@@ -517,10 +527,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
               if (blk >= a.num_blocks || pos % a.block_size + br > a.block_size) continue;
               const uint64_t row =
                   ((uint64_t)a.layer * a.num_blocks + blk) * a.block_size + pos % a.block_size;
-#pragma unroll
-              for (int j = 0; j < 4; ++j)
-                tma_load_2d(stage + ST_LAT + (uint32_t)j * 16384u + off * 128u, &map_lat, j * 128, (int)row,
-                            full);
+              // the segment's whole latent (4 column chunks) in one box
+              tma_load_4d(stage + ST_LAT + (off >> 3) * LAT_GROUP, &map_lat, 0, 0, 0, (int)(row >> 3), full);
               tma_load_2d(stage + ST_ROPE + off * 64u, &map_rope, 512, (int)row, full);
               bulk_load(stage + ST_SC + off * 36u, a.sc + row * NBLK, br * 36u, full);
             }
@@ -564,7 +572,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
               const uint32_t b = GB * gi + e;
               uint64_t ad, bd;
               if (b < 16) {
-                ad = smem_desc(stage + ST_LAT + (b >> 2) * 16384u + (b & 3u) * 32u, 16, 1024, LAYOUT_SW128);
+                ad = smem_desc(stage + ST_LAT + (b >> 2) * 1024u + (b & 3u) * 32u, 16, LAT_GROUP, LAYOUT_SW128);
                 bd = smem_desc(sbase + OFF_QD + (b >> 2) * QD_LAT_BYTES + (b & 3u) * 32u, 16, 1024,
                                LAYOUT_SW128);
               } else {
@@ -971,7 +979,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           uint16_t dsc[4];
 #pragma unroll
           for (uint32_t mt = 0; mt < 4; ++mt) {
-            raw[mt] = *reinterpret_cast<const uint4*>(stage + ST_LAT + mt * 16384u + sw128_off(t, j * 16u));
+            raw[mt] = *reinterpret_cast<const uint4*>(stage + ST_LAT + (t >> 3) * LAT_GROUP + mt * 1024u +
+                                                      sw128_off(t & 7u, j * 16u));
             dsc[mt] = *reinterpret_cast<const uint16_t*>(stage + ST_SC + t * 36u + (4u * mt + (j >> 1)) * 2u);
           }
           uint32_t hv[4][8];
@@ -1063,10 +1072,16 @@ int make_maps(const kvcu_pool* p, uint32_t box_rows, CUtensorMap* lat, CUtensorM
   const uint64_t rows = p->rows();
   const cuuint64_t dims[2] = {(cuuint64_t)W, (cuuint64_t)rows};
   const cuuint64_t strides[1] = {(cuuint64_t)W};
-  const cuuint32_t estr[2] = {1, 1};
-  const cuuint32_t box_lat[2] = {128, box_rows};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
   const cuuint32_t box_rope[2] = {64, box_rows};
-  CUresult r = enc(lat, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, p->qs, dims, strides, box_lat, estr,
+  // Latent as (byte in chunk, row in group, 128 B chunk, 8-row group), so one
+  // box lands as [group][chunk][8 rows x 128 B]: the 128B-swizzled K-major
+  // layout of all four chunks, 4096 B per 8-row group.  Rows are a multiple of
+  // 16 (the block size is), so the groups tile the pool exactly.
+  const cuuint64_t dims_lat[4] = {128, 8, 4, (cuuint64_t)(rows / 8)};
+  const cuuint64_t strides_lat[3] = {(cuuint64_t)W, 128, 8 * (cuuint64_t)W};
+  const cuuint32_t box_lat[4] = {128, 8, 4, box_rows / 8};
+  CUresult r = enc(lat, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, p->qs, dims_lat, strides_lat, box_lat, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
