@@ -97,6 +97,8 @@ constexpr int B_KV_FULL = 0, B_SL_EMPTY = 2 /* 2 stages x NSL slices */, B_QK_FU
 static_assert(NUM_BARS * 8 <= 352, "mbarriers overlap the misc words");
 constexpr uint32_t OFF_TMEM_BASE = OFF_MISC + 352;            // u32
 constexpr uint32_t OFF_ABORT = OFF_MISC + 356;                // u32
+constexpr uint32_t OFF_CUR_ITEM = OFF_MISC + 360;             // u32: the epilogue's current item
+constexpr uint32_t ITEMS_DONE = 0xFFFFFFFFu;
 constexpr uint32_t OFF_ONES = OFF_MISC + 384;                 // 128 B of f16 1.0 (l = ones x P^T)
 constexpr uint32_t OFF_QSCALE = OFF_MISC + 512;               // float[24]
 constexpr uint32_t OFF_REDMAX = OFF_MISC + 640;               // float[2][8 warps][24]
@@ -241,6 +243,9 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
       " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(bar)
       : "memory");
+}
+__device__ __forceinline__ void prefetch_l2_keep(const void* p) {
+  asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(p));
 }
 __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
   asm volatile(
@@ -462,6 +467,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     mbar_init(bar(B_EPI + 0), EPI_WARPS / 2);
     mbar_init(bar(B_EPI + 1), EPI_WARPS / 2);
     *abort_flag = 0u;
+    *reinterpret_cast<volatile uint32_t*>(smem + OFF_CUR_ITEM) = it_begin;
     uint32_t* ones = reinterpret_cast<uint32_t*>(smem + OFF_ONES);
     for (int i = 0; i < 32; ++i) ones[i] = 0x3C003C00u;  // f16 1.0 pairs
     fence_proxy_async();
@@ -648,7 +654,33 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     if (elect_one()) mma_commit(bar(B_FINAL_PV));
     __syncwarp();
     mbar_wait_drain(bar(B_FINAL_PV), 0, a.status);
-  }  // warp 3: spare warp of the issue warpgroup
+  } else {
+    // ================================================================ query prefetcher
+    // While the epilogue runs item n, pull item n+1's query into L2 (kept
+    // against the KV stream), so that its staging does not wait on a cold read:
+    // DRAM, or PCIe when q is in mapped host memory.  Best effort: the poll is
+    // bounded and gives up quietly, it never aborts the CTA.
+    const volatile uint32_t* cur = reinterpret_cast<const volatile uint32_t*>(smem + OFF_CUR_ITEM);
+    const long long t0 = clock64();
+    for (uint32_t nx = it_begin + 1; nx < it_end; ++nx) {
+      bool go = false;
+      while (true) {
+        const uint32_t c = *cur;
+        if (c == ITEMS_DONE || *abort_flag) break;
+        if (c + 1u >= nx) {
+          go = true;
+          break;
+        }
+        if (clock64() - t0 > (1ll << 32)) break;
+        __nanosleep(256);
+      }
+      if (!go) break;
+      const Item im = load_item(a, nx);
+      if (im.ntiles == 0) continue;
+      const uint8_t* qb = reinterpret_cast<const uint8_t*>(a.q + (uint64_t)im.b * H * W);
+      for (uint32_t off = lane * 128u; off < H * (uint32_t)W * 4u; off += 32u * 128u) prefetch_l2_keep(qb + off);
+    }
+  }
   } else if (warp < 12) {
     setmaxnreg_inc<EPI_REGS>();
     // ================================================================ epilogue
@@ -671,7 +703,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       ++esync;
       return r;
     };
+    volatile uint32_t* cur_item = reinterpret_cast<volatile uint32_t*>(smem + OFF_CUR_ITEM);
     for (uint32_t it = it_begin; it < it_end && ok; ++it) {
+      if (ew == 0 && lane == 0) *cur_item = it;
       const Item im = load_item(a, it);
       const bool single = a.seq_count[im.b] == 1;
       if (im.ntiles == 0) {
@@ -949,6 +983,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         if (lane == 0) mbar_arrive(bar(B_PV_EMPTY));
       }
     }
+    if (ew == 0 && lane == 0) *cur_item = ITEMS_DONE;
   } else {
     setmaxnreg_dec<CVT_REGS>();
     // ================================================================ converter
