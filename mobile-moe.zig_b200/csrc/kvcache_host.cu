@@ -176,6 +176,14 @@ void* mapped_host_range(const void* p, size_t bytes) {
 
 }  // namespace
 
+// A pinned host buffer that feeds one asynchronous upload at a time: `done`
+// is recorded after the copy, and the buffer is refilled only once it fired.
+struct HostStage {
+  uint32_t* p = nullptr;
+  size_t cap = 0;
+  cudaEvent_t done = nullptr;
+};
+
 struct kvcache {
   int device = 0;
   uint32_t n_layers = 0, kv_rank = 0, rope_dim = 0, num_blocks = 0, block_size = 0;
@@ -195,6 +203,8 @@ struct kvcache {
   size_t d_lens_cap = 0;
   bool tables_dirty = true, lens_dirty = true;
   std::vector<uint32_t> h_toff;
+  // pinned staging of the table / length uploads (truly asynchronous copies)
+  HostStage up_toff, up_tables, up_lens;
   // scratch for host-buffer calls
   float* d_f = nullptr;
   size_t d_f_cap = 0;
@@ -225,40 +235,83 @@ struct kvcache {
 
 namespace {
 
-int sync_tables(kvcache* c) {
-  if (!c->tables_dirty) return KVCU_OK;
-  c->h_toff.assign(c->seqs.size() + 1, 0);
-  size_t total = 0;
-  for (size_t s = 0; s < c->seqs.size(); ++s) {
-    c->h_toff[s] = (uint32_t)total;
-    total += c->seqs[s].table.size();
+// Make h.p hold at least n words, once the previous upload from it has run
+// (an event wait, normally long satisfied: the host stays ahead of the GPU).
+int stage_acquire(HostStage& h, size_t n) {
+  if (!h.done) KVCU_CUDA(cudaEventCreateWithFlags(&h.done, cudaEventDisableTiming));
+  else KVCU_CUDA(cudaEventSynchronize(h.done));
+  if (n > h.cap) {
+    if (h.p) KVCU_CUDA(cudaFreeHost(h.p));
+    h.p = nullptr;
+    h.cap = 0;
+    const size_t cap = std::max<size_t>(n + n / 4, 1024);
+    KVCU_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&h.p), cap * 4, cudaHostAllocDefault));
+    h.cap = cap;
   }
-  c->h_toff[c->seqs.size()] = (uint32_t)total;
-  std::vector<uint32_t> flat;
-  flat.reserve(total + 1);
-  for (auto& s : c->seqs) flat.insert(flat.end(), s.table.begin(), s.table.end());
-  if (flat.empty()) flat.push_back(0);
-  int rc = ensure_dev(&c->d_toff, &c->d_toff_cap, c->h_toff.size());
-  if (!rc) rc = ensure_dev(&c->d_tables, &c->d_tables_cap, flat.size());
+  return KVCU_OK;
+}
+
+int stage_upload(HostStage& h, uint32_t* dst, size_t n, cudaStream_t st) {
+  KVCU_CUDA(cudaMemcpyAsync(dst, h.p, n * 4, cudaMemcpyHostToDevice, st));
+  KVCU_CUDA(cudaEventRecord(h.done, st));
+  return KVCU_OK;
+}
+
+void stage_free(HostStage& h) {
+  if (h.done) {
+    cudaEventSynchronize(h.done);
+    cudaEventDestroy(h.done);
+  }
+  if (h.p) cudaFreeHost(h.p);
+  h = HostStage{};
+}
+
+// Block tables (CSR by sequence id) to the device, ordered on `st` before the
+// kernels that read them.  Pinned staging: no stream drain on the host.
+int sync_tables(kvcache* c, cudaStream_t st) {
+  // a clean mirror may still be in flight on another stream: order `st` after it
+  if (!c->tables_dirty) return c->up_tables.done ? kvcu_check_cuda(cudaStreamWaitEvent(st, c->up_tables.done, 0),
+                                                                   "cudaStreamWaitEvent(tables)")
+                                                 : KVCU_OK;
+  const size_t nseq = c->seqs.size();
+  size_t total = 0;
+  for (size_t s = 0; s < nseq; ++s) total += c->seqs[s].table.size();
+  const size_t nflat = std::max<size_t>(total, 1);
+  int rc = stage_acquire(c->up_toff, nseq + 1);
+  if (!rc) rc = stage_acquire(c->up_tables, nflat);
+  if (!rc) rc = ensure_dev(&c->d_toff, &c->d_toff_cap, nseq + 1);
+  if (!rc) rc = ensure_dev(&c->d_tables, &c->d_tables_cap, nflat);
   if (rc) return rc;
-  KVCU_CUDA(cudaMemcpyAsync(c->d_toff, c->h_toff.data(), c->h_toff.size() * 4,
-                            cudaMemcpyHostToDevice, c->stream));
-  KVCU_CUDA(cudaMemcpyAsync(c->d_tables, flat.data(), flat.size() * 4, cudaMemcpyHostToDevice,
-                            c->stream));
-  KVCU_CUDA(cudaStreamSynchronize(c->stream));  // `flat` dies at return
+  uint32_t* toff = c->up_toff.p;
+  uint32_t* flat = c->up_tables.p;
+  size_t o = 0;
+  for (size_t s = 0; s < nseq; ++s) {
+    const auto& t = c->seqs[s].table;
+    toff[s] = (uint32_t)o;
+    if (!t.empty()) memcpy(flat + o, t.data(), t.size() * 4);
+    o += t.size();
+  }
+  toff[nseq] = (uint32_t)o;
+  if (total == 0) flat[0] = 0;
+  c->h_toff.assign(toff, toff + nseq + 1);
+  rc = stage_upload(c->up_toff, c->d_toff, nseq + 1, st);
+  if (!rc) rc = stage_upload(c->up_tables, c->d_tables, nflat, st);
+  if (rc) return rc;
   c->tables_dirty = false;
   return KVCU_OK;
 }
 
-int sync_lens(kvcache* c) {
-  if (!c->lens_dirty) return KVCU_OK;
-  std::vector<uint32_t> lens(c->seqs.size());
-  for (size_t s = 0; s < c->seqs.size(); ++s) lens[s] = c->seqs[s].len;
-  int rc = ensure_dev(&c->d_lens, &c->d_lens_cap, lens.size());
+int sync_lens(kvcache* c, cudaStream_t st) {
+  if (!c->lens_dirty) return c->up_lens.done ? kvcu_check_cuda(cudaStreamWaitEvent(st, c->up_lens.done, 0),
+                                                               "cudaStreamWaitEvent(lens)")
+                                             : KVCU_OK;
+  const size_t nseq = c->seqs.size();
+  int rc = stage_acquire(c->up_lens, std::max<size_t>(nseq, 1));
+  if (!rc) rc = ensure_dev(&c->d_lens, &c->d_lens_cap, nseq);
   if (rc) return rc;
-  KVCU_CUDA(cudaMemcpyAsync(c->d_lens, lens.data(), lens.size() * 4, cudaMemcpyHostToDevice,
-                            c->stream));
-  KVCU_CUDA(cudaStreamSynchronize(c->stream));
+  for (size_t s = 0; s < nseq; ++s) c->up_lens.p[s] = c->seqs[s].len;
+  rc = stage_upload(c->up_lens, c->d_lens, nseq, st);
+  if (rc) return rc;
   c->lens_dirty = false;
   return KVCU_OK;
 }
@@ -399,8 +452,8 @@ struct DevScope {
 int append_host_rows(kvcache* c, uint32_t layer, uint32_t n, const uint32_t* seq_ids,
                      const uint32_t* positions, const float* rows) {
   const uint32_t Wd = c->row_width();
-  int rc = sync_tables(c);
-  if (!rc) rc = sync_lens(c);
+  int rc = sync_tables(c, c->stream);
+  if (!rc) rc = sync_lens(c, c->stream);
   if (!rc) rc = ensure_dev(&c->d_f, &c->d_f_cap, (size_t)n * Wd);
   if (!rc) rc = ensure_dev(&c->d_u, &c->d_u_cap, (size_t)2 * n);
   if (rc) return rc;
@@ -487,7 +540,7 @@ int get_row(kvcache* c, uint32_t layer, uint32_t pos, float* kv_out, float* pe_o
     return KVCU_ERR_POSITION_OOB;
   }
   const uint32_t Wd = c->row_width();
-  int rc = sync_tables(c);
+  int rc = sync_tables(c, c->stream);
   if (!rc) rc = ensure_dev(&c->d_f, &c->d_f_cap, Wd);
   if (!rc) rc = ensure_dev(&c->d_u, &c->d_u_cap, 2);
   if (rc) return rc;
@@ -532,8 +585,8 @@ int decode_impl(kvcache* c, uint32_t layer, uint32_t n, const uint32_t* seq_ids,
       return KVCU_ERR_INVALID_ARG;
     }
   int rc = ensure_ws(c, n, n_heads);
-  if (!rc) rc = sync_tables(c);
-  if (!rc) rc = sync_lens(c);
+  if (!rc) rc = sync_tables(c, st);
+  if (!rc) rc = sync_lens(c, st);
   if (rc) return rc;
   uint32_t launches = 0;
   // Re-plan when the batch changed, a sequence shrank, or the tokens grew by
@@ -594,6 +647,9 @@ void kvcache_deinit(kvcache* c) {
   cudaFree(c->d_step);
   cudaFree(c->d_stepu);
   cudaFree(c->d_seq_ids);
+  stage_free(c->up_toff);
+  stage_free(c->up_tables);
+  stage_free(c->up_lens);
   if (c->stream) cudaStreamDestroy(c->stream);
   delete c;
 }
@@ -809,8 +865,8 @@ int kvcache_append_batch_dev(kvcache* c, uint32_t layer, uint32_t n, const uint3
   DevScope d(c->device);
   int rc = validate_positions(c, layer, n, seq_ids, positions);
   if (!rc) rc = cow_for_write(c, n, seq_ids, positions, (cudaStream_t)stream);
-  if (!rc) rc = sync_tables(c);
-  if (!rc) rc = sync_lens(c);
+  if (!rc) rc = sync_tables(c, (cudaStream_t)stream);
+  if (!rc) rc = sync_lens(c, (cudaStream_t)stream);
   if (rc) return rc;
   const uint32_t Wd = c->row_width();
   rc = kvcu_append(c->pool, layer, n, rows_dev, Wd, rows_dev + c->kv_rank, Wd, seq_ids_dev,
@@ -830,7 +886,7 @@ int kvcache_gather(kvcache* c, uint32_t layer, uint32_t seq, float* out) {
   if (q.len == 0) return KVCU_OK;
   if (!out) return KVCU_ERR_INVALID_ARG;
   const uint32_t Wd = c->row_width();
-  int rc = sync_tables(c);
+  int rc = sync_tables(c, c->stream);
   if (!rc) rc = ensure_dev(&c->d_f, &c->d_f_cap, (size_t)q.len * Wd);
   if (rc) return rc;
   rc = kvcu_gather(c->pool, layer, c->d_tables + c->h_toff[seq], (uint32_t)q.table.size(), q.len,
@@ -896,8 +952,8 @@ int kvcache_mla_step_dev(kvcache* c, uint32_t layer, uint32_t n, const uint32_t*
   const size_t q_abs_n = (size_t)n * n_heads * Wd, rows_n = (size_t)n * Wd, lat_n = (size_t)n * n_heads * R;
   rc = ensure_dev(&c->d_step, &c->d_step_cap, q_abs_n + rows_n + lat_n + (size_t)n * n_heads);
   if (!rc) rc = ensure_dev(&c->d_stepu, &c->d_stepu_cap, 2 * (size_t)n + n_seqs);
-  if (!rc) rc = sync_tables(c);
-  if (!rc) rc = sync_lens(c);
+  if (!rc) rc = sync_tables(c, st);
+  if (!rc) rc = sync_lens(c, st);
   if (!rc) rc = ensure_ws(c, n, n_heads);
   if (rc) return rc;
   float* q_abs = c->d_step;
