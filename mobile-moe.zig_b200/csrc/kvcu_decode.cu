@@ -462,37 +462,76 @@ __global__ void __launch_bounds__(NT, 1) k_decode(DecodeArgs a) {
 
 // ------------------------------------------------------------------ combine
 // One CTA of 128 threads per (entry, head): merge the entry's partials.
-__global__ void __launch_bounds__(128) k_combine(uint32_t n, uint32_t H, uint32_t ws_heads,
-                                                 const uint32_t* __restrict__ seq_first,
-                                                 const uint32_t* __restrict__ seq_count,
-                                                 const float* __restrict__ part_o,
-                                                 const float* __restrict__ part_ml,
-                                                 float* __restrict__ out, float* __restrict__ lse) {
-  const uint32_t b = blockIdx.x / H, h = blockIdx.x % H;
-  if (b >= n) return;
-  const uint32_t cnt = seq_count[b];
-  if (cnt <= 1) return;  // written by the decode kernel
-  const uint32_t first = seq_first[b];
-  float m = -INFINITY;
-  for (uint32_t k = 0; k < cnt; ++k) m = fmaxf(m, part_ml[((uint64_t)(first + k) * ws_heads + h) * 2]);
-  float l = 0.f;
-  float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (uint32_t k = 0; k < cnt; ++k) {
-    const uint64_t base = (uint64_t)(first + k) * ws_heads + h;
-    const float mk = part_ml[base * 2], lk = part_ml[base * 2 + 1];
-    const float f = (lk > 0.f) ? expf(mk - m) : 0.f;
-    l += lk * f;
-    const float4 v = reinterpret_cast<const float4*>(part_o + base * R)[threadIdx.x];
-    o.x += v.x * f;
-    o.y += v.y * f;
-    o.z += v.z * f;
-    o.w += v.w * f;
+// One warp per (cut, head).  An entry split into several items has its second
+// item start exactly at the CTA range boundary of its first cut inside it
+// (ranges[c] == seq_first[b] + 1), so the cuts 1 .. G-1 enumerate the split
+// entries without a list; entries decoded as one item were written by the
+// decode kernel.  A fixed grid of warps strides over the (G-1) x H tasks.
+constexpr int COMBINE_WARPS = 4;
+__global__ void __launch_bounds__(32 * COMBINE_WARPS) k_combine(uint32_t H, uint32_t ws_heads,
+                                                                const uint32_t* __restrict__ meta,
+                                                                const uint32_t* __restrict__ ranges,
+                                                                const kvcu_item* __restrict__ items,
+                                                                const uint32_t* __restrict__ seq_first,
+                                                                const uint32_t* __restrict__ seq_count,
+                                                                const float* __restrict__ part_o,
+                                                                const float* __restrict__ part_ml,
+                                                                float* __restrict__ out, float* __restrict__ lse) {
+  const uint32_t n_items = meta[0], G = meta[1];
+  const uint32_t lane = threadIdx.x & 31u;
+  const uint32_t tasks = G > 1 ? (G - 1) * H : 0u;
+  for (uint32_t t = blockIdx.x * COMBINE_WARPS + (threadIdx.x >> 5); t < tasks;
+       t += gridDim.x * COMBINE_WARPS) {
+    const uint32_t c = 1 + t / H, h = t % H;
+    const uint32_t i = ranges[c];
+    if (i == 0 || i >= n_items) continue;
+    const uint32_t b = items[i].b;
+    const uint32_t cnt = seq_count[b], first = seq_first[b];
+    if (cnt <= 1 || first + 1 != i) continue;  // no split here, or not the entry's first cut
+    float m = -INFINITY;
+    for (uint32_t k = 0; k < cnt; ++k) m = fmaxf(m, part_ml[((uint64_t)(first + k) * ws_heads + h) * 2]);
+    float l = 0.f;
+    float4 o[R / 128];
+#pragma unroll
+    for (int j = 0; j < R / 128; ++j) o[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (uint32_t k = 0; k < cnt; ++k) {
+      const uint64_t base = (uint64_t)(first + k) * ws_heads + h;
+      const float mk = part_ml[base * 2], lk = part_ml[base * 2 + 1];
+      const float f = (lk > 0.f) ? expf(mk - m) : 0.f;
+      l += lk * f;
+      const float4* src = reinterpret_cast<const float4*>(part_o + base * R);
+#pragma unroll
+      for (int j = 0; j < R / 128; ++j) {
+        const float4 v = src[lane + 32 * j];
+        o[j].x += v.x * f;
+        o[j].y += v.y * f;
+        o[j].z += v.z * f;
+        o[j].w += v.w * f;
+      }
+    }
+    const float inv = l > 0.f ? 1.0f / l : 0.f;
+    float4* dst = reinterpret_cast<float4*>(out + ((uint64_t)b * H + h) * R);
+#pragma unroll
+    for (int j = 0; j < R / 128; ++j)
+      dst[lane + 32 * j] = l > 0.f ? make_float4(o[j].x * inv, o[j].y * inv, o[j].z * inv, o[j].w * inv)
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+    if (lse && lane == 0) lse[(uint64_t)b * H + h] = l > 0.f ? m + logf(l) : -INFINITY;
   }
-  const float inv = l > 0.f ? 1.0f / l : 0.f;
-  float4 r = make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv);
-  if (!(l > 0.f)) r = make_float4(0.f, 0.f, 0.f, 0.f);
-  reinterpret_cast<float4*>(out + ((uint64_t)b * H + h) * R)[threadIdx.x] = r;
-  if (lse && threadIdx.x == 0) lse[(uint64_t)b * H + h] = l > 0.f ? m + logf(l) : -INFINITY;
+}
+
+int launch_combine(kvcu_decode_ws* ws, uint32_t n_heads, float* out, float* lse, cudaStream_t st) {
+  // the plan makes at most min(max_ranges, decode CTAs) ranges
+  uint32_t G = ws->max_ranges;
+  if (ws->decode_ctas > 0 && (uint32_t)ws->decode_ctas < G) G = (uint32_t)ws->decode_ctas;
+  const uint32_t tasks = (G > 1 ? G - 1 : 1) * n_heads;
+  uint32_t grid = (tasks + COMBINE_WARPS - 1) / COMBINE_WARPS;
+  const uint32_t cap = 8u * (uint32_t)(ws->num_sms > 0 ? ws->num_sms : 148);
+  if (grid > cap) grid = cap;
+  if (grid == 0) grid = 1;
+  k_combine<<<grid, 32 * COMBINE_WARPS, 0, st>>>(n_heads, ws->max_heads, ws->meta, ws->ranges, ws->items,
+                                                 ws->seq_first, ws->seq_count, ws->part_o, ws->part_ml, out,
+                                                 lse);
+  return kvcu_check_cuda(cudaGetLastError(), "combine kernel launch");
 }
 
 size_t decode_smem(int nh) {
@@ -574,9 +613,7 @@ int kvcu_launch_decode(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint32_
     int rc = kvcu_launch_decode_tc(ws, p, layer, n, seq_ids, n_seqs, toff, tables, lens, q, n_heads,
                                    scale, out, lse, st);
     if (rc) return rc;
-    k_combine<<<n * n_heads, 128, 0, st>>>(n, n_heads, ws->max_heads, ws->seq_first, ws->seq_count,
-                                           ws->part_o, ws->part_ml, out, lse);
-    rc = kvcu_check_cuda(cudaGetLastError(), "combine kernel launch");
+    rc = launch_combine(ws, n_heads, out, lse, st);
     if (rc) return rc;
     ws->last_launches = 2;
     ws->last_impl = KVCU_DECODE_TENSOR_CORE;
@@ -629,9 +666,7 @@ int kvcu_launch_decode(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint32_
   a.ws_heads = ws->max_heads;
   int rc = p->quantized ? launch_decode_q<true>(ws, a, st) : launch_decode_q<false>(ws, a, st);
   if (rc) return rc;
-  k_combine<<<n * n_heads, 128, 0, st>>>(n, n_heads, ws->max_heads, ws->seq_first, ws->seq_count,
-                                         ws->part_o, ws->part_ml, out, lse);
-  rc = kvcu_check_cuda(cudaGetLastError(), "combine kernel launch");
+  rc = launch_combine(ws, n_heads, out, lse, st);
   if (rc) return rc;
   ws->last_launches = 2;
   return KVCU_OK;
