@@ -447,10 +447,13 @@ def run_ours(args, rank, world, local_rank):
         if world == 1 and not args.no_cpu_baseline:
             sample = cpu_sample(cores, args.cpu_sample_tokens)
             dt, toks = cpu_time(sample, cores)
+            # the reference's default pool size (src/inference.zig:149), same sample
+            dt4, toks4 = cpu_time(sample, 4)
             cpu = {"value": toks / dt, "unit": UNIT, "cores": cores, "kind": "port",
                    "sample": f"one layer, {len(sample[3])} sequences from the config-5 length "
                              f"distribution ({toks} ctx tokens, 20 heads, Q8_0); oracle C "
-                             f"restatement on a pthread FIFO pool, {cores} threads"}
+                             f"restatement on a pthread FIFO pool, {cores} threads",
+                   "reference_default_threads": {"threads": 4, "value": toks4 / dt4}}
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1e3 * job_time / args.steps,
