@@ -110,6 +110,7 @@ __global__ void __launch_bounds__(1024) k_plan(uint32_t n, const uint32_t* __res
   __shared__ uint32_t s_carry;           // items of the earlier chunks
   __shared__ unsigned long long s_ccarry;  // cost of the earlier chunks
   const uint32_t tid = threadIdx.x, lane = tid & 31u, wid = tid >> 5, nw = blockDim.x >> 5;
+  kvcu_pdl_trigger();  // a programmatically launched decode may start its prologue
   if (tid == 0) {
     s_total = 0;
     s_carry = 0;
@@ -477,6 +478,7 @@ __global__ void __launch_bounds__(32 * COMBINE_WARPS) k_combine(uint32_t H, uint
                                                                 const float* __restrict__ part_o,
                                                                 const float* __restrict__ part_ml,
                                                                 float* __restrict__ out, float* __restrict__ lse) {
+  kvcu_pdl_wait();  // launched programmatically after the decode kernel
   const uint32_t n_items = meta[0], G = meta[1];
   const uint32_t lane = threadIdx.x & 31u;
   const uint32_t tasks = G > 1 ? (G - 1) * H : 0u;
@@ -528,10 +530,12 @@ int launch_combine(kvcu_decode_ws* ws, uint32_t n_heads, float* out, float* lse,
   const uint32_t cap = 8u * (uint32_t)(ws->num_sms > 0 ? ws->num_sms : 148);
   if (grid > cap) grid = cap;
   if (grid == 0) grid = 1;
-  k_combine<<<grid, 32 * COMBINE_WARPS, 0, st>>>(n_heads, ws->max_heads, ws->meta, ws->ranges, ws->items,
-                                                 ws->seq_first, ws->seq_count, ws->part_o, ws->part_ml, out,
-                                                 lse);
-  return kvcu_check_cuda(cudaGetLastError(), "combine kernel launch");
+  return kvcu_check_cuda(kvcu_launch_pdl(k_combine, dim3(grid), dim3(32 * COMBINE_WARPS), 0, st, n_heads,
+                                         ws->max_heads, (const uint32_t*)ws->meta, (const uint32_t*)ws->ranges,
+                                         (const kvcu_item*)ws->items, (const uint32_t*)ws->seq_first,
+                                         (const uint32_t*)ws->seq_count, (const float*)ws->part_o,
+                                         (const float*)ws->part_ml, out, lse),
+                         "combine kernel launch");
 }
 
 size_t decode_smem(int nh) {

@@ -436,12 +436,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
   auto bar = [&](int i) { return sbase + OFF_MISC + 8u * (uint32_t)i; };
   volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + OFF_ABORT);
-  // this CTA's range of work items (the plan cuts the batch into equal-cost
-  // ranges, one per CTA)
-  const uint32_t n_items = a.meta[0], n_ranges = a.meta[1];
-  const uint32_t it_begin = blockIdx.x < n_ranges ? min(a.ranges[blockIdx.x], n_items) : n_items;
-  const uint32_t it_end = blockIdx.x < n_ranges ? min(a.ranges[blockIdx.x + 1], n_items) : n_items;
-  if (blockIdx.x == 0 && threadIdx.x == 0 && n_ranges > gridDim.x) atomicOr(a.status, KVCU_STATUS_BAD_PLAN);
   const uint32_t H = a.n_heads;
 
   // ---- set-up: barriers, constant operands, TMEM
@@ -467,7 +461,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     mbar_init(bar(B_EPI + 0), EPI_WARPS / 2);
     mbar_init(bar(B_EPI + 1), EPI_WARPS / 2);
     *abort_flag = 0u;
-    *reinterpret_cast<volatile uint32_t*>(smem + OFF_CUR_ITEM) = it_begin;
     uint32_t* ones = reinterpret_cast<uint32_t*>(smem + OFF_ONES);
     for (int i = 0; i < 32; ++i) ones[i] = 0x3C003C00u;  // f16 1.0 pairs
     fence_proxy_async();
@@ -480,6 +473,17 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
+  // Everything above is independent of earlier kernels in the stream (under a
+  // programmatic launch it overlaps their tail); the plan, the lengths and the
+  // pool rows are read only after this wait.
+  kvcu_pdl_wait();
+  // this CTA's range of work items (the plan cuts the batch into equal-cost
+  // ranges, one per CTA)
+  const uint32_t n_items = a.meta[0], n_ranges = a.meta[1];
+  const uint32_t it_begin = blockIdx.x < n_ranges ? min(a.ranges[blockIdx.x], n_items) : n_items;
+  const uint32_t it_end = blockIdx.x < n_ranges ? min(a.ranges[blockIdx.x + 1], n_items) : n_items;
+  if (blockIdx.x == 0 && threadIdx.x == 0 && n_ranges > gridDim.x) atomicOr(a.status, KVCU_STATUS_BAD_PLAN);
+  if (threadIdx.x == 0) *reinterpret_cast<volatile uint32_t*>(smem + OFF_CUR_ITEM) = it_begin;
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -1070,7 +1074,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
   }
 
-  // ---- teardown
+  // ---- teardown (the combine that follows may start launching now)
+  kvcu_pdl_trigger();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -1153,8 +1158,9 @@ int launch_tc(int grid, const CUtensorMap& lat, const CUtensorMap& rope, const T
     if (rc) return rc;
     configured = true;
   }
-  k_decode_tc<HK><<<grid, NTHREADS, SMEM_ALLOC, st>>>(lat, rope, a);
-  return kvcu_check_cuda(cudaGetLastError(), "decode_tc kernel launch");
+  // programmatic launch: the prologue overlaps the previous kernel's tail
+  return kvcu_check_cuda(kvcu_launch_pdl(k_decode_tc<HK>, dim3(grid), dim3(NTHREADS), SMEM_ALLOC, st, lat, rope, a),
+                         "decode_tc kernel launch");
 }
 
 }  // namespace

@@ -45,6 +45,33 @@ struct kvcu_decode_ws {
   int last_impl;             // the kernel the last decode used
 };
 
+// ---- programmatic dependent launch ----
+// A kernel launched with kvcu_launch_pdl may start while its predecessor in the
+// stream is still finishing (once every predecessor CTA has triggered or
+// exited); it runs its independent prologue, then kvcu_pdl_wait() before it
+// touches anything earlier work wrote.  Both device calls are no-ops for an
+// ordinary launch.
+#ifdef __CUDACC__
+__device__ __forceinline__ void kvcu_pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void kvcu_pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+cudaError_t kvcu_launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                            Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
+}
+#endif
+
 // ---- error plumbing (kvcu_api.cu) ----
 void kvcu_set_error(const char* fmt, ...);
 int kvcu_check_cuda(cudaError_t e, const char* what);

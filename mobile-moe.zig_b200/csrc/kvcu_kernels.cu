@@ -152,6 +152,7 @@ __global__ void __launch_bounds__(256) k_append_rows(PoolArgs a, uint32_t n_rows
   const uint32_t lane = threadIdx.x & 31u, grp = lane >> 3, sub = lane & 7u;
   const uint64_t nwarps = ((uint64_t)gridDim.x * blockDim.x) >> 5;
   const uint32_t nblk = a.nbk + a.nbp;
+  kvcu_pdl_trigger();  // a programmatically launched decode may start its prologue
   for (uint64_t r = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < n_rows; r += nwarps) {
     const uint32_t s = row_seq[r], pos = row_pos[r];
     uint64_t row;
