@@ -478,7 +478,8 @@ __global__ void __launch_bounds__(32 * COMBINE_WARPS) k_combine(uint32_t H, uint
                                                                 const float* __restrict__ part_o,
                                                                 const float* __restrict__ part_ml,
                                                                 float* __restrict__ out, float* __restrict__ lse) {
-  kvcu_pdl_wait();  // launched programmatically after the decode kernel
+  kvcu_pdl_wait();     // launched programmatically after the decode kernel
+  kvcu_pdl_trigger();  // the next layer's append may start launching
   const uint32_t n_items = meta[0], G = meta[1];
   const uint32_t lane = threadIdx.x & 31u;
   const uint32_t tasks = G > 1 ? (G - 1) * H : 0u;

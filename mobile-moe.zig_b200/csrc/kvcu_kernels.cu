@@ -152,6 +152,7 @@ __global__ void __launch_bounds__(256) k_append_rows(PoolArgs a, uint32_t n_rows
   const uint32_t lane = threadIdx.x & 31u, grp = lane >> 3, sub = lane & 7u;
   const uint64_t nwarps = ((uint64_t)gridDim.x * blockDim.x) >> 5;
   const uint32_t nblk = a.nbk + a.nbp;
+  kvcu_pdl_wait();     // the previous kernel may still read the rows this one writes
   kvcu_pdl_trigger();  // a programmatically launched decode may start its prologue
   for (uint64_t r = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < n_rows; r += nwarps) {
     const uint32_t s = row_seq[r], pos = row_pos[r];
@@ -318,13 +319,11 @@ int kvcu_launch_append(kvcu_pool* p, uint32_t layer, uint32_t n_rows, const floa
                        (reinterpret_cast<uintptr_t>(rope) & 15) == 0;
   if (rows_ok) {
     const int g = grid_for(n_rows, 256);
-    if (p->quantized)
-      k_append_rows<true><<<g, 256, 0, st>>>(a, n_rows, latent, ls, rope, ps, row_seq, row_pos, n_seqs,
-                                             toff, tables, lens);
-    else
-      k_append_rows<false><<<g, 256, 0, st>>>(a, n_rows, latent, ls, rope, ps, row_seq, row_pos, n_seqs,
-                                              toff, tables, lens);
-    return kvcu_check_cuda(cudaGetLastError(), "append kernel launch");
+    // programmatic launch: it waits for the previous kernel before any access
+    auto kern = p->quantized ? k_append_rows<true> : k_append_rows<false>;
+    return kvcu_check_cuda(kvcu_launch_pdl(kern, dim3(g), dim3(256), 0, st, a, n_rows, latent, ls, rope, ps,
+                                           row_seq, row_pos, n_seqs, toff, tables, lens),
+                           "append kernel launch");
   }
   const uint32_t nper = p->quantized ? p->nblk : (p->kv_rank + p->rope_dim + 31) / 32;
   const int g = grid_for((uint64_t)n_rows * nper, 256);
