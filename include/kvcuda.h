@@ -342,7 +342,10 @@ uint32_t kvcache_seq_block_table(const kvcache* c, uint32_t seq, uint32_t* out, 
  * (seq_ids[r], positions[r]); the positions must lie inside each sequence's
  * capacity.  Sets len = max(len, pos+1).  `rows` is a HOST pointer; the
  * _dev variant takes device pointers for rows, seq_ids and positions (the
- * host copies of seq_ids/positions are still needed for the length update). */
+ * host copies of seq_ids/positions are still needed for the length update).
+ * The _dev calls are stream-ordered: changed block tables and lengths are
+ * uploaded on `stream` from pinned staging, and a later call on another
+ * stream is ordered after that upload; the host does not wait. */
 int kvcache_append_batch(kvcache* c, uint32_t layer, uint32_t n, const uint32_t* seq_ids,
                          const uint32_t* positions, const float* rows);
 int kvcache_append_batch_dev(kvcache* c, uint32_t layer, uint32_t n, const uint32_t* seq_ids,
