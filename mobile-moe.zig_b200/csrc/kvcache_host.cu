@@ -205,6 +205,7 @@ struct kvcache {
   std::vector<uint32_t> h_toff;
   // pinned staging of the table / length uploads (truly asynchronous copies)
   HostStage up_toff, up_tables, up_lens;
+  HostStage up_rowidx;  // sequence ids and positions of a host-rows append
   // scratch for host-buffer calls
   float* d_f = nullptr;
   size_t d_f_cap = 0;
@@ -456,10 +457,16 @@ int append_host_rows(kvcache* c, uint32_t layer, uint32_t n, const uint32_t* seq
   if (!rc) rc = sync_lens(c, c->stream);
   if (!rc) rc = ensure_dev(&c->d_f, &c->d_f_cap, (size_t)n * Wd);
   if (!rc) rc = ensure_dev(&c->d_u, &c->d_u_cap, (size_t)2 * n);
+  if (!rc) rc = stage_acquire(c->up_rowidx, (size_t)2 * n);
   if (rc) return rc;
+  // rows by DMA (reading them in place from mapped host memory is slower: the
+  // append kernel's row reads are latency-bound over PCIe); the row indices
+  // through pinned staging
   KVCU_CUDA(cudaMemcpyAsync(c->d_f, rows, (size_t)n * Wd * 4, cudaMemcpyHostToDevice, c->stream));
-  KVCU_CUDA(cudaMemcpyAsync(c->d_u, seq_ids, (size_t)n * 4, cudaMemcpyHostToDevice, c->stream));
-  KVCU_CUDA(cudaMemcpyAsync(c->d_u + n, positions, (size_t)n * 4, cudaMemcpyHostToDevice, c->stream));
+  memcpy(c->up_rowidx.p, seq_ids, (size_t)n * 4);
+  memcpy(c->up_rowidx.p + n, positions, (size_t)n * 4);
+  rc = stage_upload(c->up_rowidx, c->d_u, (size_t)2 * n, c->stream);
+  if (rc) return rc;
   rc = kvcu_append(c->pool, layer, n, c->d_f, Wd, c->d_f + c->kv_rank, Wd, c->d_u, c->d_u + n,
                    (uint32_t)c->seqs.size(), c->d_toff, c->d_tables, c->d_lens, c->stream);
   if (rc) return rc;
@@ -650,6 +657,7 @@ void kvcache_deinit(kvcache* c) {
   stage_free(c->up_toff);
   stage_free(c->up_tables);
   stage_free(c->up_lens);
+  stage_free(c->up_rowidx);
   if (c->stream) cudaStreamDestroy(c->stream);
   delete c;
 }

@@ -135,6 +135,9 @@ kvcu_pool* kvcu_pool_create(int device, uint32_t n_layers, uint32_t num_blocks,
     if (!rc) rc = kvcu_check_cuda(cudaMalloc(&p->pe, rows * 4ull * rope_dim), "cudaMalloc(pe)");
   }
   if (!rc) rc = kvcu_check_cuda(cudaMalloc(&p->status, sizeof(uint32_t)), "cudaMalloc(status)");
+  if (!rc)
+    rc = kvcu_check_cuda(cudaHostAlloc(reinterpret_cast<void**>(&p->status_host), 64, cudaHostAllocDefault),
+                         "cudaHostAlloc(status)");
   if (!rc) rc = kvcu_pool_zero(p, nullptr);
   if (!rc) rc = kvcu_check_cuda(cudaDeviceSynchronize(), "pool zeroing");
   if (rc) {
@@ -152,6 +155,7 @@ int kvcu_pool_destroy(kvcu_pool* p) {
   cudaFree(p->qs);
   cudaFree(p->sc);
   cudaFree(p->status);
+  if (p->status_host) cudaFreeHost(p->status_host);
   cudaFree(p->staging);
   delete p;
   return KVCU_OK;
@@ -199,11 +203,12 @@ int kvcu_pool_status(kvcu_pool* p, uint32_t* status_out, void* stream) {
   DeviceGuard g(p->device);
   if (g.rc) return g.rc;
   cudaStream_t st = (cudaStream_t)stream;
-  uint32_t v = 0;
-  KVCU_CUDA(cudaMemcpyAsync(&v, p->status, sizeof(v), cudaMemcpyDeviceToHost, st));
+  // into pinned memory: the copy is asynchronous, and one synchronise covers
+  // the read and the reset
+  KVCU_CUDA(cudaMemcpyAsync(p->status_host, p->status, sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
   KVCU_CUDA(cudaMemsetAsync(p->status, 0, sizeof(uint32_t), st));
   KVCU_CUDA(cudaStreamSynchronize(st));
-  *status_out = v;
+  *status_out = *p->status_host;
   return KVCU_OK;
 }
 

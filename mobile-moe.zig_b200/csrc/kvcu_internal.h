@@ -18,6 +18,7 @@ struct kvcu_pool {
   int8_t* qs;                // int8 [L][NB][BS][nblk*32]
   uint16_t* sc;              // f16 bits [L][NB][BS][nblk]
   uint32_t* status;          // device status word (KVCU_STATUS_* bits)
+  uint32_t* status_host;     // pinned host word its reads land in (one synchronise per read)
   uint8_t* staging;          // device staging for checkpoint repacking
   uint64_t staging_bytes;
   uint64_t rows() const { return (uint64_t)n_layers * num_blocks * block_size; }
