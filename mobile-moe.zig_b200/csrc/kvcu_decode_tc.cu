@@ -227,31 +227,40 @@ __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y,
-                                            uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
-      : "memory");
-}
 // 4-D tile: coordinates innermost first
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int x, int y, int z, int w,
-                                            uint32_t bar) {
+                                            uint32_t bar, uint64_t policy) {
   asm volatile(
-      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(bar)
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(bar), "l"(policy)
       : "memory");
+}
+__device__ __forceinline__ void tma_load_2d_hint(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar,
+                                                 uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar), "l"(policy)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_load_hint(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar,
+                                               uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          dst),
+      "l"(src), "r"(bytes), "r"(bar), "l"(policy)
+      : "memory");
+}
+// L2 policy for data read once (the KV stream): evicted first, so that what is
+// reused (queries, partials, block tables) stays
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
 }
 __device__ __forceinline__ void prefetch_l2_keep(const void* p) {
   asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(p));
-}
-__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-      "l"(src), "r"(bytes), "r"(bar)
-      : "memory");
 }
 
 // UMMA shared-memory descriptor (sm_100): start>>4 @0, LBO>>4 @16, SBO>>4 @32,
@@ -502,6 +511,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     if (lane == 0) {
       uint32_t g = 0;  // tiles whose NSL arrivals are all made
       bool live = true;
+      const uint64_t once = policy_evict_first();
       const uint32_t br = a.box_rows;
       for (uint32_t it = it_begin; it < it_end && live; ++it) {
         const Item im = load_item(a, it);
@@ -538,9 +548,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
               const uint64_t row =
                   ((uint64_t)a.layer * a.num_blocks + blk) * a.block_size + pos % a.block_size;
               // the segment's whole latent (4 column chunks) in one box
-              tma_load_4d(stage + ST_LAT + (off >> 3) * LAT_GROUP, &map_lat, 0, 0, 0, (int)(row >> 3), full);
-              tma_load_2d(stage + ST_ROPE + off * 64u, &map_rope, 512, (int)row, full);
-              bulk_load(stage + ST_SC + off * 36u, a.sc + row * NBLK, br * 36u, full);
+              tma_load_4d(stage + ST_LAT + (off >> 3) * LAT_GROUP, &map_lat, 0, 0, 0, (int)(row >> 3), full, once);
+              tma_load_2d_hint(stage + ST_ROPE + off * 64u, &map_rope, 512, (int)row, full, once);
+              bulk_load_hint(stage + ST_SC + off * 36u, a.sc + row * NBLK, br * 36u, full, once);
             }
           }
           if (started) ++g;
