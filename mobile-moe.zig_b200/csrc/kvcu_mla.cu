@@ -92,18 +92,19 @@ __global__ void __launch_bounds__(256)
   C += z * c_hs;
   const uint32_t m0 = blockIdx.y * GM, n0 = blockIdx.x * GN;
   const uint32_t tx = tid % 16, ty = tid / 16;  // columns tx*4.., rows ty*8..
-  float acc[8][4] = {};
-  for (uint32_t k0 = 0; k0 < K; k0 += GK) {
-    // A tile [GM][GK] -> As[k][m]
+  constexpr int RA = (GM * GK) / 256, RB = (GN * GK) / 256;
+  // The next K tile is loaded into registers while the current one is used,
+  // so the global loads' latency overlaps the FMAs.
+  float ra[RA], rb[RB];
+  auto load_tile = [&](uint32_t k0) {
 #pragma unroll
-    for (int r = 0; r < (GM * GK) / 256; ++r) {
+    for (int r = 0; r < RA; ++r) {
       const uint32_t e = tid + 256u * r, mm = e / GK, kk = e % GK;
       const uint32_t gm = m0 + mm, gk = k0 + kk;
-      As[kk][mm] = (gm < M && gk < K) ? A[(uint64_t)gm * lda + gk] : 0.f;
+      ra[r] = (gm < M && gk < K) ? A[(uint64_t)gm * lda + gk] : 0.f;
     }
-    // B tile [GK][GN] -> Bs[k][n]
 #pragma unroll
-    for (int r = 0; r < (GN * GK) / 256; ++r) {
+    for (int r = 0; r < RB; ++r) {
       const uint32_t e = tid + 256u * r;
       uint32_t kk, nn;
       if (TRANS_B) {
@@ -116,20 +117,45 @@ __global__ void __launch_bounds__(256)
       const uint32_t gk = k0 + kk, gn = n0 + nn;
       float v = 0.f;
       if (gk < K && gn < N) v = TRANS_B ? B[(uint64_t)gn * ldb + gk] : B[(uint64_t)gk * ldb + gn];
-      Bs[kk][nn] = v;
+      rb[r] = v;
     }
+  };
+  // A tile [GM][GK] -> As[k][m], B tile [GK][GN] -> Bs[k][n]
+  auto store_tile = [&]() {
+#pragma unroll
+    for (int r = 0; r < RA; ++r) {
+      const uint32_t e = tid + 256u * r;
+      As[e % GK][e / GK] = ra[r];
+    }
+#pragma unroll
+    for (int r = 0; r < RB; ++r) {
+      const uint32_t e = tid + 256u * r;
+      if (TRANS_B) Bs[e % GK][e / GK] = rb[r];
+      else Bs[e / GN][e % GN] = rb[r];
+    }
+  };
+  // accumulators in column pairs: one packed f32x2 FMA is two fmaf
+  float2 acc[8][2];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = make_float2(0.f, 0.f);
+  load_tile(0);
+  for (uint32_t k0 = 0; k0 < K; k0 += GK) {
+    store_tile();
     __syncthreads();
+    if (k0 + GK < K) load_tile(k0 + GK);
 #pragma unroll
     for (int kk = 0; kk < GK; ++kk) {
       const float4 a0 = *reinterpret_cast<const float4*>(&As[kk][ty * 8]);
       const float4 a1 = *reinterpret_cast<const float4*>(&As[kk][ty * 8 + 4]);
       const float4 b4 = *reinterpret_cast<const float4*>(&Bs[kk][tx * 4]);
       const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-      const float bv[4] = {b4.x, b4.y, b4.z, b4.w};
+      const float2 b01 = make_float2(b4.x, b4.y), b23 = make_float2(b4.z, b4.w);
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], bv[j], acc[i][j]);
+      for (int i = 0; i < 8; ++i) {
+        const float2 aa = make_float2(a[i], a[i]);
+        acc[i][0] = __ffma2_rn(aa, b01, acc[i][0]);
+        acc[i][1] = __ffma2_rn(aa, b23, acc[i][1]);
+      }
     }
     __syncthreads();
   }
@@ -137,10 +163,11 @@ __global__ void __launch_bounds__(256)
   for (int i = 0; i < 8; ++i) {
     const uint32_t gm = m0 + ty * 8 + i;
     if (gm >= M) continue;
+    const float v[4] = {acc[i][0].x, acc[i][0].y, acc[i][1].x, acc[i][1].y};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const uint32_t gn = n0 + tx * 4 + j;
-      if (gn < N) C[(uint64_t)gm * ldc + gn] = acc[i][j];
+      if (gn < N) C[(uint64_t)gm * ldc + gn] = v[j];
     }
   }
 }
