@@ -140,7 +140,15 @@ __global__ void __launch_bounds__(256) k_append(PoolArgs a, uint32_t n_rows,
 // table lookups happen once; each 8-lane group owns one 32-element block per
 // step (one float4 per lane, a 3-step shuffle max, one 4-byte store per lane).
 // Same bytes as k_append.
-template <bool QUANT>
+// WHOLE_ROW: each row (up to 4 x APPEND_PREFETCH_GROUPS Q8_0 blocks, i.e.
+// kv_rank + rope_dim <= 1024) is loaded whole before its table lookup.  That
+// hides the lookup for small, latency-bound batches (one token per sequence);
+// large batches keep the leaner form, whose lower register count keeps more
+// warps resident.
+constexpr int APPEND_PREFETCH_GROUPS = 8;
+constexpr uint32_t APPEND_WHOLE_ROW_MAX_ROWS = 16384;
+
+template <bool QUANT, bool WHOLE_ROW>
 __global__ void __launch_bounds__(256) k_append_rows(PoolArgs a, uint32_t n_rows,
                                                      const float* __restrict__ latent, uint64_t ls,
                                                      const float* __restrict__ rope, uint64_t ps,
@@ -154,44 +162,64 @@ __global__ void __launch_bounds__(256) k_append_rows(PoolArgs a, uint32_t n_rows
   const uint32_t nblk = a.nbk + a.nbp;
   kvcu_pdl_wait();     // the previous kernel may still read the rows this one writes
   kvcu_pdl_trigger();  // a programmatically launched decode may start its prologue
+  // one 4-block group of the row: 8 lanes per block, a float4 each
+  auto put_group = [&](uint64_t r, uint64_t row, uint32_t b, bool act, float4 x) {
+    if (QUANT) {
+      float amax = fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w)));
+#pragma unroll
+      for (int o = 1; o < 8; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      const float d = kvcu::q8_scale(amax);
+      const float inv = d > 0.0f ? __frcp_rn(d) : 0.0f;
+      char4 q = make_char4(0, 0, 0, 0);
+      if (d > 0.0f) {
+        q.x = kvcu::q8_value_fast(x.x, d, inv);
+        q.y = kvcu::q8_value_fast(x.y, d, inv);
+        q.z = kvcu::q8_value_fast(x.z, d, inv);
+        q.w = kvcu::q8_value_fast(x.w, d, inv);
+      }
+      if (act) {
+        *reinterpret_cast<char4*>(a.qs + row * (32u * nblk) + 32u * b + 4u * sub) = q;
+        // the hardware RNE conversion gives the same bits as f32_to_f16 for
+        // every non-NaN d (normal, subnormal, overflow to inf)
+        if (sub == 0) a.sc[row * nblk + b] = d == d ? __half_as_ushort(__float2half_rn(d)) : kvcu::f32_to_f16(d);
+      }
+    } else if (act) {
+      float* dst = b < a.nbk ? a.kv + row * a.kv_rank + 32u * b + 4u * sub
+                             : a.pe + row * a.rope_dim + 32u * (b - a.nbk) + 4u * sub;
+      *reinterpret_cast<float4*>(dst) = x;
+    }
+  };
+  auto load_group = [&](uint64_t r, uint32_t b) -> float4 {
+    const float* src = b < a.nbk ? latent + r * ls + 32u * b + 4u * sub
+                                 : rope + r * ps + 32u * (b - a.nbk) + 4u * sub;
+    return __ldg(reinterpret_cast<const float4*>(src));
+  };
   for (uint64_t r = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < n_rows; r += nwarps) {
     const uint32_t s = row_seq[r], pos = row_pos[r];
-    uint64_t row;
-    if (!resolve_row(a, s, pos, n_seqs, toff, tables, lane, &row)) continue;
-    // len = max(len, pos + 1), src/kv_cache.zig:358-360
-    if (lens && lane == 0) atomicMax(lens + s, pos + 1u);
-    for (uint32_t b0 = 0; b0 < nblk; b0 += 4) {
-      const uint32_t b = b0 + grp;
-      const bool act = b < nblk;
-      float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (act) {
-        const float* src = b < a.nbk ? latent + r * ls + 32u * b + 4u * sub
-                                     : rope + r * ps + 32u * (b - a.nbk) + 4u * sub;
-        x = __ldg(reinterpret_cast<const float4*>(src));
-      }
-      if (QUANT) {
-        float amax = fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w)));
+    if (WHOLE_ROW) {
+      // The whole row is loaded first, so that its loads overlap the block
+      // table lookup below (the input does not depend on the table).
+      float4 xs[APPEND_PREFETCH_GROUPS];
 #pragma unroll
-        for (int o = 1; o < 8; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-        const float d = kvcu::q8_scale(amax);
-        const float inv = d > 0.0f ? __frcp_rn(d) : 0.0f;
-        char4 q = make_char4(0, 0, 0, 0);
-        if (d > 0.0f) {
-          q.x = kvcu::q8_value_fast(x.x, d, inv);
-          q.y = kvcu::q8_value_fast(x.y, d, inv);
-          q.z = kvcu::q8_value_fast(x.z, d, inv);
-          q.w = kvcu::q8_value_fast(x.w, d, inv);
-        }
-        if (act) {
-          *reinterpret_cast<char4*>(a.qs + row * (32u * nblk) + 32u * b + 4u * sub) = q;
-          // the hardware RNE conversion gives the same bits as f32_to_f16 for
-          // every non-NaN d (normal, subnormal, overflow to inf)
-          if (sub == 0) a.sc[row * nblk + b] = d == d ? __half_as_ushort(__float2half_rn(d)) : kvcu::f32_to_f16(d);
-        }
-      } else if (act) {
-        float* dst = b < a.nbk ? a.kv + row * a.kv_rank + 32u * b + 4u * sub
-                               : a.pe + row * a.rope_dim + 32u * (b - a.nbk) + 4u * sub;
-        *reinterpret_cast<float4*>(dst) = x;
+      for (uint32_t g = 0; g < (uint32_t)APPEND_PREFETCH_GROUPS; ++g) {
+        const uint32_t b = 4u * g + grp;
+        xs[g] = b < nblk ? load_group(r, b) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      uint64_t row;
+      if (!resolve_row(a, s, pos, n_seqs, toff, tables, lane, &row)) continue;
+      // len = max(len, pos + 1), src/kv_cache.zig:358-360
+      if (lens && lane == 0) atomicMax(lens + s, pos + 1u);
+#pragma unroll
+      for (uint32_t g = 0; g < (uint32_t)APPEND_PREFETCH_GROUPS; ++g)
+        if (4u * g < nblk) put_group(r, row, 4u * g + grp, 4u * g + grp < nblk, xs[g]);  // warp-uniform test
+    } else {
+      uint64_t row;
+      if (!resolve_row(a, s, pos, n_seqs, toff, tables, lane, &row)) continue;
+      if (lens && lane == 0) atomicMax(lens + s, pos + 1u);
+      for (uint32_t b0 = 0; b0 < nblk; b0 += 4) {
+        const uint32_t b = b0 + grp;
+        const bool act = b < nblk;
+        put_group(r, row, b, act, act ? load_group(r, b) : make_float4(0.f, 0.f, 0.f, 0.f));
       }
     }
   }
@@ -320,7 +348,9 @@ int kvcu_launch_append(kvcu_pool* p, uint32_t layer, uint32_t n_rows, const floa
   if (rows_ok) {
     const int g = grid_for(n_rows, 256);
     // programmatic launch: it waits for the previous kernel before any access
-    auto kern = p->quantized ? k_append_rows<true> : k_append_rows<false>;
+    const bool whole = n_rows <= APPEND_WHOLE_ROW_MAX_ROWS && p->nblk <= 4u * APPEND_PREFETCH_GROUPS;
+    auto kern = p->quantized ? (whole ? k_append_rows<true, true> : k_append_rows<true, false>)
+                             : (whole ? k_append_rows<false, true> : k_append_rows<false, false>);
     return kvcu_check_cuda(kvcu_launch_pdl(kern, dim3(g), dim3(256), 0, st, a, n_rows, latent, ls, rope, ps,
                                            row_seq, row_pos, n_seqs, toff, tables, lens),
                            "append kernel launch");
