@@ -43,6 +43,10 @@ OUTLIER_P = 0.01
 SCALE = float(np.float32(1.0 / math.sqrt(192.0)))
 Q8_ROW_BYTES = 18 * 34  # 612
 METRIC = "paged MLA decode ctx-tokens/s (config 5 serving step, Q8_0 KV)"
+# what the decode computes in: Q8_0 KV; QK exact in int8 (q as two int8 digits,
+# int32 per Q8_0 block); V and P in f16; f32 accumulation and softmax
+DTYPE = "q8_0 KV; int8 QK exact; f16 PV; f32 accumulate"
+CPU_DTYPE = "q8_0 KV dequantized to f32; f32 arithmetic"
 UNIT = "ctx-tokens/s"
 
 
@@ -203,7 +207,7 @@ def run_reference(args, rank, world):
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps,
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": CPU_DTYPE,
         "data": "synthetic (seeded N(0,1), 1% x20 outliers)",
         "config": {"workload": "config5_sharded_serving_step", "kv_dtype": "q8_0", "heads": H,
                    "kv_rank": R, "rope_dim": P, "sample": desc},
@@ -457,7 +461,7 @@ def run_ours(args, rank, world, local_rank):
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1e3 * job_time / args.steps,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": DTYPE,
             "data": "synthetic (seeded N(0,1) rows with 1% x20 outliers, random q)",
             "config": {"workload": ("config5_sharded_serving_step" if (args.seqs, NL) == (N_SEQS, N_LAYERS)
                                     else f"config5_reduced_{args.seqs}seqs_{NL}layers"), "n_seqs": args.seqs,
@@ -474,6 +478,9 @@ def run_ours(args, rank, world, local_rank):
                          "bound": "hbm", "achieved": dec_gbs, "peak": peak, "unit": "GB/s",
                          "frac": dec_gbs / peak, "peak_source": peak_kind,
                          "traffic": (traffic_per_tok * avg_ctx_per_launch if traffic_per_tok else None),
+                         "traffic_source": ("not measured in this run: DRAM bytes per ctx token from the ncu "
+                                            "capture in profiles/decode_tc_config5_ncu.md (64-sequence, "
+                                            "1-layer case larger than L2), scaled by this launch's tokens"),
                          "algorithmic_bytes_per_launch": dec_bytes,
                          "avg_launch_ms": avg_dec * 1e3},
             "gpu_launches": launches,

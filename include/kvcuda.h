@@ -85,7 +85,8 @@ extern "C" {
 /* metal_get_last_error, src/metal_bridge.c:50-52.  Thread-local. */
 const char* kvcu_get_last_error(void);
 /* metal_init, src/metal_bridge.c:54-87: select a CUDA device, check it is
- * sm_100 (B200), create its context.  0 on success. */
+ * sm_100 (B200), create its context and reserve the fixed scratch of
+ * kvcu_mla_decode_noalloc on it.  0 on success. */
 int kvcu_init(int device);
 /* Number of visible CUDA devices (0 without a driver/GPU). */
 int kvcu_device_count(void);
@@ -234,14 +235,17 @@ int kvcu_decode_last_impl(const kvcu_decode_ws* ws);
  * layer in a single call, with the same semantics and kernels as
  * kvcu_decode_plan + kvcu_mla_decode, but keeps the split-KV scratch (work
  * items, per-item partial outputs) in a fixed array compiled into the library
- * (KVCU_NOALLOC_SCRATCH_BYTES of device memory per device, reserved when the
- * library's device code is loaded) instead of a kvcu_decode_ws.
+ * (KVCU_NOALLOC_SCRATCH_BYTES of device memory per device) instead of a
+ * kvcu_decode_ws.  The array is reserved on a device by kvcu_init(device),
+ * which kvcu_pool_create also calls, so a runtime that reserves the rest of
+ * the device afterwards loses nothing at its first no-alloc decode.
  *   Limits: n <= KVCU_NOALLOC_MAX_BATCH, 1 <= n_heads <= KVCU_NOALLOC_MAX_HEADS;
  *   larger requests return KVCU_ERR_INVALID_ARG and change nothing.  Long
  *   sequences are split into at most KVCU_NOALLOC_MAX_ITEMS work items in all.
- *   The first call on a device looks up the array's device address (with that
- *   device current); make that first call before capturing `stream` into a
- *   graph.  The scratch is one per device and is not guarded: calls that may
+ *   The array's device address is looked up once per device, with that
+ *   device current, by kvcu_init (or by the first call on a device that
+ *   kvcu_init never saw); make that first call before capturing `stream`
+ *   into a graph.  The scratch is one per device and is not guarded: calls that may
  *   overlap on the same device (other streams, other host threads) race on it
  *   and must be serialised by the caller. */
 #define KVCU_NOALLOC_MAX_BATCH 64u

@@ -11,6 +11,7 @@ from __future__ import annotations
 import argparse
 import concurrent.futures as cf
 import glob
+import hashlib
 import os
 import shutil
 import subprocess
@@ -36,19 +37,36 @@ def nvcc() -> str:
     raise RuntimeError("nvcc not found: the CUDA toolkit is required to build libkvcuda.so")
 
 
+def _digest(src: str) -> str:
+    """Content hash of a source, every header it may include and the flags (a
+    checkout can leave any mtimes, so reuse is decided by content)."""
+    h = hashlib.sha256()
+    deps = [src] + sorted(glob.glob(os.path.join(CSRC, "*.h")) + glob.glob(os.path.join(CSRC, "*.cuh")))
+    deps.append(os.path.join(ROOT, "include", "kvcuda.h"))
+    for d in deps:
+        h.update(d.encode())
+        with open(d, "rb") as f:
+            h.update(f.read())
+    h.update(" ".join(ARCH + NVCC_FLAGS).encode())
+    return h.hexdigest()
+
+
 def _compile(src: str, ptxas_v: bool) -> tuple[str, str]:
     obj = os.path.join(BUILD, os.path.basename(src) + ".o")
-    if os.path.exists(obj) and not ptxas_v:
-        deps = [src] + glob.glob(os.path.join(CSRC, "*.h")) + glob.glob(os.path.join(CSRC, "*.cuh"))
-        deps.append(os.path.join(ROOT, "include", "kvcuda.h"))
-        if all(os.path.getmtime(obj) >= os.path.getmtime(d) for d in deps):
-            return obj, ""
+    stamp = obj + ".sha256"
+    digest = _digest(src)
+    if os.path.exists(obj) and os.path.exists(stamp) and not ptxas_v:
+        with open(stamp) as f:
+            if f.read().strip() == digest:
+                return obj, ""
     cmd = [nvcc(), *ARCH, *NVCC_FLAGS, "-c", src, "-o", obj]
     if ptxas_v:
         cmd += ["-Xptxas", "-v"]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"nvcc failed for {src}:\n{r.stdout}\n{r.stderr}")
+    with open(stamp, "w") as f:
+        f.write(digest)
     return obj, r.stdout + r.stderr
 
 
@@ -62,14 +80,19 @@ def build(verbose: bool = False, ptxas_v: bool = False) -> str:
         for _, log in results:
             if log:
                 print(log)
-    newest = max(os.path.getmtime(o) for o in objs)
-    if not os.path.exists(LIB) or os.path.getmtime(LIB) < newest:
+    # relink when any object changed (by content) or the library is missing
+    link_digest = hashlib.sha256("".join(open(o + ".sha256").read() for o in objs).encode()).hexdigest()
+    lib_stamp = os.path.join(BUILD, "libkvcuda.so.sha256")
+    old = open(lib_stamp).read().strip() if os.path.exists(lib_stamp) else ""
+    if not os.path.exists(LIB) or old != link_digest:
         tmp = LIB + ".tmp"
         cmd = [nvcc(), *ARCH, "-shared", "-o", tmp, *objs, "-lpthread"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
         os.replace(tmp, LIB)
+        with open(lib_stamp, "w") as f:
+            f.write(link_digest)
     return LIB
 
 

@@ -1154,6 +1154,17 @@ int kvcache_save_to_file(kvcache* c, const char* path) {
 // src/kv_cache.zig:497-546 with block-id validation and free-list removal.
 int kvcache_load_from_file(kvcache* c, const char* path) {
   if (!c || !path) return KVCU_ERR_INVALID_ARG;
+  // A v1 file holds one sequence and overwrites the whole pool; with other
+  // sequences holding blocks it would clobber their rows and could hand one of
+  // their blocks to sequence 0 as well.  The reference's cache has a single
+  // sequence, so refuse instead of guessing (the v2 format keeps them all).
+  for (size_t s = 1; s < c->seqs.size(); ++s)
+    if (!c->seqs[s].table.empty() || c->seqs[s].len) {
+      kvcu_set_error("loadFromFile: sequence %zu of this cache holds blocks; a v1 checkpoint restores a "
+                     "single-sequence cache (use kvcache_load_from_file_v2)",
+                     s);
+      return KVCU_ERR_INVALID_ARG;
+    }
   DevScope d(c->device);
   Fd f(open(path, O_RDONLY | O_CLOEXEC));
   if (f.fd < 0) {

@@ -9,7 +9,11 @@
 #include <string.h>
 
 #include <algorithm>
+#include <map>
+#include <mutex>
 #include <new>
+#include <set>
+#include <utility>
 
 #include "kvcu_internal.h"
 
@@ -30,6 +34,35 @@ int kvcu_check_cuda(cudaError_t e, const char* what) {
   if (e == cudaErrorMemoryAllocation) return KVCU_ERR_NO_MEMORY;
   if (e == cudaErrorNoDevice || e == cudaErrorInsufficientDriver) return KVCU_ERR_NO_DEVICE;
   return KVCU_ERR_CUDA;
+}
+
+namespace {
+std::mutex g_config_mutex;
+std::set<std::pair<const void*, int>> g_configured;  // (kernel key, device) pairs set up
+std::mutex g_sm_mutex;
+std::map<int, int> g_sm_count;
+}  // namespace
+
+int kvcu_configure_once(const void* key, int (*setup)(const void* ctx), const void* ctx) {
+  int dev = 0;
+  KVCU_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(g_config_mutex);
+  if (g_configured.count({key, dev})) return KVCU_OK;
+  const int rc = setup(ctx);
+  if (rc == KVCU_OK) g_configured.insert({key, dev});
+  return rc;
+}
+
+int kvcu_current_sm_count() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  std::lock_guard<std::mutex> lock(g_sm_mutex);
+  auto it = g_sm_count.find(dev);
+  if (it != g_sm_count.end()) return it->second;
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
+  g_sm_count[dev] = sms;
+  return sms;
 }
 
 namespace {
@@ -96,7 +129,8 @@ int kvcu_init(int device) {
   DeviceGuard g(device);
   if (g.rc) return g.rc;
   KVCU_CUDA(cudaFree(nullptr));  // create the primary context
-  return KVCU_OK;
+  // reserve the allocation-free decode's fixed scratch now, not at its first call
+  return kvcu_noalloc_prepare(device);
 }
 
 kvcu_pool* kvcu_pool_create(int device, uint32_t n_layers, uint32_t num_blocks,

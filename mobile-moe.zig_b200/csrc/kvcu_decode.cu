@@ -544,18 +544,20 @@ size_t decode_smem(int nh) {
                           3 * (size_t)nh);
 }
 
+// Per-device set-up of one instance (run once per device by kvcu_configure_once).
+template <bool QUANT, int NH>
+int setup_decode(const void*) {
+  return kvcu_check_cuda(cudaFuncSetAttribute(k_decode<QUANT, NH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              (int)decode_smem(NH)),
+                         "cudaFuncSetAttribute(decode)");
+}
+
 template <bool QUANT, int NH>
 int launch_decode_t(kvcu_decode_ws* ws, const DecodeArgs& a, cudaStream_t st) {
   const size_t smem = decode_smem(NH);
-  static bool configured = false;
-  if (!configured) {
-    int rc = kvcu_check_cuda(
-        cudaFuncSetAttribute(k_decode<QUANT, NH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)smem),
-        "cudaFuncSetAttribute(decode)");
-    if (rc) return rc;
-    configured = true;
-  }
+  const int rc =
+      kvcu_configure_once(reinterpret_cast<const void*>(&k_decode<QUANT, NH>), setup_decode<QUANT, NH>, nullptr);
+  if (rc) return rc;
   k_decode<QUANT, NH><<<ws->decode_ctas, NT, smem, st>>>(a);
   return kvcu_check_cuda(cudaGetLastError(), "decode kernel launch");
 }

@@ -1148,26 +1148,29 @@ int make_maps(const kvcu_pool* p, uint32_t box_rows, CUtensorMap* lat, CUtensorM
   return KVCU_OK;
 }
 
+// Per-device set-up of one head bucket's kernel (run once per device by
+// kvcu_configure_once).
+template <int HK>
+int setup_tc(const void*) {
+  // the setmaxnreg split assumes exactly LAUNCH_REGS registers per thread at
+  // launch; with fewer, an epilogue .inc could wait forever, so refuse
+  cudaFuncAttributes fa;
+  int rc = kvcu_check_cuda(cudaFuncGetAttributes(&fa, k_decode_tc<HK>), "cudaFuncGetAttributes(decode_tc)");
+  if (rc) return rc;
+  if (fa.numRegs != (int)LAUNCH_REGS) {
+    kvcu_set_error("decode_tc: built with %d registers per thread, the register split needs %u", fa.numRegs,
+                   LAUNCH_REGS);
+    return KVCU_ERR_UNSUPPORTED;
+  }
+  return kvcu_check_cuda(
+      cudaFuncSetAttribute(k_decode_tc<HK>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_ALLOC),
+      "cudaFuncSetAttribute(decode_tc)");
+}
+
 template <int HK>
 int launch_tc(int grid, const CUtensorMap& lat, const CUtensorMap& rope, const TcArgs& a, cudaStream_t st) {
-  static bool configured = false;
-  if (!configured) {
-    // the setmaxnreg split assumes exactly LAUNCH_REGS registers per thread at
-    // launch; with fewer, an epilogue .inc could wait forever, so refuse
-    cudaFuncAttributes fa;
-    int rc = kvcu_check_cuda(cudaFuncGetAttributes(&fa, k_decode_tc<HK>), "cudaFuncGetAttributes(decode_tc)");
-    if (rc) return rc;
-    if (fa.numRegs != (int)LAUNCH_REGS) {
-      kvcu_set_error("decode_tc: built with %d registers per thread, the register split needs %u",
-                     fa.numRegs, LAUNCH_REGS);
-      return KVCU_ERR_UNSUPPORTED;
-    }
-    rc = kvcu_check_cuda(cudaFuncSetAttribute(k_decode_tc<HK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              (int)SMEM_ALLOC),
-                         "cudaFuncSetAttribute(decode_tc)");
-    if (rc) return rc;
-    configured = true;
-  }
+  const int rc = kvcu_configure_once(reinterpret_cast<const void*>(&k_decode_tc<HK>), setup_tc<HK>, nullptr);
+  if (rc) return rc;
   // programmatic launch: the prologue overlaps the previous kernel's tail
   return kvcu_check_cuda(kvcu_launch_pdl(k_decode_tc<HK>, dim3(grid), dim3(NTHREADS), SMEM_ALLOC, st, lat, rope, a),
                          "decode_tc kernel launch");

@@ -76,6 +76,14 @@ cudaError_t kvcu_launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, siz
 // ---- error plumbing (kvcu_api.cu) ----
 void kvcu_set_error(const char* fmt, ...);
 int kvcu_check_cuda(cudaError_t e, const char* what);
+// One-time set-up of a kernel (function attributes such as its dynamic shared
+// memory limit) for the CURRENT device: `setup(ctx)` runs the first time the
+// pair (key, device) is seen, under a process-wide lock, and is recorded only
+// when it returns KVCU_OK.  Function attributes are per device, so a process
+// that drives several GPUs configures each one; host threads may race here.
+int kvcu_configure_once(const void* key, int (*setup)(const void* ctx), const void* ctx);
+// Multiprocessor count of the current device (cached per device).
+int kvcu_current_sm_count();
 #define KVCU_CUDA(call) \
   do { \
     int _rc = kvcu_check_cuda((call), #call); \
@@ -106,6 +114,10 @@ int kvcu_launch_plan(kvcu_decode_ws* ws, const kvcu_pool* p, uint32_t n, const u
 int kvcu_launch_plan_target(kvcu_decode_ws* ws, const kvcu_pool* p, uint32_t n,
                             const uint32_t* seq_ids, uint32_t n_seqs, const uint32_t* lens,
                             uint32_t target, cudaStream_t st);
+// ---- allocation-free decode (kvcu_noalloc.cu) ----
+// Resolve (and so reserve) the fixed decode scratch on `device`, which must be
+// current; kvcu_init calls it.
+int kvcu_noalloc_prepare(int device);
 // ---- tensor-core decode (kvcu_decode_tc.cu) ----
 bool kvcu_decode_tc_supported(const kvcu_pool* p, uint32_t n_heads);
 int kvcu_launch_decode_tc(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint32_t n,

@@ -47,13 +47,7 @@ PoolArgs pool_args(kvcu_pool* p, uint32_t layer) {
 }
 
 int grid_for(uint64_t warps, int threads) {
-  static int sms = 0;
-  if (!sms) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (sms <= 0) sms = 148;
-  }
+  const int sms = kvcu_current_sm_count();
   uint64_t blocks = (warps * 32 + threads - 1) / threads;
   uint64_t cap = (uint64_t)sms * 16;  // 16 resident 256-thread CTAs per SM at most
   if (blocks > cap) blocks = cap;

@@ -3,8 +3,10 @@
 // For callers that cannot allocate device memory when they decode: the split-KV
 // scratch that kvcu_decode_ws_create would cudaMalloc (work items, the plan's
 // per-entry item ranges, per-item partial outputs and softmax statistics) is a
-// fixed array compiled into this translation unit, one per device, reserved
-// when the library's device code is loaded.  The call plans and decodes with
+// fixed array compiled into this translation unit, one per device.  CUDA loads
+// a module's device memory lazily (on first use), so kvcu_init (which every
+// pool creation calls) looks the array up on its device: that is the moment
+// the memory is reserved, before any serving starts.  The call plans and decodes with
 // the same kernels as kvcu_decode_plan + kvcu_mla_decode; only where the
 // scratch lives, and the plan's range count (bounded by the array), differ.
 //
@@ -71,6 +73,13 @@ int scratch_for_device(int device, unsigned char** out) {
 }
 
 }  // namespace
+
+// Called by kvcu_init with `device` current: loads the module that holds the
+// scratch and resolves its address, so the reservation happens at set-up.
+int kvcu_noalloc_prepare(int device) {
+  unsigned char* base = nullptr;
+  return scratch_for_device(device, &base);
+}
 
 extern "C" int kvcu_mla_decode_noalloc(kvcu_pool* p, uint32_t layer, uint32_t n,
                                        const uint32_t* seq_ids, uint32_t n_seqs,

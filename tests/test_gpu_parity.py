@@ -138,6 +138,26 @@ def test_kvcache_checkpoint_errors(kv, tmp_path):
     assert e.value.name == "EndOfStream"
 
 
+def test_v1_load_refuses_a_cache_with_other_live_sequences(kv, tmp_path):
+    # A v1 file restores a single-sequence cache; loading it into a pool whose
+    # other sequences hold blocks would overwrite their rows.
+    c = kv.KVCache.with_blocks(L_T, R_T, P_T, 8, block_size=16)
+    c.ensureCapacity(20)
+    path = tmp_path / "v1.bin"
+    c.saveToFile(path)
+    s1 = c.seq_create()
+    c.seq_ensure_capacity(s1, 5)
+    free_before = c.numFreeBlocks()
+    with pytest.raises(kv.KVCudaError) as e:
+        c.loadFromFile(path)
+    assert e.value.name == "InvalidArgument"
+    assert c.numFreeBlocks() == free_before and len(c.block_table) == 2
+    # an empty extra sequence is no obstacle
+    c.seq_reset(s1)
+    c.loadFromFile(path)
+    assert len(c.block_table) == 2
+
+
 def test_kvcache_truncate_reset_and_errors(kv):
     c = kv.KVCache(L_T, R_T, P_T, 64)
     c.ensureCapacity(35)

@@ -102,6 +102,60 @@ def test_noalloc_max_batch_with_seq_ids(kv, torch):
     _compare(kv, torch, lens, 32, True, 16, 903, n_layers=1, seq_ids=ids)
 
 
+def test_noalloc_leaves_free_device_memory_unchanged(kv, torch):
+    # The point of the entry point: after kvcu_init (which reserves the fixed
+    # scratch) and one warm-up call (which lets CUDA load the kernels it
+    # launches), repeated calls take no device memory at all.
+    dev = torch.device("cuda", 0)
+    lens = [5, 300, 7000, 16000, 0, 900]
+    pool, toff, ttab, lens_dev = _build(kv, torch, lens, 64, True, 1, 905)
+    n, H = len(lens), 20
+    q = torch.randn((n, H, W), device=dev, generator=torch.Generator(device=dev).manual_seed(905))
+    out = torch.empty((n, H, 512), device=dev)
+    assert _noalloc(kv, pool, 0, n, n, toff, ttab, lens_dev, q, H, out) == 0, kv.last_error()
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info(dev)[0]
+    for _ in range(5):
+        assert _noalloc(kv, pool, 0, n, n, toff, ttab, lens_dev, q, H, out) == 0, kv.last_error()
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info(dev)[0] == free0
+    assert pool.status() == 0
+    pool.close()
+
+
+def test_noalloc_on_two_devices_from_one_process(kv, torch):
+    # Kernel set-up (dynamic shared memory limits) and the scratch address are
+    # per device; one process drives both GPUs in turn.
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    lens = [40, 2500, 9000, 130]
+    n, H = len(lens), 20
+    for d in (1, 0, 1):
+        dev = torch.device("cuda", d)
+        kv.init(d)
+        nb = sum((L + 63) // 64 for L in lens) + 4
+        pool = kv.DevicePool(d, 1, nb, 64, 512, 64, True)
+        pool.zero()
+        offs, tabs = seeded_tables(lens, 64, nb, 906 + d)
+        toff = torch.from_numpy(offs.astype(np.int32)).to(dev)
+        ttab = torch.from_numpy(tabs.astype(np.int32)).to(dev)
+        lens_dev = torch.from_numpy(np.asarray(lens, np.int32)).to(dev)
+        with torch.cuda.device(d):
+            kv.prefill_synthetic(pool, 0, lens, toff, ttab, 906, outlier_p=0.01)
+            q = torch.randn((n, H, W), device=dev, generator=torch.Generator(device=dev).manual_seed(d))
+            want = torch.empty((n, H, 512), device=dev)
+            got = torch.full((n, H, 512), float("nan"), device=dev)
+            ws = kv.DecodeWorkspace(d, n, H)
+            ws.plan(pool, lens_dev)
+            ws.decode(pool, 0, q, toff, ttab, lens_dev, SCALE, want)
+            assert _noalloc(kv, pool, 0, n, n, toff, ttab, lens_dev, q, H, got) == 0, kv.last_error()
+            torch.cuda.synchronize(dev)
+        assert pool.status() == 0
+        assert rel_err_rows(got.cpu().numpy(), want.cpu().numpy()) <= REL_TOL
+        ws.close()
+        pool.close()
+
+
 def test_noalloc_rejects_sizes_beyond_the_scratch(kv, torch):
     dev = torch.device("cuda", 0)
     pool, toff, ttab, lens_dev = _build(kv, torch, [10] * 66, 16, True, 1, 904)
