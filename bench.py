@@ -279,11 +279,211 @@ def measure_append(kvcu, torch, dev, local_rank, reps=5):
     e1.record(st)
     torch.cuda.synchronize(dev)
     dt = e0.elapsed_time(e1) / 1e3 / reps
+    # gather/dequant of the same rows back to f32 (getKVCompressed + getKPe for
+    # every position): 612 B in (+8 B of row indices) and 2,304 B out per row
+    out = torch.empty_like(rows)
+    pool.gather_rows(0, seq, pos, toff, tables, out, stream=st)  # warm-up
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    g0.record(st)
+    for _ in range(reps):
+        pool.gather_rows(0, seq, pos, toff, tables, out, stream=st)
+    g1.record(st)
+    torch.cuda.synchronize(dev)
+    gdt = g0.elapsed_time(g1) / 1e3 / reps
     status = pool.status()
     pool.close()
     if status:
-        raise RuntimeError(f"append benchmark hit device status {status:#x}")
-    return APPEND_ROWS * (2304 + Q8_ROW_BYTES + 8) / dt / 1e9
+        raise RuntimeError(f"append/gather benchmark hit device status {status:#x}")
+    return (APPEND_ROWS * (2304 + Q8_ROW_BYTES + 8) / dt / 1e9,
+            APPEND_ROWS * (Q8_ROW_BYTES + 8 + 2304) / gdt / 1e9)
+
+# ------------------------------------------------------------------ config 4 (second bench figure)
+C4_SEQS, C4_LAYERS, C4_LO, C4_HI, C4_SEED = 64, 4, 8192, 32768, 4
+
+
+def measure_config4(kvcu, torch, dev, local_rank, peak, steps=10, warmup=3):
+    """BASELINE config 4 on this GPU: 64 sequences with lengths uniform in
+    [8192, 32768], 4 layers, Q8_0, block size 64, 20 heads; a step appends one
+    token per sequence per layer, then decodes (fused Q8_0 dequant) each layer.
+    Device-resident inputs, CUDA events around `steps` steps after `warmup`."""
+    lens0 = np.random.default_rng(C4_SEED).integers(C4_LO, C4_HI + 1, C4_SEQS).astype(np.int64)
+    n, NL = C4_SEQS, C4_LAYERS
+    total = warmup + steps
+    nb = int(sum((int(L) + total + BS - 1) // BS for L in lens0)) + 8
+    cache = kvcu.KVCache.with_blocks(NL, R, P, nb, BS, quantized=True, device=local_rank)
+    for _ in range(n - 1):
+        cache.seq_create()
+    ids = np.arange(n, dtype=np.uint32)
+    for i in range(n):
+        cache.seq_ensure_capacity(i, int(lens0[i]) + total)
+    for layer in range(NL):
+        cache.prefill_synthetic(layer, ids, lens0, C4_SEED, OUTLIER_P)
+    st = torch.cuda.Stream(device=dev)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(st):
+        pos_dev = torch.stack([torch.from_numpy((lens0 + k).astype(np.int32)) for k in range(total)]).to(dev)
+        ids_dev = torch.from_numpy(ids.astype(np.int32)).to(dev)
+        rows = torch.empty((total, NL, n, W), dtype=torch.float32, device=dev)
+        for k in range(total):
+            for layer in range(NL):
+                kvcu.synth_rows(C4_SEED, layer, ids_dev, pos_dev[k], W, rows[k, layer], OUTLIER_P, st)
+        qs = torch.randn((NL, n, H, W), device=dev, generator=torch.Generator(device=dev).manual_seed(C4_SEED))
+        outs = torch.empty((NL, n, H, R), dtype=torch.float32, device=dev)
+    st.synchronize()
+    dec = []
+
+    def step(k, timed):
+        pos_h = (lens0 + k).astype(np.uint32)
+        for layer in range(NL):
+            cache.appendBatch_dev(layer, ids, pos_h, ids_dev, pos_dev[k], rows[k, layer], st)
+            if timed:
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(st)
+            cache.mlaDecode_dev(layer, ids, qs[layer], SCALE, outs[layer], st)
+            if timed:
+                e1.record(st)
+                dec.append((e0, e1))
+
+    for k in range(warmup):
+        step(k, False)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ctx = 0
+    st.synchronize()
+    t0.record(st)
+    for k in range(warmup, total):
+        step(k, True)
+        ctx += int((lens0 + k + 1).sum()) * NL
+    t1.record(st)
+    st.synchronize()
+    status = cache.pool().status()
+    secs = t0.elapsed_time(t1) / 1e3
+    avg_dec = sum(a.elapsed_time(b) for a, b in dec) / len(dec) / 1e3
+    per_launch = ctx / len(dec)
+    dec_bytes = per_launch * Q8_ROW_BYTES + n * H * W * 4 + n * H * R * 4 + 4 * nb / NL
+    cache.close()
+    if status:
+        raise RuntimeError(f"config 4 hit device status {status:#x}")
+    return {"workload": "config4_long_context_q8_step", "n_seqs": n, "layers": NL, "block_size": BS, "heads": H,
+            "lengths": f"uniform[{C4_LO},{C4_HI}] seed {C4_SEED}", "steps": steps, "warmup": warmup,
+            "ctx_tokens_per_step": ctx // steps, "ms_per_step": 1e3 * secs / steps,
+            "ctx_tokens_per_s": ctx / secs,
+            "decode": {"GB/s": dec_bytes / avg_dec / 1e9, "frac": dec_bytes / avg_dec / 1e9 / peak,
+                       "avg_launch_ms": avg_dec * 1e3, "algorithmic_bytes_per_launch": dec_bytes},
+            "what": "per step and layer: append 1 token per sequence (k_append_rows), decode (k_plan when the "
+                    "batch changes, k_decode_tc, k_combine); device-resident inputs; KV larger than L2"}
+
+
+# ------------------------------------------------------------------ checkpoint round trip (config 5)
+class _DeviceBytes:
+    """Zero-copy view of device memory the library owns, for torch."""
+
+    def __init__(self, ptr, nbytes):
+        self.__cuda_array_interface__ = {"shape": (int(nbytes),), "typestr": "|u1", "data": (int(ptr), False),
+                                         "version": 3}
+
+
+def _pool_views(cache, torch, dev):
+    d = cache.pool().describe()
+    rows = d.n_layers * d.num_blocks * d.block_size
+    return (torch.as_tensor(_DeviceBytes(d.qs, rows * 32 * d.nblk), device=dev),
+            torch.as_tensor(_DeviceBytes(d.sc, rows * 2 * d.nblk), device=dev))
+
+
+def checkpoint_roundtrip(kvcu, torch, dev, cache, local_rank, rank, NL, nb, n, directory):
+    """saveToFile / loadFromFile of this rank's whole cache (the v2 container:
+    header, every sequence's length and block table, the full Q8_0 pool in the
+    reference's 34-byte block order) into a fresh cache, compared bit for bit:
+    the payload and scale pools on the device, lengths and tables on the host."""
+    import shutil
+    import tempfile
+
+    directory = directory or tempfile.gettempdir()
+    need = cache.pool().describe().checkpoint_bytes + 64 * 1024 * 1024
+    free = shutil.disk_usage(directory).free
+    if free < need:
+        return {"skipped": f"{free / 1e9:.1f} GB free in {directory}, the file needs {need / 1e9:.1f} GB"}
+    path = os.path.join(directory, f"kvcache_ckpt_rank{rank}_{os.getpid()}.bin")
+    torch.cuda.synchronize()
+    try:
+        t0 = time.perf_counter()
+        cache.saveToFileV2(path)
+        t_save = time.perf_counter() - t0
+        size = os.path.getsize(path)
+        fresh = kvcu.KVCache.with_blocks(NL, R, P, nb, BS, quantized=True, device=local_rank)
+        t0 = time.perf_counter()
+        fresh.loadFromFileV2(path)
+        t_load = time.perf_counter() - t0
+    finally:
+        if os.path.exists(path):
+            os.remove(path)
+    same_meta = fresh.num_seqs == cache.num_seqs and all(
+        fresh.seq_len(i) == cache.seq_len(i) and np.array_equal(fresh.seq_block_table(i), cache.seq_block_table(i))
+        for i in range(cache.num_seqs))
+    qa, sa = _pool_views(cache, torch, dev)
+    qb, sb = _pool_views(fresh, torch, dev)
+    same_pool = bool(torch.equal(qa, qb)) and bool(torch.equal(sa, sb))
+    pool_bytes = qa.numel() + sa.numel()
+    del qa, sa, qb, sb
+    fresh.close()
+    return {"bytes": size, "pool_bytes": pool_bytes, "sequences": n, "bit_exact": bool(same_meta and same_pool),
+            "save_GB/s": size / t_save / 1e9, "load_GB/s": size / t_load / 1e9, "save_s": t_save, "load_s": t_load,
+            "what": "kvcache_save_to_file_v2 -> kvcache_load_from_file_v2 into a fresh cache; pools compared on the "
+                    "device, lengths and block tables on the host; outside the timed region"}
+
+
+# ------------------------------------------------------------------ multi-GPU output check
+def multi_gpu_check(kvcu, torch, dist, dev, local_rank, rank, world, parts, lens_all, n_appended, layer, outs_layer):
+    """Outputs of the last timed step for a sample of every rank's sequences
+    (its shortest and its median-length one), gathered to rank 0 with an NCCL
+    all-gather, against the same sequences decoded alone in a fresh cache on
+    rank 0's GPU (rebuilt from the seeded generator).  Returns the max relative
+    error per (sequence, head) row on rank 0, None elsewhere."""
+    per_rank = 2
+    picks = []
+    for p in parts:
+        o = sorted(p, key=lambda s: (int(lens_all[s]), s))
+        picks.append([o[0], o[len(o) // 2]] if o else [])
+    mine = [parts[rank].index(s) for s in picks[rank]]
+    local = torch.zeros((per_rank, H, R), dtype=torch.float32, device=dev)
+    if mine:
+        local[:len(mine)] = outs_layer[torch.tensor(mine, device=dev)]
+    if world > 1:
+        bufs = [torch.empty_like(local) for _ in range(world)]
+        dist.all_gather(bufs, local)
+    else:
+        bufs = [local]
+    if rank != 0:
+        return None
+    sample = [s for p in picks for s in p]
+    got = torch.cat([bufs[r][:len(picks[r])] for r in range(world)])
+    L = np.array([int(lens_all[s]) + n_appended for s in sample], np.int64)
+    m = len(sample)
+    nb = int(sum((int(x) + BS - 1) // BS for x in L)) + 4
+    ref = kvcu.KVCache.with_blocks(layer + 1, R, P, nb, BS, quantized=True, device=local_rank)
+    for _ in range(m - 1):
+        ref.seq_create()
+    ids = np.arange(m, dtype=np.uint32)
+    for i in range(m):
+        ref.seq_ensure_capacity(i, int(L[i]))
+    ref.prefill_synthetic(layer, ids, L, SEED, OUTLIER_P, seq_tags=np.array(sample, np.int64))
+    qtag = (np.array(sample, np.int64) * 64)[:, None] + np.arange(H)[None, :]
+    qb = torch.from_numpy(qtag.reshape(-1).astype(np.int32)).to(dev)
+    qc = torch.zeros(m * H, dtype=torch.int32, device=dev)
+    q = torch.empty((m, H, W), dtype=torch.float32, device=dev)
+    kvcu.synth_rows(SEED + 1, 100 + layer, qb, qc, W, q.view(m * H, W), 0.0)
+    want = torch.empty((m, H, R), dtype=torch.float32, device=dev)
+    ref.mlaDecode_dev(layer, ids, q, SCALE, want)
+    torch.cuda.synchronize()
+    status = ref.pool().status()
+    ref.close()
+    g, w = got.double(), want.double()
+    den = w.abs().amax(dim=-1)
+    err = ((g - w).abs().amax(dim=-1) / torch.where(den > 0, den, torch.ones_like(den))).max().item()
+    return {"max_rel_err": err, "tolerance": 1e-3, "ok": bool(err <= 1e-3 and status == 0), "layer": layer,
+            "sequences": m, "ctx_tokens": int(L.sum()),
+            "gather": "NCCL all_gather of each rank's sample rows to rank 0" if world > 1 else "single rank",
+            "reference": "the same sequences decoded alone in a fresh cache on rank 0's GPU, rebuilt from the "
+                         "seeded generator"}
 
 
 def physical_gpu(local_rank):
@@ -393,6 +593,11 @@ def run_ours(args, rank, world, local_rank):
     barrier()
     torch.cuda.synchronize()
     elapsed = t_start.elapsed_time(t_end) / 1e3
+    # outputs of the last timed step, checked outside the timed region: a sample
+    # of every rank's sequences gathered to rank 0 (NCCL) against the same
+    # sequences decoded alone there
+    mg_check = multi_gpu_check(kvcu, torch, dist, dev, local_rank, rank, world, parts, lens_all, W_steps, NL - 1,
+                               outs[NL - 1])
     launches = ev["launches"]
     # decode kernel roofline (per launch = one layer's decode)
     dec_ms = [e0.elapsed_time(e1) for e0, e1, _ in ev["dec"]]
@@ -440,10 +645,18 @@ def run_ours(args, rank, world, local_rank):
 
     mla = measure_mla_step(cache, ids, lens0 + base + args.e2e_warmup + args.e2e_steps, NL, args.mla_steps,
                            torch, dev, st)
-    append_gbs = measure_append(kvcu, torch, dev, local_rank)
+    append_gbs, gather_gbs = measure_append(kvcu, torch, dev, local_rank)
     clk_sum = clk.summary()
 
     peak, peak_kind = read_peaks()
+    c4 = None if args.no_config4 else measure_config4(kvcu, torch, dev, local_rank, peak)
+    ckpt = None if args.no_checkpoint else checkpoint_roundtrip(kvcu, torch, dev, cache, local_rank, rank, NL, nb, n,
+                                                                args.ckpt_dir)
+    if world > 1 and ckpt is not None:
+        # every rank's round trip must be exact
+        ok = torch.tensor([1.0 if ckpt.get("bit_exact") else 0.0], device=dev)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        ckpt["all_ranks_bit_exact"] = bool(ok.item() == 1.0)
     traffic_per_tok = read_traffic_profile()
     if rank == 0:
         cores = host_cores()
@@ -486,11 +699,20 @@ def run_ours(args, rank, world, local_rank):
             "gpu_launches": launches,
             "clocks": clk_sum,
             "append": {"GB/s": append_gbs, "rows": APPEND_ROWS,
-                       "bytes_per_row": 2304 + Q8_ROW_BYTES + 8,
+                       "bytes_per_row": 2304 + Q8_ROW_BYTES + 8, "frac": append_gbs / peak,
                        "what": "one batched f32->Q8_0 append through the block table (prefill-sized)"},
+            "gather": {"GB/s": gather_gbs, "rows": APPEND_ROWS, "bytes_per_row": Q8_ROW_BYTES + 8 + 2304,
+                       "frac": gather_gbs / peak,
+                       "what": "batched Q8_0 -> f32 gather/dequant through the block table (k_gather), "
+                               "302 MB out, larger than L2"},
             "mla_step": mla,
             "prefill_s": t_pre,
+            "multi_gpu_check": mg_check,
         }
+        if c4 is not None:
+            line["config4"] = c4
+        if ckpt is not None:
+            line["checkpoint_roundtrip"] = ckpt
         if cpu:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
@@ -511,6 +733,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seqs", type=int, default=N_SEQS, help="sequences (config 5: 512)")
     ap.add_argument("--layers", type=int, default=N_LAYERS, help="layers (config 5: 8)")
+    ap.add_argument("--no-config4", action="store_true", help="skip the config-4 measurement")
+    ap.add_argument("--no-checkpoint", action="store_true", help="skip the checkpoint round trip")
+    ap.add_argument("--ckpt-dir", default=None, help="directory for the checkpoint file (default: temp dir)")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

@@ -104,3 +104,66 @@ def test_fullsize_single_sequence_matches_batch_row(full):
     torch.cuda.synchronize()
     assert cache.pool().status() == 0
     assert rel_err_rows(one.cpu().numpy(), out[s:s + 1].cpu().numpy()) <= REL_TOL
+
+
+# ------------------------------------------------------------------ config 4
+C4_SEQS, C4_LAYERS, C4_LO, C4_HI, C4_SEED = 64, 4, 8192, 32768, 4
+
+
+def config4_lengths():
+    # 64 sequences, context lengths uniform in [8192, 32768]
+    return np.random.default_rng(C4_SEED).integers(C4_LO, C4_HI + 1, C4_SEQS).astype(np.int64)
+
+
+def test_config4_full_shape_step_against_oracle(oracle):
+    """Config 4 at its stated shape: 64 sequences of 8k-32k tokens, 4 layers,
+    Q8_0, block size 64, 20 heads.  One step appends one token per sequence per
+    layer, then decodes each layer; a sample (shortest, median, longest) of
+    every layer is checked against the oracle, <= 1e-3."""
+    import torch
+
+    import kvcu
+
+    kvcu.init(0)
+    lens = config4_lengths()
+    nb = int(sum((int(L) + 1 + BS - 1) // BS for L in lens)) + 8
+    cache = kvcu.KVCache.with_blocks(C4_LAYERS, 512, 64, nb, BS, quantized=True)
+    for _ in range(C4_SEQS - 1):
+        cache.seq_create()
+    ids = np.arange(C4_SEQS, dtype=np.uint32)
+    for i in range(C4_SEQS):
+        cache.seq_ensure_capacity(i, int(lens[i]) + 1)
+    gen = torch.Generator(device="cuda").manual_seed(C4_SEED)
+    outs = []
+    for layer in range(C4_LAYERS):
+        cache.prefill_synthetic(layer, ids, lens, C4_SEED, OUTLIER_P)
+    for layer in range(C4_LAYERS):  # the step: append one token, then decode
+        cache.prefill_synthetic(layer, ids, lens + 1, C4_SEED, OUTLIER_P, start=lens)
+        q = torch.randn((C4_SEQS, H, W), device="cuda", generator=gen)
+        out = torch.empty((C4_SEQS, H, 512), device="cuda")
+        cache.mlaDecode_dev(layer, ids, q, SCALE, out)
+        outs.append((q, out))
+    torch.cuda.synchronize()
+    assert cache.pool().status() == 0
+    assert all(cache.seq_len(i) == int(lens[i]) + 1 for i in range(C4_SEQS))
+    order = np.argsort(lens)
+    sample = [int(order[0]), int(order[C4_SEQS // 2]), int(order[-1])]
+    L = [int(lens[s]) + 1 for s in sample]
+    for layer in range(C4_LAYERS):
+        nbo = sum((x + BS - 1) // BS for x in L) + 1
+        pool = oracle.Pool(1, nbo, BS, 512, 64, True)
+        offs, tabs, k = [0], [], 0
+        for i, s in enumerate(sample):
+            need = (L[i] + BS - 1) // BS
+            tabs.extend(range(k, k + need))
+            k += need
+            offs.append(len(tabs))
+            rows = oracle.gen_rows(C4_SEED, layer, np.full(L[i], s, np.uint32), np.arange(L[i], dtype=np.uint32),
+                                   W, OUTLIER_P)
+            t = np.arange(L[i])
+            pool.put_rows(0, np.array(tabs[offs[i]:offs[i + 1]], np.uint32)[t // BS], t % BS, rows)
+        q, out = outs[layer]
+        want = pool.attention_batch(0, np.array(offs, np.uint32), np.array(tabs, np.uint32), np.array(L, np.uint32),
+                                    q[sample].cpu().numpy(), SCALE, n_threads=16)
+        assert rel_err_rows(out[sample].cpu().numpy(), want) <= REL_TOL, layer
+    cache.deinit()
