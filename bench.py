@@ -510,7 +510,10 @@ def run_ours(args, rank, world, local_rank):
     mine = np.array(parts[rank], np.int64)
     lens0 = lens_all[mine]
     n = mine.size
-    total_steps = args.warmup + args.steps + args.e2e_warmup + args.e2e_steps + 1 + args.mla_steps
+    # step indices: timed layered steps, per-layer steps (2 warm + steps), e2e
+    # (layered then per-layer), then the MLA steps
+    total_steps = (args.warmup + args.steps + 2 + args.steps + args.e2e_warmup + 2 * args.e2e_steps + 1 + 1
+                   + args.mla_steps)
     nb = int(sum((int(L) + total_steps + BS - 1) // BS for L in lens0)) + 8
     cache = kvcu.KVCache.with_blocks(NL, R, P, nb, BS, quantized=True, device=local_rank)
     for _ in range(n - 1):
@@ -549,24 +552,56 @@ def run_ours(args, rank, world, local_rank):
 
     ev = {"dec": [], "launches": 0}
 
-    def step(k, timed):
+    def step(k, timed, per_layer=False):
+        """One serving step: append one token per sequence in every layer, then
+        decode every layer.  Default: all layers in one append launch and one
+        persistent decode launch (the layers' inputs of this synthetic step are
+        all known up front); per_layer: the call sequence a model's layer loop
+        makes (append + decode per layer)."""
         pos_h = (lens0 + k).astype(np.uint32)
-        for layer in range(NL):
-            cache.appendBatch_dev(layer, ids, pos_h, ids_dev, pos_dev[k], rows[k, layer], st)
-            ev["launches"] += cache.last_launches
-            if timed:
-                e0 = torch.cuda.Event(enable_timing=True)
-                e1 = torch.cuda.Event(enable_timing=True)
-                e0.record(st)
-            cache.mlaDecode_dev(layer, ids, qs[layer], SCALE, outs[layer], st)
-            ev["launches"] += cache.last_launches
-            if timed:
-                e1.record(st)
-                ev["dec"].append((e0, e1, layer))
+        rk = rows[k % W_steps]
+        if per_layer:
+            for layer in range(NL):
+                cache.appendBatch_dev(layer, ids, pos_h, ids_dev, pos_dev[k], rk[layer], st)
+                ev["launches"] += cache.last_launches
+                if timed:
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record(st)
+                cache.mlaDecode_dev(layer, ids, qs[layer], SCALE, outs[layer], st)
+                ev["launches"] += cache.last_launches
+                if timed:
+                    e1.record(st)
+                    ev["dec"].append((e0, e1, 1))
+            return
+        cache.appendLayers_dev(0, ids, pos_h, ids_dev, pos_dev[k], rk, st)
+        ev["launches"] += cache.last_launches
+        if timed:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+        cache.mlaDecodeLayers_dev(0, ids, qs, SCALE, outs, st)
+        ev["launches"] += cache.last_launches
+        if timed:
+            e1.record(st)
+            ev["dec"].append((e0, e1, NL))
 
     def barrier():
         if world > 1:
             dist.barrier()
+
+    def timed_steps(k0, count, per_layer):
+        """`count` steps from step index k0 between CUDA events on the stream;
+        returns (seconds, ctx tokens attended over all layers)."""
+        ev["dec"].clear()
+        ev["launches"] = 0
+        toks = 0
+        t_a, t_b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t_a.record(st)
+        for k in range(k0, k0 + count):
+            step(k, True, per_layer)
+            toks += int((lens0 + k + 1).sum()) * NL
+        t_b.record(st)
+        st.synchronize()
+        return t_a, t_b, toks
 
     # the clock sampler runs from before the warm-up (nvidia-smi takes a moment to
     # start); only the samples that arrive inside the timed region are kept
@@ -576,35 +611,28 @@ def run_ours(args, rank, world, local_rank):
         st.synchronize()
         barrier()
         torch.cuda.synchronize()
-        ev["launches"] = 0
-        ctx_tokens = 0
-        t_start = torch.cuda.Event(enable_timing=True)
-        t_end = torch.cuda.Event(enable_timing=True)
         h0 = time.perf_counter()
         torch.cuda.nvtx.range_push("timed")
-        t_start.record(st)
-        for k in range(args.warmup, args.warmup + args.steps):
-            step(k, True)
-            ctx_tokens += int((lens0 + k + 1).sum()) * NL
-        t_end.record(st)
+        t_start, t_end, ctx_tokens = timed_steps(args.warmup, args.steps, False)
         torch.cuda.nvtx.range_pop()
-        st.synchronize()
         clk.mark(h0, time.perf_counter())
     barrier()
     torch.cuda.synchronize()
     elapsed = t_start.elapsed_time(t_end) / 1e3
+    launches = ev["launches"]
+    # decode kernel roofline: one launch covers `nl` layers of one step
+    dec_ms = [e0.elapsed_time(e1) for e0, e1, _ in ev["dec"]]
+    layers_per_launch = ev["dec"][0][2]
+    avg_dec = sum(dec_ms) / len(dec_ms) / 1e3
+    avg_ctx_per_launch = ctx_tokens / len(dec_ms)
+    tables_bytes = 4 * sum((int(L) + BS - 1) // BS for L in lens0)
+    dec_bytes = (avg_ctx_per_launch * Q8_ROW_BYTES + layers_per_launch * (n * H * W * 4 + n * H * R * 4)
+                 + tables_bytes)
     # outputs of the last timed step, checked outside the timed region: a sample
     # of every rank's sequences gathered to rank 0 (NCCL) against the same
     # sequences decoded alone there
     mg_check = multi_gpu_check(kvcu, torch, dist, dev, local_rank, rank, world, parts, lens_all, W_steps, NL - 1,
                                outs[NL - 1])
-    launches = ev["launches"]
-    # decode kernel roofline (per launch = one layer's decode)
-    dec_ms = [e0.elapsed_time(e1) for e0, e1, _ in ev["dec"]]
-    avg_dec = sum(dec_ms) / len(dec_ms) / 1e3
-    avg_ctx_per_launch = ctx_tokens / len(dec_ms)
-    tables_bytes = 4 * sum((int(L) + BS - 1) // BS for L in lens0)
-    dec_bytes = (avg_ctx_per_launch * Q8_ROW_BYTES + n * H * W * 4 + n * H * R * 4 + tables_bytes)
 
     # ---- cross-rank aggregation (outside the timed region)
     job_tokens, job_time = aggregate_throughput(ctx_tokens, elapsed, dist if world > 1 else None, dev)
@@ -612,38 +640,66 @@ def run_ours(args, rank, world, local_rank):
     dec_gbs = aggregate_throughput(dec_bytes / avg_dec, 0.0, dist if world > 1 else None, dev)[0] / world / 1e9
     value = job_tokens / job_time
 
+    # ---- the same steps as a model's layer loop issues them (append + decode per layer)
+    k_pl = W_steps
+    for k in range(k_pl, k_pl + 2):
+        step(k, False, True)
+    barrier()
+    torch.cuda.synchronize()
+    pl_a, pl_b, pl_tokens = timed_steps(k_pl + 2, args.steps, True)
+    pl_dec = sum(e0.elapsed_time(e1) for e0, e1, _ in ev["dec"]) / len(ev["dec"]) / 1e3
+    pl_tok, pl_time = aggregate_throughput(pl_tokens, pl_a.elapsed_time(pl_b) / 1e3, dist if world > 1 else None,
+                                           dev)
+    per_layer = {"value": pl_tok / pl_time, "unit": UNIT, "ms_per_step": 1e3 * pl_time / args.steps,
+                 "avg_decode_layer_ms": pl_dec * 1e3,
+                 "what": "the same config-5 steps issued per layer (append launch, decode + combine per layer), as "
+                         "a model's layer loop calls the cache"}
+
     # ---- e2e through the host-buffer API (pinned host memory, copies inside)
     q_host = qs.cpu().pin_memory()
     out_host = torch.empty((NL, n, H, R), dtype=torch.float32).pin_memory()
     rows_host = torch.empty((NL, n, W), dtype=torch.float32).pin_memory()
     rows_host.copy_(rows[0])  # same distribution; content does not change the work
-    base = W_steps
+    base = k_pl + 2 + args.steps
 
-    def e2e_step(k):
+    def e2e_step(k, per_layer=False):
         pos_h = (lens0 + base + k).astype(np.uint32)
-        for layer in range(NL):
-            cache.appendBatch(layer, ids, pos_h, rows_host[layer].numpy())
-            cache.mlaDecode_ptr(layer, n, ids, q_host[layer].data_ptr(), H, SCALE, out_host[layer].data_ptr())
-            _ = out_host[layer, 0, 0, 0].item()
+        if per_layer:
+            for layer in range(NL):
+                cache.appendBatch(layer, ids, pos_h, rows_host[layer].numpy())
+                cache.mlaDecode_ptr(layer, n, ids, q_host[layer].data_ptr(), H, SCALE, out_host[layer].data_ptr())
+                _ = out_host[layer, 0, 0, 0].item()
+            return
+        # one call for the whole step: appends and decodes of every layer, one synchronise
+        cache.appendDecodeLayers_ptr(0, NL, n, ids, pos_h, rows_host.data_ptr(), q_host.data_ptr(), H, SCALE,
+                                     out_host.data_ptr())
+        _ = out_host[NL - 1, 0, 0, 0].item()
+
+    def e2e_run(k0, count, per_layer):
+        barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        toks = 0
+        for k in range(k0, k0 + count):
+            e2e_step(k, per_layer)
+            toks += int((lens0 + base + k + 1).sum()) * NL
+        torch.cuda.synchronize()
+        secs = time.perf_counter() - t0
+        tok, tm = aggregate_throughput(toks, secs, dist if world > 1 else None, dev)
+        return tok / tm if tm > 0 else None
 
     for k in range(args.e2e_warmup):
         e2e_step(k)
-    barrier()
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    e2e_tokens = 0
-    for k in range(args.e2e_warmup, args.e2e_warmup + args.e2e_steps):
-        e2e_step(k)
-        e2e_tokens += int((lens0 + base + k + 1).sum()) * NL
-    torch.cuda.synchronize()
-    e2e_time = time.perf_counter() - t0
+    e2e_value = e2e_run(args.e2e_warmup, args.e2e_steps, False)
     e2e_mapped = cache.last_decode_mapped
-    e_tok, e_time = aggregate_throughput(e2e_tokens, e2e_time, dist if world > 1 else None, dev)
-    e2e_value = e_tok / e_time if e_time > 0 else None
+    kk = args.e2e_warmup + args.e2e_steps
+    e2e_step(kk, True)  # warm the per-layer host path
+    per_layer["e2e"] = e2e_run(kk + 1, args.e2e_steps, True)
     h2d = NL * n * (W * 4 + 8 + H * W * 4)
     d2h = NL * n * H * R * 4
+    e2e_end = kk + 1 + args.e2e_steps
 
-    mla = measure_mla_step(cache, ids, lens0 + base + args.e2e_warmup + args.e2e_steps, NL, args.mla_steps,
+    mla = measure_mla_step(cache, ids, lens0 + base + e2e_end, NL, args.mla_steps,
                            torch, dev, st)
     append_gbs, gather_gbs = measure_append(kvcu, torch, dev, local_rank)
     clk_sum = clk.summary()
@@ -685,9 +741,17 @@ def run_ours(args, rank, world, local_rank):
                        "shard_tokens": loads, "l2": "inputs larger than L2 (>=0.4 GB of KV per layer per GPU)"},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h,
+                    "call": "kvcache_append_decode_layers: one host-buffer call per step (all layers), one "
+                            "synchronise",
                     "host_buffers": ("pinned; q read and out written over PCIe by the kernels"
                                      if e2e_mapped else "copied in and out around the kernels")},
-            "roofline": {"kernel": "mla_decode layer call (k_decode_tc + k_combine; 98.5% k_decode_tc)",
+            "step_form": ("all layers of a step in one append launch and one persistent decode launch "
+                          "(kvcache_append_layers_dev + kvcache_mla_decode_layers_dev); per_layer below is the same "
+                          "work issued layer by layer"),
+            "per_layer": per_layer,
+            "roofline": {"kernel": (f"multi-layer decode call ({layers_per_launch} layers: k_decode_tc + k_combine, "
+                                    "k_decode_tc ~98.5% of the device time)"),
+                         "layers_per_launch": layers_per_launch,
                          "bound": "hbm", "achieved": dec_gbs, "peak": peak, "unit": "GB/s",
                          "frac": dec_gbs / peak, "peak_source": peak_kind,
                          "traffic": (traffic_per_tok * avg_ctx_per_launch if traffic_per_tok else None),

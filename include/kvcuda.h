@@ -148,6 +148,15 @@ int kvcu_append(kvcu_pool* pool, uint32_t layer, uint32_t n_rows, const float* l
                 const uint32_t* table_offsets, const uint32_t* tables, uint32_t* lens,
                 void* stream);
 
+/* kvcu_append for layers [layer, layer + n_layers) in one launch: the rows of
+ * layer layer+i start at latent + i*latent_layer_stride and rope +
+ * i*rope_layer_stride (floats), same row_seq / row_pos for every layer. */
+int kvcu_append_layers(kvcu_pool* pool, uint32_t layer, uint32_t n_layers, uint32_t n_rows, const float* latent,
+                       uint64_t latent_stride, uint64_t latent_layer_stride, const float* rope,
+                       uint64_t rope_stride, uint64_t rope_layer_stride, const uint32_t* row_seq,
+                       const uint32_t* row_pos, uint32_t n_seqs, const uint32_t* table_offsets,
+                       const uint32_t* tables, uint32_t* lens, void* stream);
+
 /* getKVCompressed + getKPe for every position of a sequence
  * (src/kv_cache.zig:225-277): out[len][kv_rank + rope_dim] f32, dequantized
  * exactly as f16ToF32(d) * q.  `table` is a device pointer to `table_len` ids. */
@@ -213,6 +222,24 @@ int kvcu_mla_prepare(kvcu_pool* pool, uint32_t n, uint32_t n_heads, uint32_t qk_
 int kvcu_mla_finish(kvcu_pool* pool, uint32_t n, uint32_t n_heads, uint32_t v_dim, const float* q_abs,
                     const float* rows, float* latent, const float* lse, float scale, const float* v_b,
                     float* attn, void* stream);
+/* Several layers in one call, all with the workspace's last plan (the batch and
+ * lengths are the same for every layer of a step): layers [layer, layer +
+ * n_layers) of the pool, layer+i reading q + i*q_layer_stride and writing
+ * out + i*out_layer_stride (strides in floats).  The tensor-core path runs
+ * them as ONE persistent launch (every CTA takes its plan range once per
+ * layer) plus one combine, so the per-launch fill and drain are paid once per
+ * step instead of once per layer.  It suits work whose layers' queries are
+ * all known up front (a benchmark step, re-scoring a cached context, layer-
+ * parallel checks); a model's decode, where layer l+1's query depends on
+ * layer l's output (src/inference.zig:279-373), calls kvcu_mla_decode per
+ * layer.  The workspace must come from kvcu_decode_ws_create_layers with
+ * max_layers >= n_layers. */
+kvcu_decode_ws* kvcu_decode_ws_create_layers(int device, uint32_t max_batch, uint32_t max_heads,
+                                             uint32_t max_layers);
+int kvcu_mla_decode_layers(kvcu_decode_ws* ws, kvcu_pool* pool, uint32_t layer, uint32_t n_layers, uint32_t n,
+                           const uint32_t* seq_ids, uint32_t n_seqs, const uint32_t* table_offsets,
+                           const uint32_t* tables, const uint32_t* lens, const float* q, uint64_t q_layer_stride,
+                           uint32_t n_heads, float scale, float* out, uint64_t out_layer_stride, void* stream);
 /* Kernel launches the last kvcu_mla_decode issued (for launch accounting). */
 uint32_t kvcu_decode_last_launches(const kvcu_decode_ws* ws);
 /* Decode kernel selection.  AUTO uses the tcgen05 tensor-core kernel for Q8_0
@@ -355,6 +382,27 @@ int kvcache_append_batch(kvcache* c, uint32_t layer, uint32_t n, const uint32_t*
 int kvcache_append_batch_dev(kvcache* c, uint32_t layer, uint32_t n, const uint32_t* seq_ids,
                              const uint32_t* positions, const uint32_t* seq_ids_dev,
                              const uint32_t* positions_dev, const float* rows_dev, void* stream);
+/* Several layers per call, for work whose layers' rows and queries are all
+ * known up front (see kvcu_mla_decode_layers; a model's decode goes layer by
+ * layer).  Layer layer+i reads rows + i*rows_layer_stride (device, floats) and
+ * the same seq_ids / positions; the decode uses q + i*q_layer_stride and
+ * writes out + i*out_layer_stride, one multi-layer launch. */
+int kvcache_append_layers_dev(kvcache* c, uint32_t layer, uint32_t n_layers, uint32_t n, const uint32_t* seq_ids,
+                              const uint32_t* positions, const uint32_t* seq_ids_dev, const uint32_t* positions_dev,
+                              const float* rows_dev, uint64_t rows_layer_stride, void* stream);
+int kvcache_mla_decode_layers_dev(kvcache* c, uint32_t layer, uint32_t n_layers, uint32_t n,
+                                  const uint32_t* seq_ids, const float* q_dev, uint64_t q_layer_stride,
+                                  uint32_t n_heads, float scale, float* out_dev, uint64_t out_layer_stride,
+                                  void* stream);
+/* appendBatch + mlaDecode for layers [layer, layer + n_layers) in one call with
+ * HOST buffers and one synchronise: rows [n_layers][n][kv_rank+rope_dim] are
+ * appended at (seq_ids[b], positions[b]) in every layer, then each layer is
+ * decoded, q [n_layers][n][n_heads][kv_rank+rope_dim] -> out
+ * [n_layers][n][n_heads][kv_rank].  Pinned, mapped q / out are used in place
+ * (as kvcache_mla_decode does). */
+int kvcache_append_decode_layers(kvcache* c, uint32_t layer, uint32_t n_layers, uint32_t n, const uint32_t* seq_ids,
+                                 const uint32_t* positions, const float* rows, const float* q, uint32_t n_heads,
+                                 float scale, float* out);
 /* gather(layer, seq): out[len][kv_rank + rope_dim] (HOST buffer). */
 int kvcache_gather(kvcache* c, uint32_t layer, uint32_t seq, float* out);
 /* mlaDecode (the call replacing src/inference.zig:518-660): HOST q

@@ -220,7 +220,7 @@ struct kvcache {
   size_t d_stepu_cap = 0;
   // decode
   kvcu_decode_ws* ws = nullptr;
-  uint32_t ws_batch = 0, ws_heads = 0;
+  uint32_t ws_batch = 0, ws_heads = 0, ws_layers = 0;
   uint32_t* d_seq_ids = nullptr;
   size_t d_seq_ids_cap = 0;
   std::vector<uint32_t> plan_ids;
@@ -566,13 +566,14 @@ int get_row(kvcache* c, uint32_t layer, uint32_t pos, float* kv_out, float* pe_o
   return KVCU_OK;
 }
 
-int ensure_ws(kvcache* c, uint32_t n, uint32_t n_heads) {
-  if (c->ws && c->ws_batch >= n && c->ws_heads >= n_heads) return KVCU_OK;
+int ensure_ws(kvcache* c, uint32_t n, uint32_t n_heads, uint32_t n_layers = 1) {
+  if (c->ws && c->ws_batch >= n && c->ws_heads >= n_heads && c->ws_layers >= n_layers) return KVCU_OK;
   kvcu_decode_ws_destroy(c->ws);
   c->ws = nullptr;
   c->ws_batch = std::max<uint32_t>(n, std::max<uint32_t>(c->ws_batch, 16));
   c->ws_heads = std::max<uint32_t>(n_heads, c->ws_heads);
-  c->ws = kvcu_decode_ws_create(c->device, c->ws_batch, c->ws_heads);
+  c->ws_layers = std::max<uint32_t>(n_layers, std::max<uint32_t>(c->ws_layers, 1));
+  c->ws = kvcu_decode_ws_create_layers(c->device, c->ws_batch, c->ws_heads, c->ws_layers);
   if (!c->ws) return KVCU_ERR_NO_MEMORY;
   kvcu_decode_ws_set_impl(c->ws, c->decode_impl);
   c->plan_epoch = ~0ull;
@@ -580,10 +581,13 @@ int ensure_ws(kvcache* c, uint32_t n, uint32_t n_heads) {
   return KVCU_OK;
 }
 
+// Decode layers [layer, layer + n_layers) of a batch (q / out of layer+i at
+// + i * the stride, floats); n_layers > 1 runs as one multi-layer launch.
 int decode_impl(kvcache* c, uint32_t layer, uint32_t n, const uint32_t* seq_ids, const float* q_dev,
-                uint32_t n_heads, float scale, float* out_dev, cudaStream_t st) {
-  if (layer >= c->n_layers) {
-    kvcu_set_error("LayerOutOfBounds: layer %u >= %u", layer, c->n_layers);
+                uint32_t n_heads, float scale, float* out_dev, cudaStream_t st, uint32_t n_layers = 1,
+                uint64_t q_lstride = 0, uint64_t out_lstride = 0) {
+  if (n_layers == 0 || layer >= c->n_layers || n_layers > c->n_layers - layer) {
+    kvcu_set_error("LayerOutOfBounds: layers [%u, %u + %u) of %u", layer, layer, n_layers, c->n_layers);
     return KVCU_ERR_LAYER_OOB;
   }
   for (uint32_t b = 0; b < n; ++b)
@@ -591,7 +595,7 @@ int decode_impl(kvcache* c, uint32_t layer, uint32_t n, const uint32_t* seq_ids,
       kvcu_set_error("sequence %u does not exist", seq_ids[b]);
       return KVCU_ERR_INVALID_ARG;
     }
-  int rc = ensure_ws(c, n, n_heads);
+  int rc = ensure_ws(c, n, n_heads, n_layers);
   if (!rc) rc = sync_tables(c, st);
   if (!rc) rc = sync_lens(c, st);
   if (rc) return rc;
@@ -616,8 +620,13 @@ int decode_impl(kvcache* c, uint32_t layer, uint32_t n, const uint32_t* seq_ids,
     c->plan_epoch = c->epoch;
     c->plan_tokens = tokens;
   }
-  rc = kvcu_mla_decode(c->ws, c->pool, layer, n, c->d_seq_ids, (uint32_t)c->seqs.size(), c->d_toff,
-                       c->d_tables, c->d_lens, q_dev, n_heads, scale, out_dev, st);
+  if (n_layers == 1)
+    rc = kvcu_mla_decode(c->ws, c->pool, layer, n, c->d_seq_ids, (uint32_t)c->seqs.size(), c->d_toff,
+                         c->d_tables, c->d_lens, q_dev, n_heads, scale, out_dev, st);
+  else
+    rc = kvcu_mla_decode_layers(c->ws, c->pool, layer, n_layers, n, c->d_seq_ids, (uint32_t)c->seqs.size(),
+                                c->d_toff, c->d_tables, c->d_lens, q_dev, q_lstride, n_heads, scale, out_dev,
+                                out_lstride, st);
   if (rc) return rc;
   c->last_launches = launches + kvcu_decode_last_launches(c->ws);
   return KVCU_OK;
@@ -884,6 +893,99 @@ int kvcache_append_batch_dev(kvcache* c, uint32_t layer, uint32_t n, const uint3
   c->last_launches = 1;
   bump_lens(c, n, seq_ids, positions);  // the kernel already advanced d_lens identically
   return KVCU_OK;
+}
+
+int kvcache_append_layers_dev(kvcache* c, uint32_t layer, uint32_t n_layers, uint32_t n, const uint32_t* seq_ids,
+                              const uint32_t* positions, const uint32_t* seq_ids_dev, const uint32_t* positions_dev,
+                              const float* rows_dev, uint64_t rows_layer_stride, void* stream) {
+  if (!c || (n && (!seq_ids || !positions || !seq_ids_dev || !positions_dev || !rows_dev)))
+    return KVCU_ERR_INVALID_ARG;
+  if (n_layers == 0 || layer >= c->n_layers || n_layers > c->n_layers - layer) {
+    kvcu_set_error("LayerOutOfBounds: layers [%u, %u + %u) of %u", layer, layer, n_layers, c->n_layers);
+    return KVCU_ERR_LAYER_OOB;
+  }
+  if (!n) return KVCU_OK;
+  DevScope d(c->device);
+  const cudaStream_t st = (cudaStream_t)stream;
+  int rc = validate_positions(c, layer, n, seq_ids, positions);
+  if (!rc) rc = cow_for_write(c, n, seq_ids, positions, st);
+  if (!rc) rc = sync_tables(c, st);
+  if (!rc) rc = sync_lens(c, st);
+  if (rc) return rc;
+  const uint32_t Wd = c->row_width();
+  rc = kvcu_append_layers(c->pool, layer, n_layers, n, rows_dev, Wd, rows_layer_stride, rows_dev + c->kv_rank, Wd,
+                          rows_layer_stride, seq_ids_dev, positions_dev, (uint32_t)c->seqs.size(), c->d_toff,
+                          c->d_tables, c->d_lens, stream);
+  if (rc) return rc;
+  c->last_launches = 1;
+  bump_lens(c, n, seq_ids, positions);  // the kernel already advanced d_lens identically
+  return KVCU_OK;
+}
+
+int kvcache_mla_decode_layers_dev(kvcache* c, uint32_t layer, uint32_t n_layers, uint32_t n,
+                                  const uint32_t* seq_ids, const float* q_dev, uint64_t q_layer_stride,
+                                  uint32_t n_heads, float scale, float* out_dev, uint64_t out_layer_stride,
+                                  void* stream) {
+  if (!c || (n && (!seq_ids || !q_dev || !out_dev))) return KVCU_ERR_INVALID_ARG;
+  if (!n) return KVCU_OK;
+  DevScope d(c->device);
+  return decode_impl(c, layer, n, seq_ids, q_dev, n_heads, scale, out_dev, (cudaStream_t)stream, n_layers,
+                     q_layer_stride, out_layer_stride);
+}
+
+int kvcache_append_decode_layers(kvcache* c, uint32_t layer, uint32_t n_layers, uint32_t n, const uint32_t* seq_ids,
+                                 const uint32_t* positions, const float* rows, const float* q, uint32_t n_heads,
+                                 float scale, float* out) {
+  if (!c || (n && (!seq_ids || !positions || !rows || !q || !out))) return KVCU_ERR_INVALID_ARG;
+  if (n_layers == 0 || layer >= c->n_layers || n_layers > c->n_layers - layer) {
+    kvcu_set_error("LayerOutOfBounds: layers [%u, %u + %u) of %u", layer, layer, n_layers, c->n_layers);
+    return KVCU_ERR_LAYER_OOB;
+  }
+  if (!n) return KVCU_OK;
+  DevScope d(c->device);
+  const cudaStream_t st = c->stream;
+  const uint32_t Wd = c->row_width();
+  // ---- the appends: rows by one DMA, row indices through pinned staging, one launch for all layers
+  int rc = validate_positions(c, layer, n, seq_ids, positions);
+  if (!rc) rc = cow_for_write(c, n, seq_ids, positions, st);
+  if (!rc) rc = sync_tables(c, st);
+  if (!rc) rc = sync_lens(c, st);
+  const size_t rows_n = (size_t)n_layers * n * Wd;
+  if (!rc) rc = ensure_dev(&c->d_step, &c->d_step_cap, rows_n);
+  if (!rc) rc = ensure_dev(&c->d_u, &c->d_u_cap, (size_t)2 * n);
+  if (!rc) rc = stage_acquire(c->up_rowidx, (size_t)2 * n);
+  if (rc) return rc;
+  KVCU_CUDA(cudaMemcpyAsync(c->d_step, rows, rows_n * 4, cudaMemcpyHostToDevice, st));
+  memcpy(c->up_rowidx.p, seq_ids, (size_t)n * 4);
+  memcpy(c->up_rowidx.p + n, positions, (size_t)n * 4);
+  rc = stage_upload(c->up_rowidx, c->d_u, (size_t)2 * n, st);
+  if (!rc)
+    rc = kvcu_append_layers(c->pool, layer, n_layers, n, c->d_step, Wd, (uint64_t)n * Wd, c->d_step + c->kv_rank,
+                            Wd, (uint64_t)n * Wd, c->d_u, c->d_u + n, (uint32_t)c->seqs.size(), c->d_toff,
+                            c->d_tables, c->d_lens, st);
+  if (rc) return rc;
+  bump_lens(c, n, seq_ids, positions);
+  uint32_t launches = 1;
+  // ---- the decode of every layer: q / out in place when pinned and mapped, else copied
+  const uint64_t qs = (uint64_t)n * n_heads * Wd, os = (uint64_t)n * n_heads * c->kv_rank;
+  const void* q_map = mapped_host_range(q, (size_t)n_layers * qs * 4);
+  void* out_map = q_map ? mapped_host_range(out, (size_t)n_layers * os * 4) : nullptr;
+  c->last_mapped = (q_map && out_map) ? 1 : 0;
+  if (c->last_mapped) {
+    rc = decode_impl(c, layer, n, seq_ids, static_cast<const float*>(q_map), n_heads, scale,
+                     static_cast<float*>(out_map), st, n_layers, qs, os);
+    if (rc) return rc;
+  } else {
+    rc = ensure_dev(&c->d_f, &c->d_f_cap, (size_t)n_layers * qs);
+    if (!rc) rc = ensure_dev(&c->d_f2, &c->d_f2_cap, (size_t)n_layers * os);
+    if (rc) return rc;
+    KVCU_CUDA(cudaMemcpyAsync(c->d_f, q, (size_t)n_layers * qs * 4, cudaMemcpyHostToDevice, st));
+    rc = decode_impl(c, layer, n, seq_ids, c->d_f, n_heads, scale, c->d_f2, st, n_layers, qs, os);
+    if (rc) return rc;
+    KVCU_CUDA(cudaMemcpyAsync(out, c->d_f2, (size_t)n_layers * os * 4, cudaMemcpyDeviceToHost, st));
+  }
+  c->last_launches += launches;
+  return check_status(c);  // the one synchronise: out is complete, rows / q may be reused
 }
 
 int kvcache_gather(kvcache* c, uint32_t layer, uint32_t seq, float* out) {

@@ -292,6 +292,28 @@ int kvcu_append(kvcu_pool* p, uint32_t layer, uint32_t n_rows, const float* late
                             row_pos, n_seqs, table_offsets, tables, lens, (cudaStream_t)stream);
 }
 
+int kvcu_append_layers(kvcu_pool* p, uint32_t layer, uint32_t n_layers, uint32_t n_rows, const float* latent,
+                       uint64_t latent_stride, uint64_t latent_layer_stride, const float* rope,
+                       uint64_t rope_stride, uint64_t rope_layer_stride, const uint32_t* row_seq,
+                       const uint32_t* row_pos, uint32_t n_seqs, const uint32_t* table_offsets,
+                       const uint32_t* tables, uint32_t* lens, void* stream) {
+  if (!valid_pool(p)) return KVCU_ERR_INVALID_ARG;
+  if (n_layers == 0 || layer >= p->n_layers || n_layers > p->n_layers - layer) {
+    kvcu_set_error("kvcu_append_layers: layers [%u, %u + %u) outside the pool's %u", layer, layer, n_layers,
+                   p->n_layers);
+    return KVCU_ERR_LAYER_OOB;
+  }
+  if (n_rows && (!latent || !rope || !row_seq || !row_pos || !table_offsets || !tables)) {
+    kvcu_set_error("kvcu_append_layers: null pointer argument");
+    return KVCU_ERR_INVALID_ARG;
+  }
+  DeviceGuard g(p->device);
+  if (g.rc) return g.rc;
+  return kvcu_launch_append_layers(p, layer, n_layers, n_rows, latent, latent_stride, latent_layer_stride, rope,
+                                   rope_stride, rope_layer_stride, row_seq, row_pos, n_seqs, table_offsets, tables,
+                                   lens, (cudaStream_t)stream);
+}
+
 int kvcu_gather(kvcu_pool* p, uint32_t layer, const uint32_t* table, uint32_t table_len,
                 uint32_t len, float* out, void* stream) {
   if (!valid_pool(p)) return KVCU_ERR_INVALID_ARG;
@@ -326,9 +348,15 @@ int kvcu_gather_rows(kvcu_pool* p, uint32_t layer, uint32_t n_rows, const uint32
 
 // ---------------------------------------------------------------- decode
 kvcu_decode_ws* kvcu_decode_ws_create(int device, uint32_t max_batch, uint32_t max_heads) {
-  if (!max_batch || !max_heads || max_heads > 32) {
-    kvcu_set_error("kvcu_decode_ws_create: max_batch=%u max_heads=%u (heads must be 1..32)",
-                   max_batch, max_heads);
+  return kvcu_decode_ws_create_layers(device, max_batch, max_heads, 1);
+}
+
+kvcu_decode_ws* kvcu_decode_ws_create_layers(int device, uint32_t max_batch, uint32_t max_heads,
+                                             uint32_t max_layers) {
+  if (!max_batch || !max_heads || max_heads > 32 || !max_layers) {
+    kvcu_set_error("kvcu_decode_ws_create: max_batch=%u max_heads=%u max_layers=%u (heads must be 1..32, "
+                   "layers >= 1)",
+                   max_batch, max_heads, max_layers);
     return nullptr;
   }
   if (kvcu_init(device) != KVCU_OK) return nullptr;
@@ -340,6 +368,7 @@ kvcu_decode_ws* kvcu_decode_ws_create(int device, uint32_t max_batch, uint32_t m
   ws->device = device;
   ws->max_batch = max_batch;
   ws->max_heads = max_heads;
+  ws->max_layers = max_layers;
   int rc = kvcu_decode_setup(ws);
   // items <= batch + ranges - 1 (each cut between CTA ranges splits at most one entry)
   ws->max_ranges = (uint32_t)ws->decode_ctas;
@@ -352,8 +381,9 @@ kvcu_decode_ws* kvcu_decode_ws_create(int device, uint32_t max_batch, uint32_t m
                          "cudaMalloc(ranges)");
   if (!rc) rc = kvcu_check_cuda(cudaMalloc(&ws->seq_first, max_batch * 4ull), "cudaMalloc");
   if (!rc) rc = kvcu_check_cuda(cudaMalloc(&ws->seq_count, max_batch * 4ull), "cudaMalloc");
-  if (!rc) rc = kvcu_check_cuda(cudaMalloc(&ws->part_o, mi * max_heads * 512ull * 4), "cudaMalloc");
-  if (!rc) rc = kvcu_check_cuda(cudaMalloc(&ws->part_ml, mi * max_heads * 2ull * 4), "cudaMalloc");
+  const uint64_t ml = (uint64_t)max_layers;
+  if (!rc) rc = kvcu_check_cuda(cudaMalloc(&ws->part_o, ml * mi * max_heads * 512ull * 4), "cudaMalloc");
+  if (!rc) rc = kvcu_check_cuda(cudaMalloc(&ws->part_ml, ml * mi * max_heads * 2ull * 4), "cudaMalloc");
   if (!rc) rc = kvcu_check_cuda(cudaMemset(ws->meta, 0, 4 * sizeof(uint32_t)), "cudaMemset");
   if (rc) {
     kvcu_decode_ws_destroy(ws);
@@ -405,6 +435,30 @@ int kvcu_mla_decode(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint32_t n
   if (g.rc) return g.rc;
   return kvcu_launch_decode(ws, p, layer, n, seq_ids, n_seqs, table_offsets, tables, lens, q,
                             n_heads, scale, out, nullptr, (cudaStream_t)stream);
+}
+
+int kvcu_mla_decode_layers(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint32_t n_layers, uint32_t n,
+                           const uint32_t* seq_ids, uint32_t n_seqs, const uint32_t* table_offsets,
+                           const uint32_t* tables, const uint32_t* lens, const float* q, uint64_t q_layer_stride,
+                           uint32_t n_heads, float scale, float* out, uint64_t out_layer_stride, void* stream) {
+  if (!ws || !valid_pool(p)) return KVCU_ERR_INVALID_ARG;
+  if (ws->device != p->device) return KVCU_ERR_INVALID_ARG;
+  if (n_layers == 0 || layer >= p->n_layers || n_layers > p->n_layers - layer) {
+    kvcu_set_error("kvcu_mla_decode_layers: layers [%u, %u + %u) outside the pool's %u", layer, layer, n_layers,
+                   p->n_layers);
+    return KVCU_ERR_LAYER_OOB;
+  }
+  if (n_layers > ws->max_layers) {
+    kvcu_set_error("kvcu_mla_decode_layers: %u layers, the workspace holds partials for %u", n_layers,
+                   ws->max_layers);
+    return KVCU_ERR_INVALID_ARG;
+  }
+  if (n && (!table_offsets || !tables || !lens || !q || !out)) return KVCU_ERR_INVALID_ARG;
+  DeviceGuard g(p->device);
+  if (g.rc) return g.rc;
+  return kvcu_launch_decode_layers(ws, p, layer, n_layers, n, seq_ids, n_seqs, table_offsets, tables, lens, q,
+                                   q_layer_stride, n_heads, scale, out, out_layer_stride, nullptr, 0,
+                                   (cudaStream_t)stream);
 }
 
 int kvcu_mla_decode_lse(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint32_t n,

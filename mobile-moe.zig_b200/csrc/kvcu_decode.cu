@@ -468,6 +468,9 @@ __global__ void __launch_bounds__(NT, 1) k_decode(DecodeArgs a) {
 // (ranges[c] == seq_first[b] + 1), so the cuts 1 .. G-1 enumerate the split
 // entries without a list; entries decoded as one item were written by the
 // decode kernel.  A fixed grid of warps strides over the (G-1) x H tasks.
+// Several layers decoded with one plan (n_layers_call > 1): layer i's
+// partials sit at item index i * part_lstride + item and its output / lse at
+// + i * out_lstride / lse_lstride floats; the tasks of all layers share the grid.
 constexpr int COMBINE_WARPS = 4;
 __global__ void __launch_bounds__(32 * COMBINE_WARPS) k_combine(uint32_t H, uint32_t ws_heads,
                                                                 const uint32_t* __restrict__ meta,
@@ -475,17 +478,25 @@ __global__ void __launch_bounds__(32 * COMBINE_WARPS) k_combine(uint32_t H, uint
                                                                 const kvcu_item* __restrict__ items,
                                                                 const uint32_t* __restrict__ seq_first,
                                                                 const uint32_t* __restrict__ seq_count,
-                                                                const float* __restrict__ part_o,
-                                                                const float* __restrict__ part_ml,
-                                                                float* __restrict__ out, float* __restrict__ lse) {
+                                                                const float* __restrict__ part_o_all,
+                                                                const float* __restrict__ part_ml_all,
+                                                                float* __restrict__ out_all, float* __restrict__ lse_all,
+                                                                uint32_t n_layers_call, uint64_t part_lstride,
+                                                                uint64_t out_lstride, uint64_t lse_lstride) {
   kvcu_pdl_wait();     // launched programmatically after the decode kernel
   kvcu_pdl_trigger();  // the next layer's append may start launching
   const uint32_t n_items = meta[0], G = meta[1];
   const uint32_t lane = threadIdx.x & 31u;
-  const uint32_t tasks = G > 1 ? (G - 1) * H : 0u;
+  const uint32_t per_layer = G > 1 ? (G - 1) * H : 0u;
+  const uint32_t tasks = per_layer * n_layers_call;
   for (uint32_t t = blockIdx.x * COMBINE_WARPS + (threadIdx.x >> 5); t < tasks;
        t += gridDim.x * COMBINE_WARPS) {
-    const uint32_t c = 1 + t / H, h = t % H;
+    const uint32_t li = t / per_layer, tl = t - li * per_layer;
+    const float* part_o = part_o_all + li * part_lstride * ws_heads * R;
+    const float* part_ml = part_ml_all + li * part_lstride * ws_heads * 2;
+    float* out = out_all + li * out_lstride;
+    float* lse = lse_all ? lse_all + li * lse_lstride : nullptr;
+    const uint32_t c = 1 + tl / H, h = tl % H;
     const uint32_t i = ranges[c];
     if (i == 0 || i >= n_items) continue;
     const uint32_t b = items[i].b;
@@ -522,11 +533,12 @@ __global__ void __launch_bounds__(32 * COMBINE_WARPS) k_combine(uint32_t H, uint
   }
 }
 
-int launch_combine(kvcu_decode_ws* ws, uint32_t n_heads, float* out, float* lse, cudaStream_t st) {
+int launch_combine(kvcu_decode_ws* ws, uint32_t n_heads, float* out, float* lse, cudaStream_t st,
+                   uint32_t n_layers_call = 1, uint64_t out_lstride = 0, uint64_t lse_lstride = 0) {
   // the plan makes at most min(max_ranges, decode CTAs) ranges
   uint32_t G = ws->max_ranges;
   if (ws->decode_ctas > 0 && (uint32_t)ws->decode_ctas < G) G = (uint32_t)ws->decode_ctas;
-  const uint32_t tasks = (G > 1 ? G - 1 : 1) * n_heads;
+  const uint32_t tasks = (G > 1 ? G - 1 : 1) * n_heads * n_layers_call;
   uint32_t grid = (tasks + COMBINE_WARPS - 1) / COMBINE_WARPS;
   const uint32_t cap = 8u * (uint32_t)(ws->num_sms > 0 ? ws->num_sms : 148);
   if (grid > cap) grid = cap;
@@ -535,7 +547,8 @@ int launch_combine(kvcu_decode_ws* ws, uint32_t n_heads, float* out, float* lse,
                                          ws->max_heads, (const uint32_t*)ws->meta, (const uint32_t*)ws->ranges,
                                          (const kvcu_item*)ws->items, (const uint32_t*)ws->seq_first,
                                          (const uint32_t*)ws->seq_count, (const float*)ws->part_o,
-                                         (const float*)ws->part_ml, out, lse),
+                                         (const float*)ws->part_ml, out, lse, n_layers_call,
+                                         (uint64_t)ws->max_items, out_lstride, lse_lstride),
                          "combine kernel launch");
 }
 
@@ -617,8 +630,8 @@ int kvcu_launch_decode(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint32_
   if (tc_ok && ws->impl != KVCU_DECODE_CUDA_CORE) {
     ws->last_launches = 0;
     if (n == 0) return KVCU_OK;
-    int rc = kvcu_launch_decode_tc(ws, p, layer, n, seq_ids, n_seqs, toff, tables, lens, q, n_heads,
-                                   scale, out, lse, st);
+    int rc = kvcu_launch_decode_tc(ws, p, layer, 1, n, seq_ids, n_seqs, toff, tables, lens, q, 0, n_heads,
+                                   scale, out, 0, lse, 0, st);
     if (rc) return rc;
     rc = launch_combine(ws, n_heads, out, lse, st);
     if (rc) return rc;
@@ -676,5 +689,40 @@ int kvcu_launch_decode(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint32_
   rc = launch_combine(ws, n_heads, out, lse, st);
   if (rc) return rc;
   ws->last_launches = 2;
+  return KVCU_OK;
+}
+
+int kvcu_launch_decode_layers(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint32_t n_layers_call,
+                              uint32_t n, const uint32_t* seq_ids, uint32_t n_seqs,
+                              const uint32_t* toff, const uint32_t* tables, const uint32_t* lens,
+                              const float* q, uint64_t q_lstride, uint32_t n_heads, float scale, float* out,
+                              uint64_t out_lstride, float* lse, uint64_t lse_lstride, cudaStream_t st) {
+  if (n_layers_call > ws->max_layers) {
+    kvcu_set_error("mla_decode: %u layers in one call, the workspace holds %u", n_layers_call, ws->max_layers);
+    return KVCU_ERR_INVALID_ARG;
+  }
+  const bool tc_ok = kvcu_decode_tc_supported(p, n_heads) && n_heads <= ws->max_heads && n <= ws->max_batch;
+  if (n_layers_call > 1 && tc_ok && ws->impl != KVCU_DECODE_CUDA_CORE) {
+    // one persistent launch for all layers: every CTA runs its plan range once per layer
+    ws->last_launches = 0;
+    if (n == 0) return KVCU_OK;
+    int rc = kvcu_launch_decode_tc(ws, p, layer, n_layers_call, n, seq_ids, n_seqs, toff, tables, lens, q,
+                                   q_lstride, n_heads, scale, out, out_lstride, lse, lse_lstride, st);
+    if (rc) return rc;
+    rc = launch_combine(ws, n_heads, out, lse, st, n_layers_call, out_lstride, lse_lstride);
+    if (rc) return rc;
+    ws->last_launches = 2;
+    ws->last_impl = KVCU_DECODE_TENSOR_CORE;
+    return KVCU_OK;
+  }
+  uint32_t launches = 0;
+  for (uint32_t i = 0; i < n_layers_call; ++i) {
+    const int rc = kvcu_launch_decode(ws, p, layer + i, n, seq_ids, n_seqs, toff, tables, lens, q + i * q_lstride,
+                                      n_heads, scale, out + i * out_lstride, lse ? lse + i * lse_lstride : nullptr,
+                                      st);
+    if (rc) return rc;
+    launches += ws->last_launches;
+  }
+  ws->last_launches = launches;
   return KVCU_OK;
 }

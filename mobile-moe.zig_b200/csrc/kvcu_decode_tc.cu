@@ -129,7 +129,23 @@ struct TcArgs {
   float* part_ml;
   uint32_t ws_heads;
   float* lse;  // optional [n][H] log-sum-exp (natural log) of single-item entries
+  // Layers [layer, layer + n_layers_call) in one launch, all with the same plan:
+  // layer layer+i reads q + i*q_lstride and writes out + i*out_lstride (floats),
+  // its partials at item index i*part_lstride + item, its lse at + i*lse_lstride.
+  uint32_t n_layers_call;
+  uint64_t q_lstride, out_lstride, part_lstride, lse_lstride;
 };
+
+// Work unit u of a CTA whose plan range holds `cnt` items from `it_begin`:
+// layer offset li = u / cnt, item it_begin + u % cnt (layer-major, so each
+// layer's items run in plan order).
+struct Unit {
+  uint32_t li, it;
+};
+__device__ __forceinline__ Unit unit_of(uint32_t u, uint32_t it_begin, uint32_t cnt) {
+  const uint32_t li = u / cnt;  // callers only ask for u < n_layers_call * cnt, so cnt > 0
+  return Unit{li, it_begin + (u - li * cnt)};
+}
 
 // ------------------------------------------------------------------ PTX helpers
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -491,8 +507,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const uint32_t n_items = a.meta[0], n_ranges = a.meta[1];
   const uint32_t it_begin = blockIdx.x < n_ranges ? min(a.ranges[blockIdx.x], n_items) : n_items;
   const uint32_t it_end = blockIdx.x < n_ranges ? min(a.ranges[blockIdx.x + 1], n_items) : n_items;
+  const uint32_t cnt = it_end > it_begin ? it_end - it_begin : 0u;
+  const uint32_t n_units = cnt * a.n_layers_call;
   if (blockIdx.x == 0 && threadIdx.x == 0 && n_ranges > gridDim.x) atomicOr(a.status, KVCU_STATUS_BAD_PLAN);
-  if (threadIdx.x == 0) *reinterpret_cast<volatile uint32_t*>(smem + OFF_CUR_ITEM) = it_begin;
+  if (threadIdx.x == 0) *reinterpret_cast<volatile uint32_t*>(smem + OFF_CUR_ITEM) = 0u;
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -513,8 +531,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       bool live = true;
       const uint64_t once = policy_evict_first();
       const uint32_t br = a.box_rows;
-      for (uint32_t it = it_begin; it < it_end && live; ++it) {
-        const Item im = load_item(a, it);
+      for (uint32_t u = 0; u < n_units && live; ++u) {
+        const Unit un = unit_of(u, it_begin, cnt);
+        const Item im = load_item(a, un.it);
+        const uint64_t layer = (uint64_t)a.layer + un.li;
         for (uint32_t k = 0; k < im.ntiles && live; ++k) {
           const uint32_t s = g & 1u;
           const uint32_t tt0 = im.tok0 + k * TILE;
@@ -545,8 +565,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
               const uint32_t pos = tt0 + off;
               const uint32_t blk = a.tables[im.t0 + pos / a.block_size];
               if (blk >= a.num_blocks || pos % a.block_size + br > a.block_size) continue;
-              const uint64_t row =
-                  ((uint64_t)a.layer * a.num_blocks + blk) * a.block_size + pos % a.block_size;
+              const uint64_t row = (layer * a.num_blocks + blk) * a.block_size + pos % a.block_size;
               // the segment's whole latent (4 column chunks) in one box
               tma_load_4d(stage + ST_LAT + (off >> 3) * LAT_GROUP, &map_lat, 0, 0, 0, (int)(row >> 3), full, once);
               tma_load_2d_hint(stage + ST_ROPE + off * 64u, &map_rope, 512, (int)row, full, once);
@@ -566,8 +585,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     // issues each MMA / commit.  One wait per pair of Q8_0 blocks.
     uint32_t g = 0, item_no = 0;
     bool ok = true;
-    for (uint32_t it = it_begin; it < it_end && ok; ++it) {
-      const Item im = load_item(a, it);
+    for (uint32_t u = 0; u < n_units && ok; ++u) {
+      const Item im = load_item(a, unit_of(u, it_begin, cnt).it);
       if (im.ntiles == 0) continue;
       if (!mbar_wait_warp(bar(B_Q_FULL), item_no & 1u, abort_flag, a.status)) break;
       tc_fence_after();
@@ -619,8 +638,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     uint32_t g = 0, item_ord = 0;
     bool ok = true;
     const uint64_t ones_desc = smem_desc(sbase + OFF_ONES, 0, 0, LAYOUT_NONE);
-    for (uint32_t it = it_begin; it < it_end && ok; ++it) {
-      const Item im = load_item(a, it);
+    for (uint32_t u = 0; u < n_units && ok; ++u) {
+      const Item im = load_item(a, unit_of(u, it_begin, cnt).it);
       if (im.ntiles == 0) continue;
       for (uint32_t k = 0; k < im.ntiles && ok; ++k, ++g) {
         if (k == 0 && item_ord > 0) {
@@ -676,7 +695,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     // bounded and gives up quietly, it never aborts the CTA.
     const volatile uint32_t* cur = reinterpret_cast<const volatile uint32_t*>(smem + OFF_CUR_ITEM);
     const long long t0 = clock64();
-    for (uint32_t nx = it_begin + 1; nx < it_end; ++nx) {
+    for (uint32_t nx = 1; nx < n_units; ++nx) {
       bool go = false;
       while (true) {
         const uint32_t c = *cur;
@@ -689,9 +708,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         __nanosleep(256);
       }
       if (!go) break;
-      const Item im = load_item(a, nx);
+      const Unit un = unit_of(nx, it_begin, cnt);
+      const Item im = load_item(a, un.it);
       if (im.ntiles == 0) continue;
-      const uint8_t* qb = reinterpret_cast<const uint8_t*>(a.q + (uint64_t)im.b * H * W);
+      const uint8_t* qb = reinterpret_cast<const uint8_t*>(a.q + un.li * a.q_lstride + (uint64_t)im.b * H * W);
       for (uint32_t off = lane * 128u; off < H * (uint32_t)W * 4u; off += 32u * 128u) prefetch_l2_keep(qb + off);
     }
   }
@@ -718,28 +738,33 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       return r;
     };
     volatile uint32_t* cur_item = reinterpret_cast<volatile uint32_t*>(smem + OFF_CUR_ITEM);
-    for (uint32_t it = it_begin; it < it_end && ok; ++it) {
-      if (ew == 0 && lane == 0) *cur_item = it;
-      const Item im = load_item(a, it);
+    for (uint32_t u = 0; u < n_units && ok; ++u) {
+      if (ew == 0 && lane == 0) *cur_item = u;
+      const Unit un = unit_of(u, it_begin, cnt);
+      const Item im = load_item(a, un.it);
       const bool single = a.seq_count[im.b] == 1;
+      // this unit's layer: its output, partial slot (item index) and lse
+      float* const out_l = a.out + un.li * a.out_lstride;
+      const uint64_t pit = un.li * a.part_lstride + un.it;
+      float* const lse_l = a.lse ? a.lse + un.li * a.lse_lstride : nullptr;
       if (im.ntiles == 0) {
         // empty item: zeros, or an empty partial
         for (uint32_t i = ew * 32 + lane; i < H * (uint32_t)R; i += 32 * EPI_WARPS) {
           const uint32_t h = i / R, c = i % R;
-          if (single) a.out[((uint64_t)im.b * H + h) * R + c] = 0.f;
-          else a.part_o[((uint64_t)it * a.ws_heads + h) * R + c] = 0.f;
+          if (single) out_l[((uint64_t)im.b * H + h) * R + c] = 0.f;
+          else a.part_o[(pit * a.ws_heads + h) * R + c] = 0.f;
         }
         if (!single && ew == 0 && lane < H) {
-          a.part_ml[((uint64_t)it * a.ws_heads + lane) * 2 + 0] = -INFINITY;
-          a.part_ml[((uint64_t)it * a.ws_heads + lane) * 2 + 1] = 0.f;
+          a.part_ml[(pit * a.ws_heads + lane) * 2 + 0] = -INFINITY;
+          a.part_ml[(pit * a.ws_heads + lane) * 2 + 1] = 0.f;
         }
-        if (single && a.lse && ew == 0 && lane < H) a.lse[(uint64_t)im.b * H + lane] = -INFINITY;
+        if (single && lse_l && ew == 0 && lane < H) lse_l[(uint64_t)im.b * H + lane] = -INFINITY;
         continue;
       }
       // ---- query -> two int8 digits per element (x = s_h * (d0 + d1/256)), per-head
       // scale; each half's 4 warps encode that half's heads
       {
-        const float* qb = a.q + (uint64_t)im.b * H * W;
+        const float* qb = a.q + un.li * a.q_lstride + (uint64_t)im.b * H * W;
         for (uint32_t hl = ew & 3u; hl < (uint32_t)HH; hl += 4) {
           const uint32_t h = h0 + hl;
           float amax = 0.f;
@@ -966,8 +991,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const uint32_t hg = h0 + h;
             if (hg >= H) continue;
             const float v = __uint_as_float(o[h]);
-            if (single) a.out[((uint64_t)im.b * H + hg) * R + c] = ltot[h] > 0.f ? v / ltot[h] : 0.f;
-            else a.part_o[((uint64_t)it * a.ws_heads + hg) * R + c] = v;
+            if (single) out_l[((uint64_t)im.b * H + hg) * R + c] = ltot[h] > 0.f ? v / ltot[h] : 0.f;
+            else a.part_o[(pit * a.ws_heads + hg) * R + c] = v;
           }
         }
         if (!single && q4 == 0 && lane < HH && h0 + lane < H) {
@@ -978,10 +1003,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
               lh = ltot[h];
               mh = mref[h];
             }
-          a.part_ml[((uint64_t)it * a.ws_heads + h0 + lane) * 2 + 0] = mh * 0.69314718055994531f;
-          a.part_ml[((uint64_t)it * a.ws_heads + h0 + lane) * 2 + 1] = lh;
+          a.part_ml[(pit * a.ws_heads + h0 + lane) * 2 + 0] = mh * 0.69314718055994531f;
+          a.part_ml[(pit * a.ws_heads + h0 + lane) * 2 + 1] = lh;
         }
-        if (single && a.lse && q4 == 0 && lane < HH && h0 + lane < H) {
+        if (single && lse_l && q4 == 0 && lane < HH && h0 + lane < H) {
           float lh = 0.f, mh = 0.f;
 #pragma unroll
           for (int h = 0; h < HH; ++h)
@@ -990,7 +1015,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
               mh = mref[h];
             }
           // mref is in log2 units of the scaled score, l = sum 2^(s - mref)
-          a.lse[(uint64_t)im.b * H + h0 + lane] = lh > 0.f ? (mh + log2f(lh)) * 0.69314718055994531f : -INFINITY;
+          lse_l[(uint64_t)im.b * H + h0 + lane] = lh > 0.f ? (mh + log2f(lh)) * 0.69314718055994531f : -INFINITY;
         }
         tc_fence_before();
         __syncwarp();
@@ -1006,8 +1031,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const uint32_t j = tid >> 4;                     // 16-column group within the M-tile, 0..7
     uint32_t g = 0;
     bool ok = true;
-    for (uint32_t it = it_begin; it < it_end && ok; ++it) {
-      const Item im = load_item(a, it);
+    for (uint32_t u = 0; u < n_units && ok; ++u) {
+      const Item im = load_item(a, unit_of(u, it_begin, cnt).it);
       for (uint32_t k = 0; k < im.ntiles && ok; ++k, ++g) {
         const uint32_t s = g & 1u;
         const uint32_t tt0 = im.tok0 + k * TILE;
@@ -1189,10 +1214,11 @@ bool kvcu_decode_tc_supported(const kvcu_pool* p, uint32_t n_heads) {
   return true;
 }
 
-int kvcu_launch_decode_tc(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint32_t n,
+int kvcu_launch_decode_tc(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint32_t n_layers_call, uint32_t n,
                           const uint32_t* seq_ids, uint32_t n_seqs, const uint32_t* toff,
-                          const uint32_t* tables, const uint32_t* lens, const float* q,
-                          uint32_t n_heads, float scale, float* out, float* lse, cudaStream_t st) {
+                          const uint32_t* tables, const uint32_t* lens, const float* q, uint64_t q_lstride,
+                          uint32_t n_heads, float scale, float* out, uint64_t out_lstride, float* lse,
+                          uint64_t lse_lstride, cudaStream_t st) {
   // one box per slice, or per block where blocks are smaller than a slice
   const uint32_t box_rows = p->block_size < SLICE ? p->block_size : SLICE;
   CUtensorMap lat, rope;
@@ -1223,6 +1249,11 @@ int kvcu_launch_decode_tc(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint
   a.part_ml = ws->part_ml;
   a.ws_heads = ws->max_heads;
   a.lse = lse;
+  a.n_layers_call = n_layers_call;
+  a.q_lstride = q_lstride;
+  a.out_lstride = out_lstride;
+  a.part_lstride = ws->max_items;
+  a.lse_lstride = lse_lstride;
   if (n_heads <= 8) return launch_tc<8>(ws->decode_ctas, lat, rope, a, st);
   if (n_heads <= 16) return launch_tc<16>(ws->decode_ctas, lat, rope, a, st);
   if (n_heads <= 20) return launch_tc<20>(ws->decode_ctas, lat, rope, a, st);

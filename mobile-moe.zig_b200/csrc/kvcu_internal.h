@@ -32,13 +32,14 @@ struct kvcu_item {
 struct kvcu_decode_ws {
   int device;
   uint32_t max_batch, max_heads, max_items, max_ranges;
+  uint32_t max_layers;       // layers one multi-layer decode may cover (partials per layer)
   kvcu_item* items;          // [max_items]
   uint32_t* meta;            // [0] n_items, [1] CTA ranges G
   uint32_t* ranges;          // [max_ranges + 1] first item of each CTA range
   uint32_t* seq_first;       // [max_batch] first item of entry b
   uint32_t* seq_count;       // [max_batch] items of entry b
-  float* part_o;             // [max_items][max_heads][512]
-  float* part_ml;            // [max_items][max_heads][2] (m, l)
+  float* part_o;             // [max_layers][max_items][max_heads][512]
+  float* part_ml;            // [max_layers][max_items][max_heads][2] (m, l)
   uint32_t last_launches;
   int num_sms;
   int decode_ctas;           // resident decode CTAs (grid of the persistent kernel)
@@ -95,6 +96,12 @@ int kvcu_launch_append(kvcu_pool* p, uint32_t layer, uint32_t n_rows, const floa
                        uint64_t ls, const float* rope, uint64_t ps, const uint32_t* row_seq,
                        const uint32_t* row_pos, uint32_t n_seqs, const uint32_t* table_offsets,
                        const uint32_t* tables, uint32_t* lens, cudaStream_t st);
+// Layers [layer, layer + n_layers_call): rows of layer layer+i at latent +
+// i*llat and rope + i*lrope (floats); one launch on the fast path.
+int kvcu_launch_append_layers(kvcu_pool* p, uint32_t layer, uint32_t n_layers_call, uint32_t n_rows,
+                              const float* latent, uint64_t ls, uint64_t llat, const float* rope, uint64_t ps,
+                              uint64_t lrope, const uint32_t* row_seq, const uint32_t* row_pos, uint32_t n_seqs,
+                              const uint32_t* toff, const uint32_t* tables, uint32_t* lens, cudaStream_t st);
 int kvcu_launch_gather_rows(kvcu_pool* p, uint32_t layer, uint32_t n_rows, const uint32_t* row_seq,
                             const uint32_t* row_pos, uint32_t n_seqs, const uint32_t* table_offsets,
                             const uint32_t* tables, const uint32_t* table, uint32_t table_len,
@@ -120,13 +127,25 @@ int kvcu_launch_plan_target(kvcu_decode_ws* ws, const kvcu_pool* p, uint32_t n,
 int kvcu_noalloc_prepare(int device);
 // ---- tensor-core decode (kvcu_decode_tc.cu) ----
 bool kvcu_decode_tc_supported(const kvcu_pool* p, uint32_t n_heads);
-int kvcu_launch_decode_tc(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint32_t n,
+// Layers [layer, layer + n_layers_call) with one plan: q / out / lse of layer
+// layer+i at + i * its stride (floats); partials of layer i at item index
+// i * ws->max_items + item (ws->max_layers >= n_layers_call).
+int kvcu_launch_decode_tc(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint32_t n_layers_call, uint32_t n,
                           const uint32_t* seq_ids, uint32_t n_seqs, const uint32_t* toff,
-                          const uint32_t* tables, const uint32_t* lens, const float* q,
-                          uint32_t n_heads, float scale, float* out, float* lse, cudaStream_t st);
+                          const uint32_t* tables, const uint32_t* lens, const float* q, uint64_t q_lstride,
+                          uint32_t n_heads, float scale, float* out, uint64_t out_lstride, float* lse,
+                          uint64_t lse_lstride, cudaStream_t st);
 // `lse` (nullable): [n][n_heads] log-sum-exp of the scaled scores, natural log
 // (-inf for an empty context), for merging further terms into `out`.
 int kvcu_launch_decode(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint32_t n,
                        const uint32_t* seq_ids, uint32_t n_seqs, const uint32_t* table_offsets,
                        const uint32_t* tables, const uint32_t* lens, const float* q,
                        uint32_t n_heads, float scale, float* out, float* lse, cudaStream_t st);
+// Several layers with one plan (strides in floats between consecutive layers'
+// q, out and lse); one decode launch and one combine launch on the tensor-core
+// path, a launch pair per layer on the CUDA-core path.
+int kvcu_launch_decode_layers(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint32_t n_layers_call,
+                              uint32_t n, const uint32_t* seq_ids, uint32_t n_seqs,
+                              const uint32_t* table_offsets, const uint32_t* tables, const uint32_t* lens,
+                              const float* q, uint64_t q_lstride, uint32_t n_heads, float scale, float* out,
+                              uint64_t out_lstride, float* lse, uint64_t lse_lstride, cudaStream_t st);

@@ -142,6 +142,8 @@ __global__ void __launch_bounds__(256) k_append(PoolArgs a, uint32_t n_rows,
 constexpr int APPEND_PREFETCH_GROUPS = 8;
 constexpr uint32_t APPEND_WHOLE_ROW_MAX_ROWS = 16384;
 
+// Layers: rows of layer a.layer + i come from latent + i*llat / rope + i*lrope
+// (n_layers_call >= 1); every (row, layer) pair is one warp's work.
 template <bool QUANT, bool WHOLE_ROW>
 __global__ void __launch_bounds__(256) k_append_rows(PoolArgs a, uint32_t n_rows,
                                                      const float* __restrict__ latent, uint64_t ls,
@@ -150,7 +152,8 @@ __global__ void __launch_bounds__(256) k_append_rows(PoolArgs a, uint32_t n_rows
                                                      const uint32_t* __restrict__ row_pos,
                                                      uint32_t n_seqs, const uint32_t* __restrict__ toff,
                                                      const uint32_t* __restrict__ tables,
-                                                     uint32_t* __restrict__ lens) {
+                                                     uint32_t* __restrict__ lens, uint32_t n_layers_call,
+                                                     uint64_t llat, uint64_t lrope) {
   const uint32_t lane = threadIdx.x & 31u, grp = lane >> 3, sub = lane & 7u;
   const uint64_t nwarps = ((uint64_t)gridDim.x * blockDim.x) >> 5;
   const uint32_t nblk = a.nbk + a.nbp;
@@ -183,12 +186,17 @@ __global__ void __launch_bounds__(256) k_append_rows(PoolArgs a, uint32_t n_rows
       *reinterpret_cast<float4*>(dst) = x;
     }
   };
-  auto load_group = [&](uint64_t r, uint32_t b) -> float4 {
-    const float* src = b < a.nbk ? latent + r * ls + 32u * b + 4u * sub
-                                 : rope + r * ps + 32u * (b - a.nbk) + 4u * sub;
-    return __ldg(reinterpret_cast<const float4*>(src));
-  };
-  for (uint64_t r = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < n_rows; r += nwarps) {
+  const uint64_t layer_rows = (uint64_t)a.num_blocks * a.block_size;
+  const uint64_t total = (uint64_t)n_rows * n_layers_call;
+  for (uint64_t ra = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; ra < total; ra += nwarps) {
+    const uint64_t li = ra / n_rows, r = ra - li * n_rows;
+    const float* lat_l = latent + li * llat;
+    const float* rope_l = rope + li * lrope;
+    auto load_group = [&](uint64_t r, uint32_t b) -> float4 {
+      const float* src = b < a.nbk ? lat_l + r * ls + 32u * b + 4u * sub
+                                   : rope_l + r * ps + 32u * (b - a.nbk) + 4u * sub;
+      return __ldg(reinterpret_cast<const float4*>(src));
+    };
     const uint32_t s = row_seq[r], pos = row_pos[r];
     if (WHOLE_ROW) {
       // The whole row is loaded first, so that its loads overlap the block
@@ -201,15 +209,17 @@ __global__ void __launch_bounds__(256) k_append_rows(PoolArgs a, uint32_t n_rows
       }
       uint64_t row;
       if (!resolve_row(a, s, pos, n_seqs, toff, tables, lane, &row)) continue;
+      row += li * layer_rows;
       // len = max(len, pos + 1), src/kv_cache.zig:358-360
-      if (lens && lane == 0) atomicMax(lens + s, pos + 1u);
+      if (lens && li == 0 && lane == 0) atomicMax(lens + s, pos + 1u);
 #pragma unroll
       for (uint32_t g = 0; g < (uint32_t)APPEND_PREFETCH_GROUPS; ++g)
         if (4u * g < nblk) put_group(r, row, 4u * g + grp, 4u * g + grp < nblk, xs[g]);  // warp-uniform test
     } else {
       uint64_t row;
       if (!resolve_row(a, s, pos, n_seqs, toff, tables, lane, &row)) continue;
-      if (lens && lane == 0) atomicMax(lens + s, pos + 1u);
+      row += li * layer_rows;
+      if (lens && li == 0 && lane == 0) atomicMax(lens + s, pos + 1u);
       for (uint32_t b0 = 0; b0 < nblk; b0 += 4) {
         const uint32_t b = b0 + grp;
         const bool act = b < nblk;
@@ -389,30 +399,45 @@ int kvcu_launch_append(kvcu_pool* p, uint32_t layer, uint32_t n_rows, const floa
                        uint64_t ls, const float* rope, uint64_t ps, const uint32_t* row_seq,
                        const uint32_t* row_pos, uint32_t n_seqs, const uint32_t* toff,
                        const uint32_t* tables, uint32_t* lens, cudaStream_t st) {
-  if (n_rows == 0) return KVCU_OK;
+  return kvcu_launch_append_layers(p, layer, 1, n_rows, latent, ls, 0, rope, ps, 0, row_seq, row_pos, n_seqs, toff,
+                                   tables, lens, st);
+}
+
+int kvcu_launch_append_layers(kvcu_pool* p, uint32_t layer, uint32_t n_layers_call, uint32_t n_rows,
+                              const float* latent, uint64_t ls, uint64_t llat, const float* rope, uint64_t ps,
+                              uint64_t lrope, const uint32_t* row_seq, const uint32_t* row_pos, uint32_t n_seqs,
+                              const uint32_t* toff, const uint32_t* tables, uint32_t* lens, cudaStream_t st) {
+  if (n_rows == 0 || n_layers_call == 0) return KVCU_OK;
   PoolArgs a = pool_args(p, layer);
   const bool rows_ok = p->kv_rank % 32 == 0 && p->rope_dim % 32 == 0 && ls % 4 == 0 && ps % 4 == 0 &&
-                       (reinterpret_cast<uintptr_t>(latent) & 15) == 0 &&
+                       llat % 4 == 0 && lrope % 4 == 0 && (reinterpret_cast<uintptr_t>(latent) & 15) == 0 &&
                        (reinterpret_cast<uintptr_t>(rope) & 15) == 0;
   if (rows_ok) {
-    const int g = grid_for(n_rows, 256);
+    const uint64_t pairs = (uint64_t)n_rows * n_layers_call;
+    const int g = grid_for(pairs, 256);
     // programmatic launch: it waits for the previous kernel before any access
-    const bool whole = n_rows <= APPEND_WHOLE_ROW_MAX_ROWS && p->nblk <= 4u * APPEND_PREFETCH_GROUPS;
+    const bool whole = pairs <= APPEND_WHOLE_ROW_MAX_ROWS && p->nblk <= 4u * APPEND_PREFETCH_GROUPS;
     auto kern = p->quantized ? (whole ? k_append_rows<true, true> : k_append_rows<true, false>)
                              : (whole ? k_append_rows<false, true> : k_append_rows<false, false>);
     return kvcu_check_cuda(kvcu_launch_pdl(kern, dim3(g), dim3(256), 0, st, a, n_rows, latent, ls, rope, ps,
-                                           row_seq, row_pos, n_seqs, toff, tables, lens),
+                                           row_seq, row_pos, n_seqs, toff, tables, lens, n_layers_call, llat,
+                                           lrope),
                            "append kernel launch");
   }
   const uint32_t nper = p->quantized ? p->nblk : (p->kv_rank + p->rope_dim + 31) / 32;
   const int g = grid_for((uint64_t)n_rows * nper, 256);
-  if (p->quantized)
-    k_append<true><<<g, 256, 0, st>>>(a, n_rows, latent, ls, rope, ps, row_seq, row_pos, n_seqs,
-                                      toff, tables, lens);
-  else
-    k_append<false><<<g, 256, 0, st>>>(a, n_rows, latent, ls, rope, ps, row_seq, row_pos, n_seqs,
-                                       toff, tables, lens);
-  return kvcu_check_cuda(cudaGetLastError(), "append kernel launch");
+  for (uint32_t i = 0; i < n_layers_call; ++i) {
+    a.layer = layer + i;
+    if (p->quantized)
+      k_append<true><<<g, 256, 0, st>>>(a, n_rows, latent + i * llat, ls, rope + i * lrope, ps, row_seq, row_pos,
+                                        n_seqs, toff, tables, lens);
+    else
+      k_append<false><<<g, 256, 0, st>>>(a, n_rows, latent + i * llat, ls, rope + i * lrope, ps, row_seq, row_pos,
+                                         n_seqs, toff, tables, lens);
+    const int rc = kvcu_check_cuda(cudaGetLastError(), "append kernel launch");
+    if (rc) return rc;
+  }
+  return KVCU_OK;
 }
 
 int kvcu_launch_gather_rows(kvcu_pool* p, uint32_t layer, uint32_t n_rows, const uint32_t* row_seq,

@@ -65,9 +65,14 @@ _SIGS = {
     "kvcu_pool_status": (_i32, [_vp, C.POINTER(_u32), _vp]),
     "kvcu_pool_copy_block": (_i32, [_vp, _u32, _u32, _vp]),
     "kvcu_append": (_i32, [_vp, _u32, _u32, _vp, _u64, _vp, _u64, _vp, _vp, _u32, _vp, _vp, _vp, _vp]),
+    "kvcu_append_layers": (_i32, [_vp, _u32, _u32, _u32, _vp, _u64, _u64, _vp, _u64, _u64, _vp, _vp, _u32, _vp, _vp,
+                                  _vp, _vp]),
     "kvcu_gather": (_i32, [_vp, _u32, _vp, _u32, _u32, _vp, _vp]),
     "kvcu_gather_rows": (_i32, [_vp, _u32, _u32, _vp, _vp, _u32, _vp, _vp, _vp, _vp]),
     "kvcu_decode_ws_create": (_vp, [_i32, _u32, _u32]),
+    "kvcu_decode_ws_create_layers": (_vp, [_i32, _u32, _u32, _u32]),
+    "kvcu_mla_decode_layers": (_i32, [_vp, _vp, _u32, _u32, _u32, _vp, _u32, _vp, _vp, _vp, _vp, _u64, _u32, _f32,
+                                      _vp, _u64, _vp]),
     "kvcu_decode_ws_destroy": (_i32, [_vp]),
     "kvcu_decode_plan": (_i32, [_vp, _vp, _u32, _vp, _u32, _vp, _vp]),
     "kvcu_mla_decode": (_i32, [_vp, _vp, _u32, _u32, _vp, _u32, _vp, _vp, _vp, _vp, _u32, _f32, _vp, _vp]),
@@ -123,6 +128,9 @@ _SIGS = {
     "kvcache_gather": (_i32, [_vp, _u32, _u32, _vp]),
     "kvcache_mla_decode": (_i32, [_vp, _u32, _u32, _vp, _vp, _u32, _f32, _vp]),
     "kvcache_mla_decode_dev": (_i32, [_vp, _u32, _u32, _vp, _vp, _u32, _f32, _vp, _vp]),
+    "kvcache_append_layers_dev": (_i32, [_vp, _u32, _u32, _u32, _vp, _vp, _vp, _vp, _vp, _u64, _vp]),
+    "kvcache_mla_decode_layers_dev": (_i32, [_vp, _u32, _u32, _u32, _vp, _vp, _u64, _u32, _f32, _vp, _u64, _vp]),
+    "kvcache_append_decode_layers": (_i32, [_vp, _u32, _u32, _u32, _vp, _vp, _vp, _vp, _u32, _f32, _vp]),
     "kvcache_mla_step_dev": (_i32, [_vp, _u32, _u32, _vp, _vp, _vp, _vp, _vp, _f32, _f32, _vp, _vp, _u32,
                                     _u32, _u32, _f32, _vp, _vp]),
     "kvcache_last_launches": (_u32, [_vp]),
@@ -270,6 +278,15 @@ class DevicePool:
                                 _dptr(table_offsets), _dptr(tables), _dptr(lens), _stream(stream)),
               "kvcu_append")
 
+    def append_layers(self, layer, rows, row_seq, row_pos, table_offsets, tables, lens=None, stream=None):
+        """rows: device f32 [n_layers][n][kv_rank+rope_dim]; one launch for layers [layer, layer+n_layers)."""
+        d = self.describe()
+        nl, n, W = rows.shape
+        check(lib().kvcu_append_layers(self._h, layer, nl, n, C.c_void_p(rows.data_ptr()), W, n * W,
+                                       C.c_void_p(rows.data_ptr() + 4 * d.kv_rank), W, n * W, _dptr(row_seq),
+                                       _dptr(row_pos), table_offsets.numel() - 1, _dptr(table_offsets),
+                                       _dptr(tables), _dptr(lens), _stream(stream)), "kvcu_append_layers")
+
     def gather(self, layer, table, length, out, stream=None):
         check(lib().kvcu_gather(self._h, layer, _dptr(table), table.numel(), length, _dptr(out),
                                 _stream(stream)), "kvcu_gather")
@@ -295,8 +312,8 @@ class DevicePool:
 
 
 class DecodeWorkspace:
-    def __init__(self, device, max_batch, max_heads):
-        h = lib().kvcu_decode_ws_create(device, max_batch, max_heads)
+    def __init__(self, device, max_batch, max_heads, max_layers=1):
+        h = lib().kvcu_decode_ws_create_layers(device, max_batch, max_heads, max_layers)
         if not h:
             raise KVCudaError(-14, "kvcu_decode_ws_create", last_error())
         self._h = h
@@ -323,6 +340,15 @@ class DecodeWorkspace:
         check(lib().kvcu_mla_decode(self._h, pool.handle, layer, n, _dptr(seq_ids), lens.numel(),
                                     _dptr(table_offsets), _dptr(tables), _dptr(lens), _dptr(q), H,
                                     scale, _dptr(out), _stream(stream)), "kvcu_mla_decode")
+
+    def decode_layers(self, pool: DevicePool, layer, q, table_offsets, tables, lens, scale, out, seq_ids=None,
+                      stream=None):
+        """q [n_layers][n][H][576], out [n_layers][n][H][512]: layers [layer, layer+n_layers), one plan."""
+        nl, n, H = q.shape[0], q.shape[1], q.shape[2]
+        check(lib().kvcu_mla_decode_layers(self._h, pool.handle, layer, nl, n, _dptr(seq_ids), lens.numel(),
+                                           _dptr(table_offsets), _dptr(tables), _dptr(lens), _dptr(q),
+                                           q[0].numel(), H, scale, _dptr(out), out[0].numel(), _stream(stream)),
+              "kvcu_mla_decode_layers")
 
     @property
     def last_launches(self):
@@ -568,6 +594,32 @@ class KVCache:
         check(lib().kvcache_append_batch_dev(self._h, layer, s.size, _np_ptr(s), _np_ptr(p),
                                              _dptr(seq_ids_dev), _dptr(positions_dev), _dptr(rows_dev),
                                              _stream(stream)), "appendBatch_dev")
+
+    def appendLayers_dev(self, layer, seq_ids, positions, seq_ids_dev, positions_dev, rows_dev, stream=None):
+        """rows_dev [n_layers][n][W]: appendBatch of layers [layer, layer+n_layers) in one launch."""
+        s = np.ascontiguousarray(seq_ids, np.uint32)
+        p = np.ascontiguousarray(positions, np.uint32)
+        nl = rows_dev.shape[0]
+        check(lib().kvcache_append_layers_dev(self._h, layer, nl, s.size, _np_ptr(s), _np_ptr(p), _dptr(seq_ids_dev),
+                                              _dptr(positions_dev), _dptr(rows_dev), rows_dev[0].numel(),
+                                              _stream(stream)), "appendLayers_dev")
+
+    def mlaDecodeLayers_dev(self, layer, seq_ids, q_dev, scale, out_dev, stream=None):
+        """q_dev [n_layers][n][H][W] -> out_dev [n_layers][n][H][R], one multi-layer launch."""
+        s = np.ascontiguousarray(seq_ids, np.uint32)
+        nl, n, H = q_dev.shape[0], q_dev.shape[1], q_dev.shape[2]
+        check(lib().kvcache_mla_decode_layers_dev(self._h, layer, nl, n, _np_ptr(s), _dptr(q_dev), q_dev[0].numel(),
+                                                  H, scale, _dptr(out_dev), out_dev[0].numel(), _stream(stream)),
+              "mlaDecodeLayers_dev")
+
+    def appendDecodeLayers_ptr(self, layer, n_layers, n, seq_ids, positions, rows_ptr, q_ptr, n_heads, scale,
+                               out_ptr):
+        """Host buffers (raw addresses): rows [nl][n][W], q [nl][n][H][W] -> out [nl][n][H][R]; one sync."""
+        s = np.ascontiguousarray(seq_ids, np.uint32)
+        p = np.ascontiguousarray(positions, np.uint32)
+        check(lib().kvcache_append_decode_layers(self._h, layer, n_layers, n, _np_ptr(s), _np_ptr(p),
+                                                 C.c_void_p(rows_ptr), C.c_void_p(q_ptr), n_heads, scale,
+                                                 C.c_void_p(out_ptr)), "appendDecodeLayers")
 
     def gather(self, layer, seq):
         n = self.seq_len(seq)
