@@ -373,6 +373,45 @@ def measure_config4(kvcu, torch, dev, local_rank, peak, steps=10, warmup=3):
                     "batch changes, k_decode_tc, k_combine); device-resident inputs; KV larger than L2"}
 
 
+# ------------------------------------------------------------------ prefill (causal multi-query attention)
+PREFILL_LEN = 4096
+
+
+def measure_prefill(kvcu, torch, dev, local_rank, reps=5):
+    """mlaAttentionBatch over a 4,096-token prompt of one sequence (one layer,
+    Q8_0, block size 64, 20 heads): the prompt's rows are appended, then every
+    position attends causally to itself and the positions before it, in one
+    call (kvcache_mla_attention_batch_dev).  Prompt tokens/s and the context
+    tokens attended (sum of 1..4096) per second."""
+    L = PREFILL_LEN
+    c = kvcu.KVCache.with_blocks(1, R, P, (L + BS - 1) // BS + 2, BS, quantized=True, device=local_rank)
+    c.seq_ensure_capacity(0, L)
+    c.prefill_synthetic(0, [0], [L], SEED + 9, OUTLIER_P)
+    st = torch.cuda.Stream(device=dev)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(st):
+        q = torch.randn((L, H, W), device=dev, generator=torch.Generator(device=dev).manual_seed(SEED + 9))
+        out = torch.empty((L, H, R), device=dev)
+    st.synchronize()
+    c.mlaAttentionBatch_dev(0, 0, 0, q, SCALE, out, st)  # warm-up
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(reps):
+        c.mlaAttentionBatch_dev(0, 0, 0, q, SCALE, out, st)
+    e1.record(st)
+    st.synchronize()
+    status = c.pool().status()
+    c.close()
+    if status:
+        raise RuntimeError(f"prefill hit device status {status:#x}")
+    secs = e0.elapsed_time(e1) / 1e3 / reps
+    ctx = L * (L + 1) // 2
+    return {"prompt_tokens": L, "prompt_tokens_per_s": L / secs, "ms_per_prompt_layer": secs * 1e3,
+            "ctx_tokens_per_s": ctx / secs,
+            "what": "one layer of a 4,096-token prompt: every position attends causally (one causal plan, one "
+                    "decode launch, one combine; the prefix re-reads are served from L2)"}
+
+
 # ------------------------------------------------------------------ checkpoint round trip (config 5)
 class _DeviceBytes:
     """Zero-copy view of device memory the library owns, for torch."""
@@ -706,6 +745,7 @@ def run_ours(args, rank, world, local_rank):
 
     peak, peak_kind = read_peaks()
     c4 = None if args.no_config4 else measure_config4(kvcu, torch, dev, local_rank, peak)
+    prefill = measure_prefill(kvcu, torch, dev, local_rank)
     ckpt = None if args.no_checkpoint else checkpoint_roundtrip(kvcu, torch, dev, cache, local_rank, rank, NL, nb, n,
                                                                 args.ckpt_dir)
     if world > 1 and ckpt is not None:
@@ -772,6 +812,7 @@ def run_ours(args, rank, world, local_rank):
             "mla_step": mla,
             "prefill_s": t_pre,
             "multi_gpu_check": mg_check,
+            "prefill": prefill,
         }
         if c4 is not None:
             line["config4"] = c4

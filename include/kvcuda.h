@@ -189,6 +189,17 @@ int kvcu_decode_ws_destroy(kvcu_decode_ws* ws);
  * sequences shrink); all layers of a step share it. */
 int kvcu_decode_plan(kvcu_decode_ws* ws, const kvcu_pool* pool, uint32_t n, const uint32_t* seq_ids,
                      uint32_t n_seqs, const uint32_t* lens, void* stream);
+/* The plan for causal multi-query attention, the loop of
+ * InferenceEngine.mlaAttentionBatch (src/inference.zig:771-877): entry b
+ * attends positions [0, min(entry_lens[b], lens[seq])) of its sequence, so the
+ * n new positions p0..p0+n-1 of one prompt become n entries of the same
+ * sequence with entry_lens = p0+1 .. p0+n (their rows appended first, as the
+ * reference puts every position before attending, :733).  Entries of any
+ * sequences may be mixed.  entry_lens is a device array that must stay
+ * unchanged while decodes use this plan (kvcu_mla_decode / _layers read it);
+ * the next kvcu_decode_plan drops it. */
+int kvcu_decode_plan_causal(kvcu_decode_ws* ws, const kvcu_pool* pool, uint32_t n, const uint32_t* seq_ids,
+                            uint32_t n_seqs, const uint32_t* lens, const uint32_t* entry_lens, void* stream);
 /* Run decode for one layer with the last plan of `ws`. */
 int kvcu_mla_decode(kvcu_decode_ws* ws, kvcu_pool* pool, uint32_t layer, uint32_t n,
                     const uint32_t* seq_ids, uint32_t n_seqs, const uint32_t* table_offsets,
@@ -414,6 +425,18 @@ int kvcache_gather(kvcache* c, uint32_t layer, uint32_t seq, float* out);
  * following it. */
 int kvcache_mla_decode(kvcache* c, uint32_t layer, uint32_t n, const uint32_t* seq_ids,
                        const float* q, uint32_t n_heads, float scale, float* out);
+/* mlaAttentionBatch (src/inference.zig:670-883, its attention loop :771-877):
+ * the n_pos prompt positions start_pos .. start_pos+n_pos-1 of sequence `seq`
+ * (already appended, so len >= start_pos + n_pos, else
+ * KVCU_ERR_POSITION_NOT_WRITTEN) attend causally: query i sees positions
+ * [0, start_pos + i].  q [n_pos][n_heads][R+P] -> out [n_pos][n_heads][R], HOST
+ * buffers (used in place when pinned and mapped); the _dev variant takes
+ * device pointers and is stream-ordered.  One causal plan + one decode. */
+int kvcache_mla_attention_batch(kvcache* c, uint32_t layer, uint32_t seq, uint32_t start_pos, uint32_t n_pos,
+                                const float* q, uint32_t n_heads, float scale, float* out);
+int kvcache_mla_attention_batch_dev(kvcache* c, uint32_t layer, uint32_t seq, uint32_t start_pos, uint32_t n_pos,
+                                    const float* q_dev, uint32_t n_heads, float scale, float* out_dev,
+                                    void* stream);
 /* 1 when the last kvcache_mla_decode used its buffers in place (pinned,
  * mapped), 0 when it copied. */
 int kvcache_last_decode_mapped(const kvcache* c);

@@ -632,9 +632,85 @@ int decode_impl(kvcache* c, uint32_t layer, uint32_t n, const uint32_t* seq_ids,
   return KVCU_OK;
 }
 
+// Causal multi-query attention over one sequence (mlaAttentionBatch,
+// src/inference.zig:771-877): query i is position start_pos + i and attends
+// positions [0, start_pos + i].  Stream-ordered on `st`.
+int attention_batch_impl(kvcache* c, uint32_t layer, uint32_t seq, uint32_t start_pos, uint32_t n_pos,
+                         const float* q_dev, uint32_t n_heads, float scale, float* out_dev, cudaStream_t st) {
+  if (layer >= c->n_layers) {
+    kvcu_set_error("LayerOutOfBounds: layer %u >= %u", layer, c->n_layers);
+    return KVCU_ERR_LAYER_OOB;
+  }
+  if (seq >= c->seqs.size()) {
+    kvcu_set_error("sequence %u does not exist", seq);
+    return KVCU_ERR_INVALID_ARG;
+  }
+  if ((uint64_t)start_pos + n_pos > c->seqs[seq].len) {
+    kvcu_set_error("PositionNotWritten: queries up to position %llu, sequence %u holds %u",
+                   (unsigned long long)start_pos + n_pos - 1, seq, c->seqs[seq].len);
+    return KVCU_ERR_POSITION_NOT_WRITTEN;
+  }
+  int rc = ensure_ws(c, n_pos, n_heads);
+  if (!rc) rc = sync_tables(c, st);
+  if (!rc) rc = sync_lens(c, st);
+  if (!rc) rc = ensure_dev(&c->d_stepu, &c->d_stepu_cap, (size_t)2 * n_pos);
+  if (!rc) rc = stage_acquire(c->up_rowidx, (size_t)2 * n_pos);
+  if (rc) return rc;
+  for (uint32_t i = 0; i < n_pos; ++i) {
+    c->up_rowidx.p[i] = seq;
+    c->up_rowidx.p[n_pos + i] = start_pos + i + 1;  // attended length of query i
+  }
+  rc = stage_upload(c->up_rowidx, c->d_stepu, (size_t)2 * n_pos, st);
+  const uint32_t n_seqs = (uint32_t)c->seqs.size();
+  if (!rc)
+    rc = kvcu_decode_plan_causal(c->ws, c->pool, n_pos, c->d_stepu, n_seqs, c->d_lens, c->d_stepu + n_pos, st);
+  c->plan_epoch = ~0ull;  // the cached decode plan no longer matches the workspace
+  c->plan_ids.clear();
+  if (!rc)
+    rc = kvcu_mla_decode(c->ws, c->pool, layer, n_pos, c->d_stepu, n_seqs, c->d_toff, c->d_tables, c->d_lens, q_dev,
+                         n_heads, scale, out_dev, st);
+  if (rc) return rc;
+  c->last_launches = 1 + kvcu_decode_last_launches(c->ws);
+  return KVCU_OK;
+}
+
 }  // namespace
 
 extern "C" {
+
+int kvcache_mla_attention_batch_dev(kvcache* c, uint32_t layer, uint32_t seq, uint32_t start_pos, uint32_t n_pos,
+                                    const float* q_dev, uint32_t n_heads, float scale, float* out_dev,
+                                    void* stream) {
+  if (!c || (n_pos && (!q_dev || !out_dev))) return KVCU_ERR_INVALID_ARG;
+  if (!n_pos) return KVCU_OK;
+  DevScope d(c->device);
+  return attention_batch_impl(c, layer, seq, start_pos, n_pos, q_dev, n_heads, scale, out_dev, (cudaStream_t)stream);
+}
+
+int kvcache_mla_attention_batch(kvcache* c, uint32_t layer, uint32_t seq, uint32_t start_pos, uint32_t n_pos,
+                                const float* q, uint32_t n_heads, float scale, float* out) {
+  if (!c || (n_pos && (!q || !out))) return KVCU_ERR_INVALID_ARG;
+  if (!n_pos) return KVCU_OK;
+  DevScope d(c->device);
+  const size_t qn = (size_t)n_pos * n_heads * c->row_width(), on = (size_t)n_pos * n_heads * c->kv_rank;
+  const void* q_map = mapped_host_range(q, qn * 4);
+  void* out_map = q_map ? mapped_host_range(out, on * 4) : nullptr;
+  int rc;
+  if (q_map && out_map) {
+    rc = attention_batch_impl(c, layer, seq, start_pos, n_pos, static_cast<const float*>(q_map), n_heads, scale,
+                              static_cast<float*>(out_map), c->stream);
+    if (rc) return rc;
+    return check_status(c);
+  }
+  rc = ensure_dev(&c->d_f, &c->d_f_cap, qn);
+  if (!rc) rc = ensure_dev(&c->d_f2, &c->d_f2_cap, on);
+  if (rc) return rc;
+  KVCU_CUDA(cudaMemcpyAsync(c->d_f, q, qn * 4, cudaMemcpyHostToDevice, c->stream));
+  rc = attention_batch_impl(c, layer, seq, start_pos, n_pos, c->d_f, n_heads, scale, c->d_f2, c->stream);
+  if (rc) return rc;
+  KVCU_CUDA(cudaMemcpyAsync(out, c->d_f2, on * 4, cudaMemcpyDeviceToHost, c->stream));
+  return check_status(c);
+}
 
 kvcache* kvcache_init(int device, uint32_t n_layers, uint32_t kv_rank, uint32_t rope_dim,
                       uint32_t max_seq_len, uint32_t block_size) {

@@ -437,6 +437,20 @@ int kvcu_mla_decode(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint32_t n
                             n_heads, scale, out, nullptr, (cudaStream_t)stream);
 }
 
+int kvcu_decode_plan_causal(kvcu_decode_ws* ws, const kvcu_pool* p, uint32_t n, const uint32_t* seq_ids,
+                            uint32_t n_seqs, const uint32_t* lens, const uint32_t* entry_lens, void* stream) {
+  if (!ws || !valid_pool(p)) return KVCU_ERR_INVALID_ARG;
+  if (n > ws->max_batch) {
+    kvcu_set_error("kvcu_decode_plan_causal: batch %u exceeds workspace capacity %u", n, ws->max_batch);
+    return KVCU_ERR_INVALID_ARG;
+  }
+  if (ws->device != p->device) return KVCU_ERR_INVALID_ARG;
+  if (n && (!lens || !entry_lens)) return KVCU_ERR_INVALID_ARG;
+  DeviceGuard g(p->device);
+  if (g.rc) return g.rc;
+  return kvcu_launch_plan(ws, p, n, seq_ids, n_seqs, lens, (cudaStream_t)stream, entry_lens);
+}
+
 int kvcu_mla_decode_layers(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint32_t n_layers, uint32_t n,
                            const uint32_t* seq_ids, uint32_t n_seqs, const uint32_t* table_offsets,
                            const uint32_t* tables, const uint32_t* lens, const float* q, uint64_t q_layer_stride,

@@ -57,6 +57,7 @@ struct DecodeArgs {
   float* part_ml;
   uint32_t ws_heads;
   float* lse;  // optional [n][H] log-sum-exp of the scaled scores (natural log)
+  const uint32_t* entry_lens;  // optional per-entry attended length (capped by lens[seq]); from the plan
 };
 
 __device__ __forceinline__ float warp_max(float v) {
@@ -96,8 +97,11 @@ __device__ __forceinline__ unsigned long long ceil_div_u64(unsigned long long x,
   return (x + y - 1) / y;
 }
 
+// entry_lens (nullable): entry b attends min(entry_lens[b], lens[seq]) positions
+// instead of the sequence's whole length (causal multi-query attention).
 __global__ void __launch_bounds__(1024) k_plan(uint32_t n, const uint32_t* __restrict__ seq_ids,
                                                uint32_t n_seqs, const uint32_t* __restrict__ lens,
+                                               const uint32_t* __restrict__ entry_lens,
                                                uint32_t max_ranges, uint32_t align, uint32_t max_items,
                                                kvcu_item* __restrict__ items,
                                                uint32_t* __restrict__ meta,
@@ -119,7 +123,8 @@ __global__ void __launch_bounds__(1024) k_plan(uint32_t n, const uint32_t* __res
   __syncthreads();
   auto units_of = [&](uint32_t b) -> uint32_t {
     const uint32_t s = seq_ids ? seq_ids[b] : b;
-    const uint32_t len = s < n_seqs ? lens[s] : 0u;
+    uint32_t len = s < n_seqs ? lens[s] : 0u;
+    if (entry_lens) len = min(len, entry_lens[b]);
     return (uint32_t)ceil_div_u64(len, align);
   };
   unsigned long long local = 0;
@@ -292,6 +297,7 @@ __global__ void __launch_bounds__(NT, 1) k_decode(DecodeArgs a) {
         if (tid == 0) atomicOr(a.status, KVCU_STATUS_BAD_LEN);
         len = (uint32_t)cap;
       }
+      if (a.entry_lens) len = min(len, a.entry_lens[b]);
     } else if (tid == 0) {
       atomicOr(a.status, KVCU_STATUS_BAD_SEQ);
     }
@@ -597,8 +603,8 @@ int kvcu_decode_setup(kvcu_decode_ws* ws) {
 }
 
 int kvcu_launch_plan(kvcu_decode_ws* ws, const kvcu_pool* p, uint32_t n, const uint32_t* seq_ids,
-                     uint32_t n_seqs, const uint32_t* lens, cudaStream_t st) {
-  return kvcu_launch_plan_target(ws, p, n, seq_ids, n_seqs, lens, (uint32_t)ws->decode_ctas, st);
+                     uint32_t n_seqs, const uint32_t* lens, cudaStream_t st, const uint32_t* entry_lens) {
+  return kvcu_launch_plan_target(ws, p, n, seq_ids, n_seqs, lens, (uint32_t)ws->decode_ctas, st, entry_lens);
 }
 
 // The plan with at most `ranges` CTA ranges. It makes at most n + ranges - 1
@@ -606,12 +612,13 @@ int kvcu_launch_plan(kvcu_decode_ws* ws, const kvcu_pool* p, uint32_t n, const u
 // (ws->decode_ctas) must be >= ranges.
 int kvcu_launch_plan_target(kvcu_decode_ws* ws, const kvcu_pool* p, uint32_t n,
                             const uint32_t* seq_ids, uint32_t n_seqs, const uint32_t* lens,
-                            uint32_t ranges, cudaStream_t st) {
+                            uint32_t ranges, cudaStream_t st, const uint32_t* entry_lens) {
   const uint32_t align = p->block_size > 128u ? p->block_size : 128u;
   if (ranges > ws->max_ranges) ranges = ws->max_ranges;
   if (ranges > (uint32_t)ws->decode_ctas) ranges = (uint32_t)ws->decode_ctas;
   if (ranges < 1) ranges = 1;
-  k_plan<<<1, 1024, 0, st>>>(n, seq_ids, n_seqs, lens, ranges, align, ws->max_items, ws->items,
+  ws->entry_lens = entry_lens;  // the decodes that use this plan read the same per-entry lengths
+  k_plan<<<1, 1024, 0, st>>>(n, seq_ids, n_seqs, lens, entry_lens, ranges, align, ws->max_items, ws->items,
                              ws->meta, ws->ranges, ws->seq_first, ws->seq_count);
   return kvcu_check_cuda(cudaGetLastError(), "plan kernel launch");
 }
@@ -684,6 +691,7 @@ int kvcu_launch_decode(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint32_
   a.part_ml = ws->part_ml;
   a.lse = lse;
   a.ws_heads = ws->max_heads;
+  a.entry_lens = ws->entry_lens;
   int rc = p->quantized ? launch_decode_q<true>(ws, a, st) : launch_decode_q<false>(ws, a, st);
   if (rc) return rc;
   rc = launch_combine(ws, n_heads, out, lse, st);

@@ -134,6 +134,7 @@ struct TcArgs {
   // its partials at item index i*part_lstride + item, its lse at + i*lse_lstride.
   uint32_t n_layers_call;
   uint64_t q_lstride, out_lstride, part_lstride, lse_lstride;
+  const uint32_t* entry_lens;  // optional per-entry attended length (capped by lens[seq]); from the plan
 };
 
 // Work unit u of a CTA whose plan range holds `cnt` items from `it_begin`:
@@ -441,6 +442,7 @@ __device__ __forceinline__ Item load_item(const TcArgs& a, uint32_t it) {
     len = a.lens[r.s];
     const uint64_t cap = (uint64_t)(r.t1 - r.t0) * a.block_size;
     if (len > cap) len = (uint32_t)cap;
+    if (a.entry_lens) len = min(len, a.entry_lens[ki.b]);
   }
   r.tok0 = ki.start;
   r.tok1 = min(ki.end, len);
@@ -1254,6 +1256,7 @@ int kvcu_launch_decode_tc(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint
   a.out_lstride = out_lstride;
   a.part_lstride = ws->max_items;
   a.lse_lstride = lse_lstride;
+  a.entry_lens = ws->entry_lens;
   if (n_heads <= 8) return launch_tc<8>(ws->decode_ctas, lat, rope, a, st);
   if (n_heads <= 16) return launch_tc<16>(ws->decode_ctas, lat, rope, a, st);
   if (n_heads <= 20) return launch_tc<20>(ws->decode_ctas, lat, rope, a, st);

@@ -40,6 +40,7 @@ struct kvcu_decode_ws {
   uint32_t* seq_count;       // [max_batch] items of entry b
   float* part_o;             // [max_layers][max_items][max_heads][512]
   float* part_ml;            // [max_layers][max_items][max_heads][2] (m, l)
+  const uint32_t* entry_lens;  // per-entry lengths of the last plan (device; nullptr: whole sequences)
   uint32_t last_launches;
   int num_sms;
   int decode_ctas;           // resident decode CTAs (grid of the persistent kernel)
@@ -116,11 +117,13 @@ int kvcu_launch_synth(uint64_t seed, uint64_t a, uint32_t n_rows, const uint32_t
 
 // ---- decode (kvcu_decode.cu) ----
 int kvcu_decode_setup(kvcu_decode_ws* ws);
+// entry_lens (nullable, device): entry b attends min(entry_lens[b], lens[seq])
+// positions; recorded in the workspace for the decodes that use the plan.
 int kvcu_launch_plan(kvcu_decode_ws* ws, const kvcu_pool* p, uint32_t n, const uint32_t* seq_ids,
-                     uint32_t n_seqs, const uint32_t* lens, cudaStream_t st);
+                     uint32_t n_seqs, const uint32_t* lens, cudaStream_t st, const uint32_t* entry_lens = nullptr);
 int kvcu_launch_plan_target(kvcu_decode_ws* ws, const kvcu_pool* p, uint32_t n,
                             const uint32_t* seq_ids, uint32_t n_seqs, const uint32_t* lens,
-                            uint32_t target, cudaStream_t st);
+                            uint32_t target, cudaStream_t st, const uint32_t* entry_lens = nullptr);
 // ---- allocation-free decode (kvcu_noalloc.cu) ----
 // Resolve (and so reserve) the fixed decode scratch on `device`, which must be
 // current; kvcu_init calls it.

@@ -75,6 +75,7 @@ _SIGS = {
                                       _vp, _u64, _vp]),
     "kvcu_decode_ws_destroy": (_i32, [_vp]),
     "kvcu_decode_plan": (_i32, [_vp, _vp, _u32, _vp, _u32, _vp, _vp]),
+    "kvcu_decode_plan_causal": (_i32, [_vp, _vp, _u32, _vp, _u32, _vp, _vp, _vp]),
     "kvcu_mla_decode": (_i32, [_vp, _vp, _u32, _u32, _vp, _u32, _vp, _vp, _vp, _vp, _u32, _f32, _vp, _vp]),
     "kvcu_mla_decode_lse": (_i32, [_vp, _vp, _u32, _u32, _vp, _u32, _vp, _vp, _vp, _vp, _u32, _f32, _vp, _vp,
                                    _vp]),
@@ -127,6 +128,8 @@ _SIGS = {
     "kvcache_append_batch_dev": (_i32, [_vp, _u32, _u32, _vp, _vp, _vp, _vp, _vp, _vp]),
     "kvcache_gather": (_i32, [_vp, _u32, _u32, _vp]),
     "kvcache_mla_decode": (_i32, [_vp, _u32, _u32, _vp, _vp, _u32, _f32, _vp]),
+    "kvcache_mla_attention_batch": (_i32, [_vp, _u32, _u32, _u32, _u32, _vp, _u32, _f32, _vp]),
+    "kvcache_mla_attention_batch_dev": (_i32, [_vp, _u32, _u32, _u32, _u32, _vp, _u32, _f32, _vp, _vp]),
     "kvcache_mla_decode_dev": (_i32, [_vp, _u32, _u32, _vp, _vp, _u32, _f32, _vp, _vp]),
     "kvcache_append_layers_dev": (_i32, [_vp, _u32, _u32, _u32, _vp, _vp, _vp, _vp, _vp, _u64, _vp]),
     "kvcache_mla_decode_layers_dev": (_i32, [_vp, _u32, _u32, _u32, _vp, _vp, _u64, _u32, _f32, _vp, _u64, _vp]),
@@ -637,6 +640,22 @@ class KVCache:
         check(lib().kvcache_mla_decode(self._h, layer, n, _np_ptr(s), _np_ptr(q), H, scale,
                                        _np_ptr(out)), "mlaDecode")
         return out
+
+    def mlaAttentionBatch(self, layer, seq, start_pos, q, scale, out=None):
+        """mlaAttentionBatch (src/inference.zig:670-883): host q [n_pos][H][W] for positions
+        start_pos.. of `seq`, each attending causally -> out host [n_pos][H][kv_rank]."""
+        q = np.ascontiguousarray(q, np.float32)
+        n, H = q.shape[0], q.shape[1]
+        if out is None:
+            out = np.zeros((n, H, self.kv_rank), np.float32)
+        check(lib().kvcache_mla_attention_batch(self._h, layer, seq, start_pos, n, _np_ptr(q), H, scale,
+                                                _np_ptr(out)), "mlaAttentionBatch")
+        return out
+
+    def mlaAttentionBatch_dev(self, layer, seq, start_pos, q_dev, scale, out_dev, stream=None):
+        n, H = q_dev.shape[0], q_dev.shape[1]
+        check(lib().kvcache_mla_attention_batch_dev(self._h, layer, seq, start_pos, n, _dptr(q_dev), H, scale,
+                                                    _dptr(out_dev), _stream(stream)), "mlaAttentionBatch_dev")
 
     def mlaDecode_ptr(self, layer, n, seq_ids, q_ptr, n_heads, scale, out_ptr):
         """Host-buffer decode on raw host addresses (pinned buffers for the e2e path)."""
