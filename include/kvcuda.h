@@ -468,6 +468,22 @@ int kvcache_last_decode_impl(const kvcache* c);
  * pool).  Single-sequence caches use kvcache_save_to_file (v1, byte-exact). */
 int kvcache_save_to_file_v2(kvcache* c, const char* path);
 int kvcache_load_from_file_v2(kvcache* c, const char* path);
+/* The v2 save in the background, overlapped with serving (the asynchronous
+ * checkpoint I/O around src/kv_cache.zig:453-591).  The call captures the
+ * header, every sequence's length and block table, and retains each block of
+ * those tables once more, so none returns to the free list and any later write
+ * into one first copies it (copy-on-write): the file holds the cache exactly
+ * as it was when the work queued on `stream` (may be NULL) and on the cache's
+ * own stream had run.  A worker thread then copies the pool section device ->
+ * pinned host -> file on its own CUDA stream while the caller keeps appending
+ * and decoding.  kvcache_save_wait joins it, drops the snapshot's references
+ * and returns its status; kvcache_save_done polls.  One save per cache at a
+ * time; loadFromFile and enableQuantization are refused while it runs, and
+ * kvcache_deinit waits for it. */
+typedef struct kvcache_save kvcache_save;
+int kvcache_save_to_file_v2_async(kvcache* c, const char* path, void* stream, kvcache_save** job);
+int kvcache_save_done(const kvcache_save* job);
+int kvcache_save_wait(kvcache_save* job);
 
 /* ---- continuous batching over one pool (BatchScheduler, src/batch_queue.zig:75-232) ----
  * Each request is a sequence of the kvcache (instead of owning a KVCache,

@@ -21,7 +21,9 @@
 #include <unistd.h>
 
 #include <algorithm>
+#include <atomic>
 #include <errno.h>
+#include <string>
 #include <new>
 #include <thread>
 #include <unordered_map>
@@ -229,6 +231,11 @@ struct kvcache {
   uint32_t last_launches = 0;
   int decode_impl = KVCU_DECODE_AUTO;
   int last_mapped = 0;  // the last host-buffer decode read q / wrote out in place (pinned, mapped)
+  // background save (kvcache_save_to_file_v2_async): the job in flight, and its
+  // device staging and two pinned host buffers, kept for the next save
+  kvcache_save* active_save = nullptr;
+  uint8_t* save_stg = nullptr;
+  uint8_t* save_host[2] = {nullptr, nullptr};
 
   bool quantized() const { return pool && pool->quantized; }
   uint32_t row_width() const { return kv_rank + rope_dim; }
@@ -727,6 +734,10 @@ kvcache* kvcache_init_blocks(int device, uint32_t n_layers, uint32_t kv_rank, ui
 void kvcache_deinit(kvcache* c) {
   if (!c) return;
   DevScope d(c->device);
+  if (c->active_save) kvcache_save_wait(c->active_save);  // the worker reads the pool
+  if (c->save_stg) cudaFree(c->save_stg);
+  for (uint8_t* h : c->save_host)
+    if (h) cudaFreeHost(h);
   if (c->stream) cudaStreamSynchronize(c->stream);
   kvcu_decode_ws_destroy(c->ws);
   kvcu_pool_destroy(c->pool);
@@ -751,6 +762,10 @@ void kvcache_deinit(kvcache* c) {
 // reference keeps both; data written before the switch is not converted
 // there either, its getters read the new Q8_0 pools afterwards).
 int kvcache_enable_quantization(kvcache* c) {
+  if (c && c->active_save) {
+    kvcu_set_error("enableQuantization: a background save is reading the pool (kvcache_save_wait first)");
+    return KVCU_ERR_INVALID_ARG;
+  }
   if (!c) return KVCU_ERR_INVALID_ARG;
   if (c->quantized()) return KVCU_OK;
   DevScope d(c->device);
@@ -1332,6 +1347,10 @@ int kvcache_save_to_file(kvcache* c, const char* path) {
 // src/kv_cache.zig:497-546 with block-id validation and free-list removal.
 int kvcache_load_from_file(kvcache* c, const char* path) {
   if (!c || !path) return KVCU_ERR_INVALID_ARG;
+  if (c->active_save) {
+    kvcu_set_error("loadFromFile: a background save is reading the pool (kvcache_save_wait first)");
+    return KVCU_ERR_INVALID_ARG;
+  }
   // A v1 file holds one sequence and overwrites the whole pool; with other
   // sequences holding blocks it would clobber their rows and could hand one of
   // their blocks to sequence 0 as well.  The reference's cache has a single
@@ -1454,6 +1473,10 @@ int kvcache_save_to_file_v2(kvcache* c, const char* path) {
 
 int kvcache_load_from_file_v2(kvcache* c, const char* path) {
   if (!c || !path) return KVCU_ERR_INVALID_ARG;
+  if (c->active_save) {
+    kvcu_set_error("loadFromFile: a background save is reading the pool (kvcache_save_wait first)");
+    return KVCU_ERR_INVALID_ARG;
+  }
   DevScope d(c->device);
   Fd f(open(path, O_RDONLY | O_CLOEXEC));
   if (f.fd < 0) {
@@ -1505,6 +1528,158 @@ int kvcache_load_from_file_v2(kvcache* c, const char* path) {
   c->tables_dirty = c->lens_dirty = true;
   c->epoch++;
   return KVCU_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------- background save
+// A v2 checkpoint written while serving goes on.  At the call, the header and
+// every sequence's length and block table are captured and every block in
+// those tables is retained once more, so (i) no block of the snapshot returns
+// to the free list and (ii) any write into one of them first copies it to a
+// fresh block (copy-on-write, as for shared prefix blocks).  The snapshot's
+// rows therefore stay as they were while a worker thread copies the pool
+// section device -> pinned host -> file on its own stream, overlapped with
+// the caller's kernels; kvcache_save_wait joins it and drops the extra refs.
+struct kvcache_save {
+  kvcache* c = nullptr;
+  std::thread worker;
+  std::atomic<int> done{0};
+  int rc = KVCU_OK;
+  char err[512] = {0};
+  std::vector<uint32_t> held;  // blocks retained for the snapshot
+  uint64_t bytes = 0;
+};
+
+namespace {
+
+constexpr size_t kSaveChunk = 64ull << 20;
+
+void save_worker(kvcache_save* job, int device, kvcu_pool* pool, std::string path, std::vector<uint8_t> head,
+                 cudaEvent_t start, uint8_t* stg, uint8_t* hbuf0, uint8_t* hbuf1) {
+  int rc = kvcu_check_cuda(cudaSetDevice(device), "cudaSetDevice(save worker)");
+  cudaStream_t st = nullptr;
+  if (!rc) rc = kvcu_check_cuda(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking), "cudaStreamCreate(save)");
+  // the pool section is read only after the work queued before the call
+  if (!rc) rc = kvcu_check_cuda(cudaStreamWaitEvent(st, start, 0), "cudaStreamWaitEvent(save)");
+  Fd f(rc ? -1 : open(path.c_str(), O_WRONLY | O_CREAT | O_TRUNC | O_CLOEXEC, 0644));
+  if (!rc && f.fd < 0) {
+    kvcu_set_error("open(%s): %s", path.c_str(), strerror(errno));
+    rc = KVCU_ERR_IO;
+  }
+  if (!rc) rc = write_all(f.fd, head.data(), head.size());
+  uint64_t written = head.size();
+  kvcu_pool_desc desc;
+  if (!rc) rc = kvcu_pool_describe(pool, &desc);
+  if (!rc) {
+    // chunk k is copied into one buffer while the file write of chunk k-1 from
+    // the other runs in a helper thread
+    uint8_t* bufs[2] = {hbuf0, hbuf1};
+    const uint64_t total = desc.checkpoint_bytes;
+    std::thread writer;
+    int wrc = KVCU_OK;
+    uint64_t k = 0;
+    for (uint64_t off = 0; off < total; off += kSaveChunk, ++k) {
+      const uint64_t n = std::min<uint64_t>(kSaveChunk, total - off);
+      uint8_t* b = bufs[k & 1];
+      rc = kvcu_pool_read_checkpoint_staged(pool, off, n, b, st, stg, kSaveChunk);
+      if (writer.joinable()) writer.join();
+      if (rc || wrc) break;
+      writer = std::thread([&wrc, fd = f.fd, b, n]() { wrc = write_all(fd, b, n); });
+      written += n;
+    }
+    if (writer.joinable()) writer.join();
+    if (!rc && wrc) {
+      kvcu_set_error("checkpoint write failed");
+      rc = wrc;
+    }
+  }
+  if (st) cudaStreamDestroy(st);
+  cudaEventDestroy(start);
+  job->rc = rc;
+  job->bytes = written;
+  if (rc) snprintf(job->err, sizeof(job->err), "%s", kvcu_get_last_error());
+  job->done.store(1);
+}
+
+}  // namespace
+
+extern "C" {
+
+int kvcache_save_to_file_v2_async(kvcache* c, const char* path, void* stream, kvcache_save** job_out) {
+  if (!c || !path || !job_out) return KVCU_ERR_INVALID_ARG;
+  *job_out = nullptr;
+  if (c->active_save) {
+    kvcu_set_error("a background save of this cache is already running");
+    return KVCU_ERR_INVALID_ARG;
+  }
+  DevScope d(c->device);
+  // buffers kept across saves: device staging for the Q8_0 repacking, two pinned chunks
+  if (!c->save_stg) KVCU_CUDA(cudaMalloc(&c->save_stg, kSaveChunk));
+  for (auto& h : c->save_host)
+    if (!h) KVCU_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&h), kSaveChunk, cudaHostAllocDefault));
+  // start after the caller's stream and the cache's own stream
+  cudaEvent_t start = nullptr;
+  KVCU_CUDA(cudaEventCreateWithFlags(&start, cudaEventDisableTiming));
+  if (stream) {
+    KVCU_CUDA(cudaEventRecord(start, (cudaStream_t)stream));
+    KVCU_CUDA(cudaStreamWaitEvent(c->stream, start, 0));
+  }
+  KVCU_CUDA(cudaEventRecord(start, c->stream));
+  // header and tables as kvcache_save_to_file_v2 writes them, captured now
+  uint64_t total = 0;
+  for (auto& s : c->seqs) total += s.table.size();
+  std::vector<uint8_t> head(48 + 8 * c->seqs.size() + 4 * total, 0);
+  uint8_t* h = head.data();
+  memcpy(h, "KVCK", 4);
+  put_le32(h + 4, 2);
+  put_le32(h + 8, (uint32_t)c->seqs.size());
+  h[12] = c->quantized() ? 1 : 0;
+  put_le32(h + 16, c->n_layers);
+  put_le32(h + 20, c->num_blocks);
+  put_le32(h + 24, c->block_size);
+  put_le32(h + 28, c->kv_rank);
+  put_le32(h + 32, c->rope_dim);
+  put_le32(h + 36, (uint32_t)total);
+  size_t o = 48;
+  for (auto& s : c->seqs) {
+    put_le32(h + o, s.len);
+    put_le32(h + o + 4, (uint32_t)s.table.size());
+    o += 8;
+  }
+  kvcache_save* job = new (std::nothrow) kvcache_save();
+  if (!job) {
+    cudaEventDestroy(start);
+    return KVCU_ERR_NO_MEMORY;
+  }
+  job->c = c;
+  job->held.reserve(total);
+  for (auto& s : c->seqs)
+    for (uint32_t id : s.table) {
+      put_le32(h + o, id);
+      o += 4;
+      retain_block(c, id);  // the snapshot's own reference
+      job->held.push_back(id);
+    }
+  c->active_save = job;
+  job->worker = std::thread(save_worker, job, c->device, c->pool, std::string(path), std::move(head), start,
+                            c->save_stg, c->save_host[0], c->save_host[1]);
+  *job_out = job;
+  return KVCU_OK;
+}
+
+int kvcache_save_done(const kvcache_save* job) { return job ? job->done.load() : 1; }
+
+int kvcache_save_wait(kvcache_save* job) {
+  if (!job) return KVCU_ERR_INVALID_ARG;
+  if (job->worker.joinable()) job->worker.join();
+  kvcache* c = job->c;
+  for (uint32_t id : job->held) release_block(c, id);  // blocks no sequence holds any more go back
+  if (c->active_save == job) c->active_save = nullptr;
+  const int rc = job->rc;
+  if (rc) kvcu_set_error("%s", job->err);
+  delete job;
+  return rc;
 }
 
 }  // extern "C"

@@ -513,8 +513,9 @@ static int ensure_staging(kvcu_pool* p) {
 // Walk [offset, offset+nbytes) of the checkpoint pool section in chunks.
 // f32: plain copies out of / into the kv and pe pools.  Q8_0: whole 34-byte
 // blocks are (un)packed through the device staging buffer.
+// Q8_0 pools repack through `stg` (stg_bytes of device memory); f32 pools need none.
 static int checkpoint_io(kvcu_pool* p, uint64_t offset, uint64_t nbytes, uint8_t* host,
-                         bool to_host, cudaStream_t st) {
+                         bool to_host, cudaStream_t st, uint8_t* stg, uint64_t stg_bytes) {
   const uint64_t total = checkpoint_bytes(p);
   if (offset > total || nbytes > total - offset) {
     kvcu_set_error("checkpoint range [%llu, +%llu) outside the %llu-byte pool section",
@@ -547,11 +548,14 @@ static int checkpoint_io(kvcu_pool* p, uint64_t offset, uint64_t nbytes, uint8_t
     KVCU_CUDA(cudaStreamSynchronize(st));
     return KVCU_OK;
   }
-  int rc = ensure_staging(p);
-  if (rc) return rc;
+  int rc = KVCU_OK;
+  if (!stg || stg_bytes < 34u) {
+    kvcu_set_error("checkpoint repacking needs a device staging buffer");
+    return KVCU_ERR_INVALID_ARG;
+  }
   const uint64_t part0_blocks = p->rows() * p->nbk;
   const uint64_t part0_bytes = part0_blocks * 34u;
-  const uint64_t chunk_blocks = p->staging_bytes / 34u;
+  const uint64_t chunk_blocks = stg_bytes / 34u;
   uint64_t done = 0;
   while (done < nbytes) {
     const uint64_t off = offset + done;
@@ -566,18 +570,18 @@ static int checkpoint_io(kvcu_pool* p, uint64_t offset, uint64_t nbytes, uint8_t
     nblk = std::min(nblk, part_blocks - blk0);
     const uint64_t n = std::min(want, nblk * 34u - skip);
     if (to_host) {
-      rc = kvcu_launch_pack_q8(p, part, blk0, nblk, p->staging, st);
+      rc = kvcu_launch_pack_q8(p, part, blk0, nblk, stg, st);
       if (rc) return rc;
-      KVCU_CUDA(cudaMemcpyAsync(host + done, p->staging + skip, n, cudaMemcpyDeviceToHost, st));
+      KVCU_CUDA(cudaMemcpyAsync(host + done, stg + skip, n, cudaMemcpyDeviceToHost, st));
       KVCU_CUDA(cudaStreamSynchronize(st));
     } else {
       // partial first/last blocks: read-modify-write through the staging buffer
       if (skip != 0 || n != nblk * 34u) {
-        rc = kvcu_launch_pack_q8(p, part, blk0, nblk, p->staging, st);
+        rc = kvcu_launch_pack_q8(p, part, blk0, nblk, stg, st);
         if (rc) return rc;
       }
-      KVCU_CUDA(cudaMemcpyAsync(p->staging + skip, host + done, n, cudaMemcpyHostToDevice, st));
-      rc = kvcu_launch_unpack_q8(p, part, blk0, nblk, p->staging, st);
+      KVCU_CUDA(cudaMemcpyAsync(stg + skip, host + done, n, cudaMemcpyHostToDevice, st));
+      rc = kvcu_launch_unpack_q8(p, part, blk0, nblk, stg, st);
       if (rc) return rc;
       KVCU_CUDA(cudaStreamSynchronize(st));
     }
@@ -591,8 +595,12 @@ int kvcu_pool_read_checkpoint(kvcu_pool* p, uint64_t offset, uint64_t nbytes, vo
   if (!valid_pool(p) || (nbytes && !host_dst)) return KVCU_ERR_INVALID_ARG;
   DeviceGuard g(p->device);
   if (g.rc) return g.rc;
-  return checkpoint_io(p, offset, nbytes, static_cast<uint8_t*>(host_dst), true,
-                       (cudaStream_t)stream);
+  if (p->quantized) {
+    const int rc = ensure_staging(p);
+    if (rc) return rc;
+  }
+  return checkpoint_io(p, offset, nbytes, static_cast<uint8_t*>(host_dst), true, (cudaStream_t)stream, p->staging,
+                       p->staging_bytes);
 }
 
 int kvcu_pool_write_checkpoint(kvcu_pool* p, uint64_t offset, uint64_t nbytes,
@@ -600,9 +608,27 @@ int kvcu_pool_write_checkpoint(kvcu_pool* p, uint64_t offset, uint64_t nbytes,
   if (!valid_pool(p) || (nbytes && !host_src)) return KVCU_ERR_INVALID_ARG;
   DeviceGuard g(p->device);
   if (g.rc) return g.rc;
-  return checkpoint_io(p, offset, nbytes, const_cast<uint8_t*>(static_cast<const uint8_t*>(host_src)),
-                       false, (cudaStream_t)stream);
+  if (p->quantized) {
+    const int rc = ensure_staging(p);
+    if (rc) return rc;
+  }
+  return checkpoint_io(p, offset, nbytes, const_cast<uint8_t*>(static_cast<const uint8_t*>(host_src)), false,
+                       (cudaStream_t)stream, p->staging, p->staging_bytes);
 }
+
+}  // extern "C"
+
+// Read a checkpoint byte range through a caller-owned staging buffer (the
+// background save uses its own, so the pool's stays free for other calls).
+int kvcu_pool_read_checkpoint_staged(kvcu_pool* p, uint64_t offset, uint64_t nbytes, void* host_dst,
+                                     cudaStream_t st, uint8_t* staging, uint64_t staging_bytes) {
+  if (!valid_pool(p) || (nbytes && !host_dst)) return KVCU_ERR_INVALID_ARG;
+  DeviceGuard g(p->device);
+  if (g.rc) return g.rc;
+  return checkpoint_io(p, offset, nbytes, static_cast<uint8_t*>(host_dst), true, st, staging, staging_bytes);
+}
+
+extern "C" {
 
 int kvcu_synth_rows(uint64_t seed, uint64_t a, uint32_t n_rows, const uint32_t* b,
                     const uint32_t* c, uint32_t width, float outlier_p, float* out, void* stream) {

@@ -124,6 +124,9 @@ int kvcu_launch_plan(kvcu_decode_ws* ws, const kvcu_pool* p, uint32_t n, const u
 int kvcu_launch_plan_target(kvcu_decode_ws* ws, const kvcu_pool* p, uint32_t n,
                             const uint32_t* seq_ids, uint32_t n_seqs, const uint32_t* lens,
                             uint32_t target, cudaStream_t st, const uint32_t* entry_lens = nullptr);
+// ---- checkpoint bytes through a caller-owned device staging buffer (kvcu_api.cu) ----
+int kvcu_pool_read_checkpoint_staged(kvcu_pool* p, uint64_t offset, uint64_t nbytes, void* host_dst,
+                                     cudaStream_t st, uint8_t* staging, uint64_t staging_bytes);
 // ---- allocation-free decode (kvcu_noalloc.cu) ----
 // Resolve (and so reserve) the fixed decode scratch on `device`, which must be
 // current; kvcu_init calls it.

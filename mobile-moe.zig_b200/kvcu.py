@@ -142,6 +142,9 @@ _SIGS = {
     "kvcache_last_decode_impl": (_i32, [_vp]),
     "kvcache_save_to_file_v2": (_i32, [_vp, _cp]),
     "kvcache_load_from_file_v2": (_i32, [_vp, _cp]),
+    "kvcache_save_to_file_v2_async": (_i32, [_vp, _cp, _vp, C.POINTER(_vp)]),
+    "kvcache_save_done": (_i32, [_vp]),
+    "kvcache_save_wait": (_i32, [_vp]),
     "kvcu_batch_create": (_vp, [_vp, _u32]),
     "kvcu_batch_destroy": (_i32, [_vp]),
     "kvcu_batch_add_request": (_i64, [_vp, _u32, _i32]),
@@ -522,6 +525,14 @@ class KVCache:
     def loadFromFileV2(self, path):
         check(lib().kvcache_load_from_file_v2(self._h, os.fsencode(str(path))), "loadFromFileV2")
 
+    def saveToFileV2Async(self, path, stream=None) -> "SaveJob":
+        """Background v2 save of the cache as it is now (kvcache_save_to_file_v2_async);
+        serving may go on; .wait() returns when the file is complete."""
+        h = C.c_void_p()
+        check(lib().kvcache_save_to_file_v2_async(self._h, os.fsencode(str(path)), _stream(stream), C.byref(h)),
+              "saveToFileV2Async")
+        return SaveJob(h.value)
+
     def cacheBlock(self, block_idx, token_ids, prefix_hash):
         t = np.ascontiguousarray(token_ids, np.uint32)
         lib().kvcache_cache_block(self._h, block_idx, _np_ptr(t), t.size, prefix_hash)
@@ -732,6 +743,21 @@ class KVCache:
             synth_rows(seed, layer, t_d, p_d, W, rows[:n], outlier_p, stream)
             self.appendBatch_dev(layer, s_h, p_h, s_d, p_d, rows[:n], stream)
         return total
+
+
+class SaveJob:
+    """A background checkpoint save (kvcache_save_to_file_v2_async)."""
+
+    def __init__(self, handle):
+        self._h = handle
+
+    def done(self) -> bool:
+        return bool(lib().kvcache_save_done(self._h))
+
+    def wait(self):
+        if self._h:
+            h, self._h = self._h, None
+            check(lib().kvcache_save_wait(h), "kvcache_save_wait")
 
 
 SEQ_WAITING, SEQ_RUNNING, SEQ_PAUSED, SEQ_COMPLETED = 0, 1, 2, 3
