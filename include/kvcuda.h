@@ -251,6 +251,18 @@ int kvcu_mla_decode_layers(kvcu_decode_ws* ws, kvcu_pool* pool, uint32_t layer, 
                            const uint32_t* seq_ids, uint32_t n_seqs, const uint32_t* table_offsets,
                            const uint32_t* tables, const uint32_t* lens, const float* q, uint64_t q_layer_stride,
                            uint32_t n_heads, float scale, float* out, uint64_t out_layer_stride, void* stream);
+/* The step's per-head contractions as one call: for head z < heads,
+ * C_z[m][n] = sum_k A_z[m][k] * B_z(k, n) with A_z = A + z*a_hs (row stride
+ * lda), C_z = C + z*c_hs (ldc), B_z(k, n) = B[z*b_hs + (trans_b ? n*ldb + k :
+ * k*ldb + n)], all f32 device arrays.  impl 0: the tcgen05 kernel (3xTF32:
+ * hi/lo TF32 parts, three MMAs per K-step, f32 accumulation in TMEM) where the
+ * shapes fit it (N % 128 == 0, K % 32 == 0, 16-byte aligned rows), else the
+ * CUDA-core f32 kernel; 1: CUDA cores; 2: tensor cores or
+ * KVCU_ERR_UNSUPPORTED.  kvcu_mla_prepare / kvcu_mla_finish use impl 0.
+ * `pool` gives the device and the status word for a timed-out wait. */
+int kvcu_head_gemm(int trans_b, uint32_t heads, uint32_t M, uint32_t N, uint32_t K, const float* A, uint32_t lda,
+                   uint64_t a_hs, const float* B, uint32_t ldb, uint64_t b_hs, float* C, uint32_t ldc,
+                   uint64_t c_hs, int impl, kvcu_pool* pool, void* stream);
 /* Kernel launches the last kvcu_mla_decode issued (for launch accounting). */
 uint32_t kvcu_decode_last_launches(const kvcu_decode_ws* ws);
 /* Decode kernel selection.  AUTO uses the tcgen05 tensor-core kernel for Q8_0
@@ -262,6 +274,18 @@ uint32_t kvcu_decode_last_launches(const kvcu_decode_ws* ws);
 #define KVCU_DECODE_CUDA_CORE 1
 #define KVCU_DECODE_TENSOR_CORE 2
 int kvcu_decode_ws_set_impl(kvcu_decode_ws* ws, int impl);
+/* Every wait of the tensor-core decode kernel is bounded: after `cycles` SM
+ * clocks (0 = the default, 2^31, about a second at 1.9 GHz) the CTA records
+ * KVCU_STATUS_TIMEOUT in the pool's status word, all its roles unwind, its
+ * in-flight copies and MMAs are waited for (with the same bound) and its TMEM
+ * is released, so the context stays usable and the host reads the error.  At
+ * most 2^40. */
+int kvcu_decode_ws_set_wait_limit(kvcu_decode_ws* ws, uint64_t cycles);
+/* Test hook for that unwind, needing no GPU fault: in the tensor-core kernel,
+ * every CTA's producer skips the copy and the arrival of the first slice of
+ * its tile number `tile` (0-based, counted over the CTA's whole range), so the
+ * waits on that tile run out.  0xFFFFFFFF turns it off (the default). */
+int kvcu_decode_ws_test_withhold(kvcu_decode_ws* ws, uint32_t tile);
 int kvcu_decode_last_impl(const kvcu_decode_ws* ws);
 
 /* Decode without any allocation.  No counterpart in the reference: this is an

@@ -502,6 +502,18 @@ int kvcu_decode_ws_set_impl(kvcu_decode_ws* ws, int impl) {
 
 int kvcu_decode_last_impl(const kvcu_decode_ws* ws) { return ws ? ws->last_impl : 0; }
 
+int kvcu_decode_ws_set_wait_limit(kvcu_decode_ws* ws, uint64_t cycles) {
+  if (!ws || cycles > (1ull << 40)) return KVCU_ERR_INVALID_ARG;
+  ws->wait_limit = cycles;
+  return KVCU_OK;
+}
+
+int kvcu_decode_ws_test_withhold(kvcu_decode_ws* ws, uint32_t tile) {
+  if (!ws) return KVCU_ERR_INVALID_ARG;
+  ws->withhold_plus1 = tile == 0xFFFFFFFFu ? 0u : tile + 1u;
+  return KVCU_OK;
+}
+
 // ---------------------------------------------------------------- checkpoint
 static int ensure_staging(kvcu_pool* p) {
   if (p->staging) return KVCU_OK;

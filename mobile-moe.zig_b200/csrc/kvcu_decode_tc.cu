@@ -40,8 +40,10 @@
 #include <math.h>
 
 #include "kvcu_internal.h"
+#include "kvcu_tcgen05.cuh"
 
 namespace {
+using namespace kvtc;
 
 constexpr int R = 512, P = 64, W = 576;
 constexpr int TILE = 128;            // tokens per tile (MMA M for QK)
@@ -96,10 +98,13 @@ constexpr int B_KV_FULL = 0, B_SL_EMPTY = 2 /* 2 stages x NSL slices */, B_QK_FU
               NUM_BARS = B_EPI + 2;
 static_assert(NUM_BARS * 8 <= 352, "mbarriers overlap the misc words");
 constexpr uint32_t OFF_TMEM_BASE = OFF_MISC + 352;            // u32
-constexpr uint32_t OFF_ABORT = OFF_MISC + 356;                // u32
+constexpr uint32_t OFF_ABORT = OFF_MISC + 368;                // u32, followed by the wait limit
+constexpr uint32_t OFF_WAIT_LIMIT = OFF_MISC + 376;           // i64: clocks a bounded wait may take
 constexpr uint32_t OFF_CUR_ITEM = OFF_MISC + 360;             // u32: the epilogue's current item
 constexpr uint32_t ITEMS_DONE = 0xFFFFFFFFu;
 constexpr uint32_t OFF_ONES = OFF_MISC + 384;                 // 128 B of f16 1.0 (l = ones x P^T)
+static_assert(OFF_WAIT_LIMIT == OFF_ABORT + 8 && OFF_WAIT_LIMIT % 8 == 0 && OFF_WAIT_LIMIT + 8 <= OFF_ONES,
+              "the wait limit sits two words after the abort flag");
 constexpr uint32_t OFF_QSCALE = OFF_MISC + 512;               // float[24]
 constexpr uint32_t OFF_REDMAX = OFF_MISC + 640;               // float[2][8 warps][24]
 constexpr uint32_t OFF_VOTE = OFF_REDMAX + 2 * EPI_WARPS * 24 * 4;  // u32[2][8 warps] rescale votes
@@ -135,6 +140,8 @@ struct TcArgs {
   uint32_t n_layers_call;
   uint64_t q_lstride, out_lstride, part_lstride, lse_lstride;
   const uint32_t* entry_lens;  // optional per-entry attended length (capped by lens[seq]); from the plan
+  long long wait_limit;        // clocks a bounded wait may take before the CTA gives up
+  uint32_t withhold_plus1;     // test hook: 0, or 1 + the tile whose first slice the producer withholds
 };
 
 // Work unit u of a CTA whose plan range holds `cnt` items from `it_begin`:
@@ -149,40 +156,18 @@ __device__ __forceinline__ Unit unit_of(uint32_t u, uint32_t it_begin, uint32_t 
 }
 
 // ------------------------------------------------------------------ PTX helpers
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive_tx(uint32_t bar, uint32_t tx) {
-  asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(tx)
-               : "memory");
-}
-__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n"
-      " selp.u32 %0, 1, 0, p;\n}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// Bounded wait: gives up after ~2^31 clocks (about a second) or when another
-// role has aborted; any give-up records a timeout in the status word.
+// Bounded wait: gives up after the CTA's wait limit (the 64-bit word two
+// words after the abort flag; ~2^31 clocks, about a second, unless the host
+// set another) or when another role has aborted; any give-up records a
+// timeout in the status word.
 // (Inlined: a call would have to run under several setmaxnreg budgets.)
 __device__ __forceinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity,
                                             volatile uint32_t* abort_flag, uint32_t* status) {
   const long long t0 = clock64();
+  const long long limit = *reinterpret_cast<const volatile long long*>(abort_flag + 2);
   while (true) {
     if (mbar_try(bar, parity)) return true;
-    if (*abort_flag || clock64() - t0 > (1ll << 31)) {
+    if (*abort_flag || clock64() - t0 > limit) {
       *abort_flag = 1u;
       atomicOr(status, STATUS_TIMEOUT);
       return false;
@@ -214,34 +199,16 @@ template <uint32_t N>
 __device__ __forceinline__ void setmaxnreg_inc() {
   asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
 }
-// One lane of a converged warp (the lane that issues tcgen05 work).
-__device__ __forceinline__ bool elect_one() {
-  uint32_t pred = 0;
-  asm volatile(
-      "{\n .reg .b32 r;\n .reg .pred p;\n elect.sync r|p, 0xffffffff;\n selp.u32 %0, 1, 0, p;\n}"
-      : "=r"(pred));
-  return pred != 0;
-}
 // Wait for this CTA's own asynchronous work (copies, MMAs) to retire: bounded
 // by time only, so it still waits after another role has aborted.
-__device__ __forceinline__ void mbar_wait_drain(uint32_t bar, uint32_t parity, uint32_t* status) {
+__device__ __forceinline__ void mbar_wait_drain(uint32_t bar, uint32_t parity, uint32_t* status, long long limit) {
   const long long t0 = clock64();
   while (!mbar_try(bar, parity)) {
-    if (clock64() - t0 > (1ll << 31)) {
+    if (clock64() - t0 > limit) {
       atomicOr(status, STATUS_TIMEOUT);
       return;
     }
   }
-}
-
-__device__ __forceinline__ void fence_proxy_async() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_before() {
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_after() {
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
 // 4-D tile: coordinates innermost first
@@ -279,15 +246,6 @@ __device__ __forceinline__ uint64_t policy_evict_first() {
 __device__ __forceinline__ void prefetch_l2_keep(const void* p) {
   asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(p));
 }
-
-// UMMA shared-memory descriptor (sm_100): start>>4 @0, LBO>>4 @16, SBO>>4 @32,
-// version 1 @46, layout type @61 (0 = none, 2 = 128B swizzle, 4 = 64B swizzle).
-__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo,
-                                              uint32_t layout) {
-  return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
-         ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | ((uint64_t)layout << 61);
-}
-constexpr uint32_t LAYOUT_NONE = 0, LAYOUT_SW128 = 2, LAYOUT_SW64 = 4;
 
 // Instruction descriptors: kind::i8 (s8 x s8 -> s32, both K-major, M=128, N=nqk),
 // kind::f16 (f16 x f16 -> f32, A MN-major, B K-major, M=128, N=32) for PV, and
@@ -328,101 +286,6 @@ __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a, uint64_t b,
       "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
       : "memory");
 }
-__device__ __forceinline__ void mma_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
-               : "memory");
-}
-
-// TMEM loads / stores of N consecutive 32-bit columns of the warp's 32 lanes.
-__device__ __forceinline__ void tld1(uint32_t ta, uint32_t* r) {
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r[0]) : "r"(ta));
-}
-__device__ __forceinline__ void tld2(uint32_t ta, uint32_t* r) {
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0,%1}, [%2];" : "=r"(r[0]), "=r"(r[1]) : "r"(ta));
-}
-__device__ __forceinline__ void tld4(uint32_t ta, uint32_t* r) {
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(ta));
-}
-__device__ __forceinline__ void tld8(uint32_t ta, uint32_t* r) {
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-                 "=r"(r[7])
-               : "r"(ta));
-}
-template <int N>
-__device__ __forceinline__ void tmem_ld(uint32_t ta, uint32_t* r) {
-  if constexpr (N >= 8) {
-    tld8(ta, r);
-    tmem_ld<N - 8>(ta + 8, r + 8);
-  } else if constexpr (N >= 4) {
-    tld4(ta, r);
-    tmem_ld<N - 4>(ta + 4, r + 4);
-  } else if constexpr (N >= 2) {
-    tld2(ta, r);
-    tmem_ld<N - 2>(ta + 2, r + 2);
-  } else if constexpr (N == 1) {
-    tld1(ta, r);
-  }
-}
-__device__ __forceinline__ void tst1(uint32_t ta, const uint32_t* r) {
-  asm volatile("tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};" ::"r"(ta), "r"(r[0]) : "memory");
-}
-__device__ __forceinline__ void tst2(uint32_t ta, const uint32_t* r) {
-  asm volatile("tcgen05.st.sync.aligned.32x32b.x2.b32 [%0], {%1,%2};" ::"r"(ta), "r"(r[0]), "r"(r[1])
-               : "memory");
-}
-__device__ __forceinline__ void tst4(uint32_t ta, const uint32_t* r) {
-  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1,%2,%3,%4};" ::"r"(ta), "r"(r[0]),
-               "r"(r[1]), "r"(r[2]), "r"(r[3])
-               : "memory");
-}
-__device__ __forceinline__ void tst8(uint32_t ta, const uint32_t* r) {
-  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(ta),
-               "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
-               : "memory");
-}
-template <int N>
-__device__ __forceinline__ void tmem_st(uint32_t ta, const uint32_t* r) {
-  if constexpr (N >= 8) {
-    tst8(ta, r);
-    tmem_st<N - 8>(ta + 8, r + 8);
-  } else if constexpr (N >= 4) {
-    tst4(ta, r);
-    tmem_st<N - 4>(ta + 4, r + 4);
-  } else if constexpr (N >= 2) {
-    tst2(ta, r);
-    tmem_st<N - 2>(ta + 2, r + 2);
-  } else if constexpr (N == 1) {
-    tst1(ta, r);
-  }
-}
-__device__ __forceinline__ void tmem_wait_ld() {
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-// Ties registers written by an earlier tcgen05.ld to a point after
-// tcgen05.wait::ld, so no use of them is scheduled before the wait.
-template <int N>
-__device__ __forceinline__ void reg_fence(uint32_t (&r)[N]) {
-#pragma unroll
-  for (int i = 0; i < N; ++i) asm volatile("" : "+r"(r[i]));
-}
-__device__ __forceinline__ void tmem_wait_st() {
-  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-}
-
-// Byte offset of (row, byte) inside a K-major 128B-swizzled region whose rows
-// are 128 B and whose 8-row atoms are 1024 B apart (region base 1024-aligned).
-__device__ __forceinline__ uint32_t sw128_off(uint32_t row, uint32_t byte) {
-  return (row >> 3) * 1024u + (row & 7u) * 128u + ((((byte >> 4) ^ row) & 7u) << 4) + (byte & 15u);
-}
-// Same for 64-byte rows with the 64B swizzle (8-row atoms of 512 B).
-__device__ __forceinline__ uint32_t sw64_off(uint32_t row, uint32_t byte) {
-  return (row >> 3) * 512u + (row & 7u) * 64u + ((((byte >> 4) ^ ((row & 7u) >> 1)) & 3u) << 4) +
-         (byte & 15u);
-}
-
 struct Item {
   uint32_t b, s, t0, t1, tok0, tok1;  // entry, sequence, table range, token range
   uint32_t ntiles;
@@ -488,6 +351,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     mbar_init(bar(B_EPI + 0), EPI_WARPS / 2);
     mbar_init(bar(B_EPI + 1), EPI_WARPS / 2);
     *abort_flag = 0u;
+    *reinterpret_cast<volatile long long*>(smem + OFF_WAIT_LIMIT) = a.wait_limit;
     uint32_t* ones = reinterpret_cast<uint32_t*>(smem + OFF_ONES);
     for (int i = 0; i < 32; ++i) ones[i] = 0x3C003C00u;  // f16 1.0 pairs
     fence_proxy_async();
@@ -552,6 +416,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             // arrive (without bytes) so that the drain below sees the phase end.
             if (!live && !started) break;
             started = true;
+            // test hook (kvcu_decode_ws_test_withhold): no copy and no arrival
+            // for this slice, so the tile never lands and every wait on it runs out
+            if (a.withhold_plus1 && g + 1u == a.withhold_plus1 && i == 0) continue;
             // every segment is one box of br rows inside one physical block (the
             // plan aligns items to max(128, block size); anything else is refused)
             uint32_t bytes = 0;
@@ -579,7 +446,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       }
       // wait (bounded) for the copies of the last two stages to land
       for (uint32_t k = (g >= 2 ? g - 2 : 0); k < g; ++k)
-        mbar_wait_drain(bar(B_KV_FULL + (k & 1u)), (k >> 1) & 1u, a.status);
+        mbar_wait_drain(bar(B_KV_FULL + (k & 1u)), (k >> 1) & 1u, a.status, a.wait_limit);
     }
   } else if (warp == 1) {
     // ================================================================ QK issuer
@@ -633,7 +500,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     // all issued tcgen05 work retires before TMEM is freed
     if (elect_one()) mma_commit(bar(B_FINAL));
     __syncwarp();
-    mbar_wait_drain(bar(B_FINAL), 0, a.status);
+    mbar_wait_drain(bar(B_FINAL), 0, a.status, a.wait_limit);
   } else if (warp == 2) {
     // ================================================================ PV issuer
     // Converged warp, elected issue lane; one wait per 16-token V chunk.
@@ -688,7 +555,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
     if (elect_one()) mma_commit(bar(B_FINAL_PV));
     __syncwarp();
-    mbar_wait_drain(bar(B_FINAL_PV), 0, a.status);
+    mbar_wait_drain(bar(B_FINAL_PV), 0, a.status, a.wait_limit);
   } else {
     // ================================================================ query prefetcher
     // While the epilogue runs item n, pull item n+1's query into L2 (kept
@@ -1257,6 +1124,8 @@ int kvcu_launch_decode_tc(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint
   a.part_lstride = ws->max_items;
   a.lse_lstride = lse_lstride;
   a.entry_lens = ws->entry_lens;
+  a.wait_limit = ws->wait_limit ? (long long)ws->wait_limit : (1ll << 31);
+  a.withhold_plus1 = ws->withhold_plus1;
   if (n_heads <= 8) return launch_tc<8>(ws->decode_ctas, lat, rope, a, st);
   if (n_heads <= 16) return launch_tc<16>(ws->decode_ctas, lat, rope, a, st);
   if (n_heads <= 20) return launch_tc<20>(ws->decode_ctas, lat, rope, a, st);

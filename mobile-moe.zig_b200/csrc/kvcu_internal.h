@@ -41,6 +41,8 @@ struct kvcu_decode_ws {
   float* part_o;             // [max_layers][max_items][max_heads][512]
   float* part_ml;            // [max_layers][max_items][max_heads][2] (m, l)
   const uint32_t* entry_lens;  // per-entry lengths of the last plan (device; nullptr: whole sequences)
+  uint64_t wait_limit;         // clocks a bounded device wait may take (0: the default, ~2^31)
+  uint32_t withhold_plus1;     // test hook: 0, or 1 + the tile whose first slice the producer withholds
   uint32_t last_launches;
   int num_sms;
   int decode_ctas;           // resident decode CTAs (grid of the persistent kernel)
@@ -127,6 +129,12 @@ int kvcu_launch_plan_target(kvcu_decode_ws* ws, const kvcu_pool* p, uint32_t n,
 // ---- checkpoint bytes through a caller-owned device staging buffer (kvcu_api.cu) ----
 int kvcu_pool_read_checkpoint_staged(kvcu_pool* p, uint64_t offset, uint64_t nbytes, void* host_dst,
                                      cudaStream_t st, uint8_t* staging, uint64_t staging_bytes);
+// ---- per-head GEMM on the tensor cores, 3xTF32 (kvcu_gemm_tc.cu) ----
+// KVCU_ERR_UNSUPPORTED (nothing launched) unless N % 128 == 0, K % 32 == 0 and
+// every row and pointer is 16-byte aligned.
+int kvcu_launch_head_gemm_tc(bool trans_b, uint32_t heads, uint32_t M, uint32_t N, uint32_t K, const float* A,
+                             uint32_t lda, uint64_t a_hs, const float* B, uint32_t ldb, uint64_t b_hs, float* C,
+                             uint32_t ldc, uint64_t c_hs, uint32_t* status, cudaStream_t st);
 // ---- allocation-free decode (kvcu_noalloc.cu) ----
 // Resolve (and so reserve) the fixed decode scratch on `device`, which must be
 // current; kvcu_init calls it.

@@ -229,6 +229,80 @@ __global__ void __launch_bounds__(256) k_append_rows(PoolArgs a, uint32_t n_rows
   }
 }
 
+// Q8_0 append for rows of whole 32-element blocks (kv_rank and rope_dim
+// multiples of 32, 16-byte aligned sources, at most 8*NS blocks a row): one
+// warp per (row, layer).  A 4-lane group quantizes one block per step, 8
+// values a lane (two float4 loads, a 2-step shuffle max, one 8-byte store), so
+// a 576-wide row is 3 steps and the per-block work (scale division, f16
+// conversion, scale store) is shared by 4 lanes instead of 8.  The whole row
+// is loaded before its block-table lookup, so both latencies overlap.  Same
+// bytes as k_append.
+template <int NS>
+__global__ void __launch_bounds__(256) k_append_q8(PoolArgs a, uint32_t n_rows, const float* __restrict__ latent,
+                                                   uint64_t ls, const float* __restrict__ rope, uint64_t ps,
+                                                   const uint32_t* __restrict__ row_seq,
+                                                   const uint32_t* __restrict__ row_pos, uint32_t n_seqs,
+                                                   const uint32_t* __restrict__ toff,
+                                                   const uint32_t* __restrict__ tables, uint32_t* __restrict__ lens,
+                                                   uint32_t n_layers_call, uint64_t llat, uint64_t lrope) {
+  const uint32_t lane = threadIdx.x & 31u, grp = lane >> 2, sub = lane & 3u;
+  const uint64_t nwarps = ((uint64_t)gridDim.x * blockDim.x) >> 5;
+  const uint32_t nblk = a.nbk + a.nbp;
+  kvcu_pdl_wait();     // the previous kernel may still read the rows this one writes
+  kvcu_pdl_trigger();  // a programmatically launched decode may start its prologue
+  const uint64_t layer_rows = (uint64_t)a.num_blocks * a.block_size;
+  const uint64_t total = (uint64_t)n_rows * n_layers_call;
+  for (uint64_t ra = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; ra < total; ra += nwarps) {
+    const uint64_t li = ra / n_rows, r = ra - li * n_rows;
+    const float* lat_r = latent + li * llat + r * ls;
+    const float* rope_r = rope + li * lrope + r * ps;
+    const uint32_t s = row_seq[r], pos = row_pos[r];
+    float4 xa[NS], xb[NS];
+#pragma unroll
+    for (int k = 0; k < NS; ++k) {
+      const uint32_t b = 8u * k + grp, e = 32u * b + 8u * sub;
+      xa[k] = xb[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (b < nblk) {
+        const float* src = e < a.kv_rank ? lat_r + e : rope_r + (e - a.kv_rank);
+        xa[k] = __ldg(reinterpret_cast<const float4*>(src));
+        xb[k] = __ldg(reinterpret_cast<const float4*>(src + 4));
+      }
+    }
+    uint64_t row;
+    if (!resolve_row(a, s, pos, n_seqs, toff, tables, lane, &row)) continue;
+    row += li * layer_rows;
+    // len = max(len, pos + 1), src/kv_cache.zig:358-360
+    if (lens && li == 0 && lane == 0) atomicMax(lens + s, pos + 1u);
+    int8_t* qrow = a.qs + row * (32u * nblk);
+    uint16_t* srow = a.sc + row * nblk;
+#pragma unroll
+    for (int k = 0; k < NS; ++k) {
+      if (8u * k >= nblk) break;  // warp-uniform
+      const uint32_t b = 8u * k + grp;
+      const float v[8] = {xa[k].x, xa[k].y, xa[k].z, xa[k].w, xb[k].x, xb[k].y, xb[k].z, xb[k].w};
+      float amax = fabsf(v[0]);
+#pragma unroll
+      for (int i = 1; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+      const float d = kvcu::q8_scale(amax);
+      uint32_t w[2] = {0u, 0u};
+      if (d > 0.0f) {
+        const float inv = kvcu::rcp_approx(d);
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          w[i >> 2] |= (uint32_t)(uint8_t)kvcu::q8_value_fast(v[i], d, inv) << (8 * (i & 3));
+      }
+      if (b < nblk) {
+        *reinterpret_cast<uint2*>(qrow + 32u * b + 8u * sub) = make_uint2(w[0], w[1]);
+        // the hardware RNE conversion gives the same bits as f32_to_f16 for
+        // every non-NaN d (normal, subnormal, overflow to inf)
+        if (sub == 0) srow[b] = d == d ? __half_as_ushort(__float2half_rn(d)) : kvcu::f32_to_f16(d);
+      }
+    }
+  }
+}
+
 // One warp per (row, 32-element block): out = f16ToF32(d) * q, or the f32 row.
 // Rows come either from one table (table != nullptr, row r = position r) or
 // from (row_seq[r], row_pos[r]) through the CSR tables.
@@ -412,6 +486,15 @@ int kvcu_launch_append_layers(kvcu_pool* p, uint32_t layer, uint32_t n_layers_ca
   const bool rows_ok = p->kv_rank % 32 == 0 && p->rope_dim % 32 == 0 && ls % 4 == 0 && ps % 4 == 0 &&
                        llat % 4 == 0 && lrope % 4 == 0 && (reinterpret_cast<uintptr_t>(latent) & 15) == 0 &&
                        (reinterpret_cast<uintptr_t>(rope) & 15) == 0;
+  if (rows_ok && p->quantized && p->nblk <= 32u) {
+    const uint64_t pairs = (uint64_t)n_rows * n_layers_call;
+    const int g = grid_for(pairs, 256);
+    auto kern = p->nblk <= 24u ? (p->nblk <= 16u ? k_append_q8<2> : k_append_q8<3>) : k_append_q8<4>;
+    return kvcu_check_cuda(kvcu_launch_pdl(kern, dim3(g), dim3(256), 0, st, a, n_rows, latent, ls, rope, ps,
+                                           row_seq, row_pos, n_seqs, toff, tables, lens, n_layers_call, llat,
+                                           lrope),
+                           "append kernel launch");
+  }
   if (rows_ok) {
     const uint64_t pairs = (uint64_t)n_rows * n_layers_call;
     const int g = grid_for(pairs, 256);

@@ -173,12 +173,25 @@ __global__ void __launch_bounds__(256)
 }
 
 template <bool TRANS_B>
-int launch_head_gemm(uint32_t heads, uint32_t M, uint32_t N, uint32_t K, const float* A, uint32_t lda,
-                     uint64_t a_hs, const float* B, uint32_t ldb, uint64_t b_hs, float* C, uint32_t ldc,
-                     uint64_t c_hs, cudaStream_t st) {
+int launch_head_gemm_cc(uint32_t heads, uint32_t M, uint32_t N, uint32_t K, const float* A, uint32_t lda,
+                        uint64_t a_hs, const float* B, uint32_t ldb, uint64_t b_hs, float* C, uint32_t ldc,
+                        uint64_t c_hs, cudaStream_t st) {
   const dim3 grid((N + GN - 1) / GN, (M + GM - 1) / GM, heads);
   k_head_gemm<TRANS_B><<<grid, 256, 0, st>>>(M, N, K, A, lda, a_hs, B, ldb, b_hs, C, ldc, c_hs);
   return kvcu_check_cuda(cudaGetLastError(), "head gemm launch");
+}
+
+// The per-head GEMM of the step: the tensor-core 3xTF32 kernel when the shapes
+// fit its tiles (the model's: N = 512 or 128, K = 128 or 512), else the
+// CUDA-core f32 kernel.
+template <bool TRANS_B>
+int launch_head_gemm(uint32_t heads, uint32_t M, uint32_t N, uint32_t K, const float* A, uint32_t lda,
+                     uint64_t a_hs, const float* B, uint32_t ldb, uint64_t b_hs, float* C, uint32_t ldc,
+                     uint64_t c_hs, uint32_t* status, cudaStream_t st) {
+  const int rc =
+      kvcu_launch_head_gemm_tc(TRANS_B, heads, M, N, K, A, lda, a_hs, B, ldb, b_hs, C, ldc, c_hs, status, st);
+  if (rc != KVCU_ERR_UNSUPPORTED) return rc;
+  return launch_head_gemm_cc<TRANS_B>(heads, M, N, K, A, lda, a_hs, B, ldb, b_hs, C, ldc, c_hs, st);
 }
 
 // One CTA per (entry, head): the newest token's score with the unquantized
@@ -274,7 +287,7 @@ extern "C" int kvcu_mla_prepare(kvcu_pool* pool, uint32_t n, uint32_t n_heads, u
   if (rc) return rc;
   // q_abs[b][h][0:R] = q_nope[b][h] (n x qk_nope) x k_b_h (qk_nope x R)
   return launch_head_gemm<false>(n_heads, n, R, qk_nope, q, n_heads * (qk_nope + P), qk_nope + P, k_b, R,
-                                 (uint64_t)qk_nope * R, q_abs, n_heads * (R + P), R + P, st);
+                                 (uint64_t)qk_nope * R, q_abs, n_heads * (R + P), R + P, pool->status, st);
 }
 
 extern "C" int kvcu_mla_finish(kvcu_pool* pool, uint32_t n, uint32_t n_heads, uint32_t v_dim,
@@ -296,5 +309,30 @@ extern "C" int kvcu_mla_finish(kvcu_pool* pool, uint32_t n, uint32_t n_heads, ui
   if (rc) return rc;
   // attn[b][h][j] = latent[b][h] (n x R) x v_b_h^T, v_b_h = v_b[h*v_dim .. +v_dim][0:R]
   return launch_head_gemm<true>(n_heads, n, v_dim, R, latent, n_heads * R, R, v_b, R, (uint64_t)v_dim * R,
-                                attn, n_heads * v_dim, v_dim, st);
+                                attn, n_heads * v_dim, v_dim, pool->status, st);
+}
+
+// Per-head batched GEMM entry point (the step's two contractions, exposed so a
+// caller, or a test, can run either kernel): impl 0 = the tensor-core 3xTF32
+// kernel where the shapes fit it, else CUDA cores; 1 = CUDA cores; 2 = tensor
+// cores or KVCU_ERR_UNSUPPORTED.
+extern "C" int kvcu_head_gemm(int trans_b, uint32_t heads, uint32_t M, uint32_t N, uint32_t K, const float* A,
+                              uint32_t lda, uint64_t a_hs, const float* B, uint32_t ldb, uint64_t b_hs, float* C,
+                              uint32_t ldc, uint64_t c_hs, int impl, kvcu_pool* pool, void* stream) {
+  if (!pool || !(pool->kv || pool->qs) || impl < 0 || impl > 2) return KVCU_ERR_INVALID_ARG;
+  if (M && heads && (!A || !B || !C)) return KVCU_ERR_INVALID_ARG;
+  DevScope d(pool->device);
+  if (d.rc) return d.rc;
+  const cudaStream_t st = (cudaStream_t)stream;
+  if (impl != 1) {
+    const int rc = kvcu_launch_head_gemm_tc(trans_b != 0, heads, M, N, K, A, lda, a_hs, B, ldb, b_hs, C, ldc, c_hs,
+                                            pool->status, st);
+    if (rc != KVCU_ERR_UNSUPPORTED || impl == 2) {
+      if (rc == KVCU_ERR_UNSUPPORTED)
+        kvcu_set_error("kvcu_head_gemm: the tensor-core kernel needs N %% 128 == 0, K %% 32 == 0 and 16-byte rows");
+      return rc;
+    }
+  }
+  return trans_b ? launch_head_gemm_cc<true>(heads, M, N, K, A, lda, a_hs, B, ldb, b_hs, C, ldc, c_hs, st)
+                 : launch_head_gemm_cc<false>(heads, M, N, K, A, lda, a_hs, B, ldb, b_hs, C, ldc, c_hs, st);
 }

@@ -110,10 +110,11 @@ __device__ __forceinline__ int8_t q8_value(float x, float d) {
   return (int8_t)(int)r;
 }
 
-// q8_value through a multiply: t = x * inv with inv = RN(1/d) lies within
-// |x/d| * 2^-22 <= 3.1e-5 of RN(x/d) for |x/d| <= 128, so both round to the
-// same integer unless t is within 1e-4 of a half-integer; there (and for NaN /
-// inf) the IEEE quotient decides.  Away from half-integers, round-half-even
+// q8_value through a multiply: for any inv within 2^-22 (relative) of 1/d,
+// t = x * inv lies within |x/d| * 2^-21 <= 6.1e-5 of RN(x/d) for |x/d| <= 128,
+// so both round to the same integer unless t is within 1e-4 of a
+// half-integer; there (and for NaN / inf, e.g. from a reciprocal that
+// overflowed) the IEEE quotient decides.  Away from half-integers, round-half-even
 // (rintf) and the reference's round-half-away agree.  For |x| <= amax of its
 // block (d = RN(amax/127)), |t| <= 127 * (1 + 3 * 2^-24), so the result needs
 // no clamp.  Same results as q8_value for such x.
@@ -122,6 +123,14 @@ __device__ __forceinline__ int8_t q8_value_fast(float x, float d, float inv) {
   const float r = rintf(t);
   if (!(fabsf(t - r) < 0.4999f)) return q8_value(x, d);
   return (int8_t)(int)r;
+}
+
+// Hardware approximate reciprocal (PTX rcp.approx.f32: at most 1 ulp of error,
+// subnormal inputs kept), accurate enough for q8_value_fast's `inv`.
+__device__ __forceinline__ float rcp_approx(float x) {
+  float r;
+  asm("rcp.approx.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
 }
 
 // Block scale from the block's max |x| (NaN-free max): d = amax/127 or 0.

@@ -82,7 +82,11 @@ _SIGS = {
     "kvcu_mla_prepare": (_i32, [_vp, _u32, _u32, _u32, _vp, _vp, _vp, _vp, _f32, _f32, _vp, _vp, _vp, _vp]),
     "kvcu_mla_finish": (_i32, [_vp, _u32, _u32, _u32, _vp, _vp, _vp, _vp, _f32, _vp, _vp, _vp]),
     "kvcu_decode_last_launches": (_u32, [_vp]),
+    "kvcu_head_gemm": (_i32, [_i32, _u32, _u32, _u32, _u32, _vp, _u32, _u64, _vp, _u32, _u64, _vp, _u32, _u64, _i32,
+                              _vp, _vp]),
     "kvcu_decode_ws_set_impl": (_i32, [_vp, _i32]),
+    "kvcu_decode_ws_set_wait_limit": (_i32, [_vp, _u64]),
+    "kvcu_decode_ws_test_withhold": (_i32, [_vp, _u32]),
     "kvcu_decode_last_impl": (_i32, [_vp]),
     "kvcu_mla_decode_noalloc": (_i32, [_vp, _u32, _u32, _vp, _u32, _vp, _vp, _vp, _vp, _u32, _f32, _vp, _vp]),
     "kvcu_pool_read_checkpoint": (_i32, [_vp, _u64, _u64, _vp, _vp]),
@@ -362,6 +366,13 @@ class DecodeWorkspace:
 
     def set_impl(self, impl):
         check(lib().kvcu_decode_ws_set_impl(self._h, impl), "kvcu_decode_ws_set_impl")
+
+    def set_wait_limit(self, cycles):
+        check(lib().kvcu_decode_ws_set_wait_limit(self._h, cycles), "kvcu_decode_ws_set_wait_limit")
+
+    def test_withhold(self, tile):
+        """Test hook: withhold the first slice of tile `tile` of every CTA (0xFFFFFFFF: off)."""
+        check(lib().kvcu_decode_ws_test_withhold(self._h, tile), "kvcu_decode_ws_test_withhold")
 
     @property
     def last_impl(self):

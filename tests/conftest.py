@@ -19,6 +19,18 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA GPU (B200); runs the product kernels")
 
 
+def pytest_terminal_summary(terminalreporter):
+    """The worst max-relative attention error (per (sequence, head) row, against
+    the oracle or another kernel path) seen by any test of this session."""
+    try:
+        import kvdata
+    except ImportError:
+        return
+    if kvdata.WORST["where"]:
+        terminalreporter.write_line(f"worst attention error this run: {kvdata.WORST['err']:.3e} "
+                                    f"({kvdata.WORST['where']}; tolerance {kvdata.REL_TOL:g})")
+
+
 @pytest.fixture(scope="session")
 def oracle():
     import kvoracle
