@@ -377,6 +377,47 @@ def measure_config4(kvcu, torch, dev, local_rank, peak, steps=10, warmup=3):
 PREFILL_LEN = 4096
 
 
+def measure_config3(kvcu, torch, dev, local_rank, peak, reps=20):
+    """MLA decode over an f32 paged cache, 16 sequences with
+    context lengths uniform in [1, 4096], block size 16, 20 heads, one layer
+    (the CUDA-core kernel; f32 pools have no tensor-core path).  2,304 B per
+    context token; the 75 MB of KV fit in L2, so this is a latency-sized case."""
+    lens = np.random.default_rng(3).integers(1, 4097, 16).astype(np.int64)
+    n = lens.size
+    nb = int(sum((int(L) + 15) // 16 for L in lens)) + 4
+    c = kvcu.KVCache.with_blocks(1, R, P, nb, 16, quantized=False, device=local_rank)
+    for _ in range(n - 1):
+        c.seq_create()
+    ids = np.arange(n, dtype=np.uint32)
+    for i in range(n):
+        c.seq_ensure_capacity(i, int(lens[i]))
+    c.prefill_synthetic(0, ids, lens, 3, 0.0)
+    st = torch.cuda.Stream(device=dev)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(st):
+        q = torch.randn((n, H, W), device=dev, generator=torch.Generator(device=dev).manual_seed(3))
+        out = torch.empty((n, H, R), device=dev)
+    st.synchronize()
+    c.mlaDecode_dev(0, ids, q, SCALE, out, st)  # plan + warm-up
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(reps):
+        c.mlaDecode_dev(0, ids, q, SCALE, out, st)
+    e1.record(st)
+    st.synchronize()
+    status = c.pool().status()
+    c.close()
+    if status:
+        raise RuntimeError(f"config 3 hit device status {status:#x}")
+    secs = e0.elapsed_time(e1) / 1e3 / reps
+    ctx = int(lens.sum())
+    gbs = (ctx * 2304 + n * H * (W + R) * 4) / secs / 1e9
+    return {"workload": "config3_f32_decode", "n_seqs": n, "ctx_tokens": ctx, "ms_per_decode": secs * 1e3,
+            "ctx_tokens_per_s": ctx / secs, "GB/s": gbs, "frac": gbs / peak,
+            "kernel": "k_decode (CUDA cores, f32 pool) + k_combine",
+            "note": "the KV (75 MB) is smaller than L2: a latency-sized case"}
+
+
 def measure_prefill(kvcu, torch, dev, local_rank, reps=5):
     """mlaAttentionBatch over a 4,096-token prompt of one sequence (one layer,
     Q8_0, block size 64, 20 heads): the prompt's rows are appended, then every
@@ -761,6 +802,7 @@ def run_ours(args, rank, world, local_rank):
     peak, peak_kind = read_peaks()
     c4 = None if args.no_config4 else measure_config4(kvcu, torch, dev, local_rank, peak)
     prefill = measure_prefill(kvcu, torch, dev, local_rank)
+    c3 = measure_config3(kvcu, torch, dev, local_rank, peak)
     def serve_decode():
         # one decode step of every layer (reads only, so the pool stays as saved), finished
         cache.mlaDecodeLayers_dev(0, ids, qs, SCALE, outs, st)
@@ -833,6 +875,7 @@ def run_ours(args, rank, world, local_rank):
             "prefill_s": t_pre,
             "multi_gpu_check": mg_check,
             "prefill": prefill,
+            "config3": c3,
         }
         if c4 is not None:
             line["config4"] = c4
