@@ -11,7 +11,8 @@
 //
 // One CTA per (128-row M tile, NT-column N tile, head), 256 threads: all
 // threads stage each 32-deep K slice of A and B into shared memory (split into
-// hi / lo, 128B-swizzled K-major layout, two stages), one elected thread issues
+// hi / lo, 128B-swizzled K-major layout, two stages; the next slice's global
+// loads are in flight meanwhile), one elected thread issues
 // 4 K-steps x 3 tcgen05.mma.kind::tf32 (M = 128, N = NT, K = 8) per slice, and
 // the accumulator (128 lanes x NT f32 columns of TMEM) is read back by the 8
 // warps at the end.  Every wait is bounded; a timeout sets the pool's status
@@ -117,6 +118,29 @@ __global__ void __launch_bounds__(NTHR, 1) k_head_gemm_tc(GemmArgs g) {
   constexpr uint32_t IDESC = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(NT >> 3) << 17) |
                              ((uint32_t)(TM >> 4) << 24);
   const uint32_t nk = g.K / TK;
+  // The next K slice is read from global memory into registers while the
+  // current one is stored, synchronised and multiplied.
+  constexpr int NA = TM * 8 / NTHR, NB = NT * 8 / NTHR;
+  float4 pa[NA], pb[NB];
+  auto load_slice = [&](uint32_t c) {
+    const uint32_t k0 = c * TK;
+#pragma unroll
+    for (int i = 0; i < NA; ++i) {
+      const uint32_t e = tid + NTHR * i, r = e >> 3, ch = e & 7u;
+      pa[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (m0 + r < g.M) pa[i] = __ldg(reinterpret_cast<const float4*>(A + (uint64_t)(m0 + r) * g.lda + k0 + 4 * ch));
+    }
+#pragma unroll
+    for (int i = 0; i < NB; ++i) {
+      const uint32_t e = tid + NTHR * i;
+      if (TRANS_B)  // B(k, n) = B[n * ldb + k]: rows n, K contiguous, like A
+        pb[i] = __ldg(reinterpret_cast<const float4*>(B + (uint64_t)(n0 + (e >> 3)) * g.ldb + k0 + 4 * (e & 7u)));
+      else  // B(k, n) = B[k * ldb + n]: 4 consecutive n of one k
+        pb[i] = __ldg(reinterpret_cast<const float4*>(B + (uint64_t)(k0 + e / (NT / 4)) * g.ldb + n0 +
+                                                      4 * (e % (NT / 4))));
+    }
+  };
+  load_slice(0);
   bool ok = true;
   for (uint32_t c = 0; c < nk && ok; ++c) {
     const uint32_t s = c % STAGES;
@@ -127,30 +151,20 @@ __global__ void __launch_bounds__(NTHR, 1) k_head_gemm_tc(GemmArgs g) {
     }
     uint8_t* st = smem + s * L::STAGE;
     uint8_t *a_hi = st, *a_lo = st + L::A_BYTES, *b_hi = st + 2 * L::A_BYTES, *b_lo = b_hi + L::B_BYTES;
-    const uint32_t k0 = c * TK;
-    // A: 128 rows x 8 chunks of 4 floats
 #pragma unroll
-    for (int i = 0; i < TM * 8 / NTHR; ++i) {
-      const uint32_t e = tid + NTHR * i, r = e >> 3, ch = e & 7u;
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (m0 + r < g.M) v = __ldg(reinterpret_cast<const float4*>(A + (uint64_t)(m0 + r) * g.lda + k0 + 4 * ch));
-      put4(a_hi, a_lo, r, ch, v);
+    for (int i = 0; i < NA; ++i) {
+      const uint32_t e = tid + NTHR * i;
+      put4(a_hi, a_lo, e >> 3, e & 7u, pa[i]);
     }
-    if (TRANS_B) {
-      // B(k, n) = B[n * ldb + k]: rows n, K contiguous, like A
 #pragma unroll
-      for (int i = 0; i < NT * 8 / NTHR; ++i) {
-        const uint32_t e = tid + NTHR * i, r = e >> 3, ch = e & 7u;
-        const float4 v = __ldg(reinterpret_cast<const float4*>(B + (uint64_t)(n0 + r) * g.ldb + k0 + 4 * ch));
-        put4(b_hi, b_lo, r, ch, v);
-      }
-    } else {
-      // B(k, n) = B[k * ldb + n]: 4 consecutive n of one k go to 4 rows
-#pragma unroll
-      for (int i = 0; i < NT * 8 / NTHR; ++i) {
-        const uint32_t e = tid + NTHR * i, kk = e / (NT / 4), n4 = e % (NT / 4);
-        const float4 v = __ldg(reinterpret_cast<const float4*>(B + (uint64_t)(k0 + kk) * g.ldb + n0 + 4 * n4));
-        const float x[4] = {v.x, v.y, v.z, v.w};
+    for (int i = 0; i < NB; ++i) {
+      const uint32_t e = tid + NTHR * i;
+      if (TRANS_B) {
+        put4(b_hi, b_lo, e >> 3, e & 7u, pb[i]);
+      } else {
+        // 4 consecutive n of one k go to 4 rows
+        const uint32_t kk = e / (NT / 4), n4 = e % (NT / 4);
+        const float x[4] = {pb[i].x, pb[i].y, pb[i].z, pb[i].w};
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const uint32_t off = sw128_off(4 * n4 + j, 4 * kk);
@@ -160,6 +174,7 @@ __global__ void __launch_bounds__(NTHR, 1) k_head_gemm_tc(GemmArgs g) {
         }
       }
     }
+    if (c + 1 < nk) load_slice(c + 1);
     fence_proxy_async();  // the generic-proxy stores, seen by the tensor cores
     __syncthreads();
     if (warp == 0) {
@@ -249,6 +264,11 @@ int kvcu_launch_head_gemm_tc(bool trans_b, uint32_t heads, uint32_t M, uint32_t 
       !aligned16(A) || !aligned16(B) || !aligned16(C) || !status)
     return KVCU_ERR_UNSUPPORTED;
   GemmArgs g{M, N, K, A, lda, a_hs, B, ldb, b_hs, C, ldc, c_hs, status};
-  if (N % 256 == 0) return trans_b ? launch<256, true>(g, heads, st) : launch<256, false>(g, heads, st);
+  // one CTA per SM (shared memory): pick the N tile whose waves of CTAs cover
+  // the fewest columns per SM
+  const uint64_t sms = (uint64_t)kvcu_current_sm_count(), mt = (M + TM - 1) / TM;
+  const uint64_t waves256 = (N / 256 * mt * heads + sms - 1) / sms, waves128 = (N / 128 * mt * heads + sms - 1) / sms;
+  if (N % 256 == 0 && waves256 * 256 <= waves128 * 128)
+    return trans_b ? launch<256, true>(g, heads, st) : launch<256, false>(g, heads, st);
   return trans_b ? launch<128, true>(g, heads, st) : launch<128, false>(g, heads, st);
 }

@@ -286,12 +286,28 @@ __global__ void __launch_bounds__(256) k_append_q8(PoolArgs a, uint32_t n_rows, 
       amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
       amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
       const float d = kvcu::q8_scale(amax);
+      // round(x/d) through a multiply (q8_value_fast's argument) for all 8
+      // values without a branch each; if any lane of the warp met a value near a
+      // half-integer (or a NaN / inf), the whole warp redoes its values with the
+      // IEEE quotient (rare), so the common path has no divergence
+      const float inv = d > 0.0f ? kvcu::rcp_approx(d) : 0.0f;
+      int qv[8];
+      bool near_tie = false;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float t = v[i] * inv;
+        const float r = rintf(t);
+        near_tie |= !(fabsf(t - r) < 0.4999f);
+        qv[i] = (int)r;
+      }
+      if (__any_sync(0xffffffffu, near_tie && d > 0.0f)) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) qv[i] = d > 0.0f ? kvcu::q8_value(v[i], d) : 0;
+      }
       uint32_t w[2] = {0u, 0u};
       if (d > 0.0f) {
-        const float inv = kvcu::rcp_approx(d);
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-          w[i >> 2] |= (uint32_t)(uint8_t)kvcu::q8_value_fast(v[i], d, inv) << (8 * (i & 3));
+        for (int i = 0; i < 8; ++i) w[i >> 2] |= (uint32_t)(uint8_t)(int8_t)qv[i] << (8 * (i & 3));
       }
       if (b < nblk) {
         *reinterpret_cast<uint2*>(qrow + 32u * b + 8u * sub) = make_uint2(w[0], w[1]);
