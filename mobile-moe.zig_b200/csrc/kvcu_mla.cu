@@ -21,9 +21,10 @@
 //                     (unquantized c, k_pe as the cache holds it), then v_b
 //                     k_mla_merge + k_head_gemm
 // The two per-head products are small f32 GEMMs (k_b: n x qk_nope x R, v_b:
-// n x R x v_dim per head) kept on the CUDA cores in f32: at a 512-sequence
-// batch they are ~1.3 GFLOP each, a few percent of the decode, and f32 keeps
-// them as exact as the reference's matVecMul.
+// n x R x v_dim per head), ~1.3 GFLOP each at a 512-sequence batch. They run
+// on the tensor cores as 3xTF32 (k_head_gemm_tc, f32-level error) where the
+// shapes allow, else on the CUDA cores in f32, as exact as the reference's
+// matVecMul.
 #include <cuda_runtime.h>
 #include <math.h>
 
