@@ -236,6 +236,22 @@ __device__ __forceinline__ void bulk_load_hint(uint32_t dst, const void* src, ui
       "l"(src), "r"(bytes), "r"(bar), "l"(policy)
       : "memory");
 }
+// L2 prefetches of the same boxes (no shared memory, no barrier)
+__device__ __forceinline__ void tma_prefetch_4d(const CUtensorMap* map, int x, int y, int z, int w) {
+  asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(z), "r"(w)
+               : "memory");
+}
+__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* map, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_prefetch(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
 // L2 policy for data read once (the KV stream): evicted first, so that what is
 // reused (queries, partials, block tables) stays
 __device__ __forceinline__ uint64_t policy_evict_first() {
@@ -397,6 +413,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       bool live = true;
       const uint64_t once = policy_evict_first();
       const uint32_t br = a.box_rows;
+      // The rows of tile k of an item go to L2 (no shared memory, no barrier),
+      // so that its copy, issued once the converter hands a slot back, reads L2.
+      auto prefetch_tile = [&](const Item& pi, uint64_t player, uint32_t pk) {
+        const uint32_t p0 = pi.tok0 + pk * TILE, p1 = min(p0 + TILE, pi.tok1);
+        for (uint32_t pos = p0; pos < p1; pos += br) {
+          const uint32_t blk = a.tables[pi.t0 + pos / a.block_size];
+          if (blk >= a.num_blocks || pos % a.block_size + br > a.block_size) continue;
+          const uint64_t row = (player * a.num_blocks + blk) * a.block_size + pos % a.block_size;
+          tma_prefetch_4d(&map_lat, 0, 0, 0, (int)(row >> 3));
+          tma_prefetch_2d(&map_rope, 512, (int)row);
+          bulk_prefetch(a.sc + row * NBLK, br * 36u);
+        }
+      };
       for (uint32_t u = 0; u < n_units && live; ++u) {
         const Unit un = unit_of(u, it_begin, cnt);
         const Item im = load_item(a, un.it);
@@ -405,6 +434,20 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           const uint32_t s = g & 1u;
           const uint32_t tt0 = im.tok0 + k * TILE;
           const uint32_t tt1 = min(tt0 + TILE, im.tok1);
+          // one tile ahead: the next tile of this item, or the first of the
+          // next non-empty unit (looking a few units ahead)
+          if (k + 1 < im.ntiles) {
+            prefetch_tile(im, layer, k + 1);
+          } else {
+            for (uint32_t u2 = u + 1; u2 < n_units && u2 < u + 4; ++u2) {
+              const Unit un2 = unit_of(u2, it_begin, cnt);
+              const Item im2 = load_item(a, un2.it);
+              if (im2.ntiles) {
+                prefetch_tile(im2, (uint64_t)a.layer + un2.li, 0);
+                break;
+              }
+            }
+          }
           const uint32_t stage = sbase + s * STAGE_BYTES;
           const uint32_t full = bar(B_KV_FULL + s);
           bool started = false;
@@ -817,7 +860,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           for (int h = 0; h < HH; ++h)
             if ((flagged >> h) & 1u) mref[h] = tmax[h];
         }
-        // ---- P (f16) -> shared memory, K-major 128B-swizzled [head][token]
+        // ---- P (f16) -> shared memory, K-major 128B-swizzled [head][token];
+        // the values are formed before the wait for the buffer (the previous
+        // tile's PV)
+        __half ph[HH];
+#pragma unroll
+        for (int h = 0; h < HH; ++h) ph[h] = __float2half_rn(sc[h] == -INFINITY ? 0.f : exp2f(sc[h] - mref[h]));
         if (!mbar_wait(bar(B_P_EMPTY), (g & 1u) ^ 1u, abort_flag, a.status)) {
           ok = false;
           break;
@@ -826,10 +874,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           uint8_t* pb = smem + OFF_P + (trow >> 6) * 4096u;
           const uint32_t tb = (trow & 63u) * 2u;
 #pragma unroll
-          for (int h = 0; h < HH; ++h) {
-            const float p = sc[h] == -INFINITY ? 0.f : exp2f(sc[h] - mref[h]);
-            *reinterpret_cast<__half*>(pb + sw128_off(16u * hf + (uint32_t)h, tb)) = __float2half_rn(p);
-          }
+          for (int h = 0; h < HH; ++h) *reinterpret_cast<__half*>(pb + sw128_off(16u * hf + (uint32_t)h, tb)) = ph[h];
         }
         fence_proxy_async();
         __syncwarp();
