@@ -20,7 +20,7 @@
 //   warps 4-11  epilogue (two halves of the heads, each over all 128 token
 //               rows): combine the 18 per-block dot products with the block
 //               scales, online softmax over the tile (lazy rescale of O / l in
-//               TMEM only when a head's max grows by > 2^8), P (f16) -> shared
+//               TMEM only when a head's max grows by > 2^14), P (f16) -> shared
 //               memory; at item end O / l -> output (or the split partial).
 //   warps 12-15 converter: V = f16(d * q) for the tile's 512 latent columns in
 //               16 KB chunks through a 2-deep ring, in the MN-major f16 layout.
@@ -65,7 +65,7 @@ constexpr uint32_t VU_BYTES = 4096;  // one V unit: 16 tokens x 128 columns (one
 constexpr uint32_t VCH_BYTES = 4 * VU_BYTES;  // one V chunk: 16 tokens x 512 columns
 constexpr int NTHREADS = 512;        // 4 warpgroups: issue, epilogue x2, converter
 constexpr int EPI_WARPS = 8;
-constexpr float RESCALE_LOG2 = 8.0f;         // lazy rescale threshold (factor 256)
+constexpr float RESCALE_LOG2 = 14.0f;        // lazy rescale threshold (factor 16384; P stays < f16 max)
 constexpr uint32_t STATUS_TIMEOUT = KVCU_STATUS_TIMEOUT;
 
 // ---- shared memory map (offsets from a 1024-aligned base) ----
@@ -798,7 +798,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           sc[2 * p + 1] = (valid && h0 + 2 * p + 1 < H && vy == vy) ? vy : -INFINITY;
         }
         // lazy rescale: a head's reference max moves only when some score of
-        // the tile exceeds it by more than 2^8 (so P <= 256 otherwise).  Each
+        // the tile exceeds it by more than 2^14 (so P <= 16384 otherwise, inside f16).  Each
         // warp votes per head; the half combines the 4 votes after one sync.
         uint32_t bits = 0;
 #pragma unroll

@@ -379,23 +379,37 @@ def test_decode_tensor_core_vs_cuda_core_same_data(kv, oracle):
 
 
 def test_decode_lazy_rescale_when_scores_jump(kv, oracle):
-    """Late tokens with much larger scores force the tensor-core kernel to
-    rescale the TMEM accumulators (max grows by far more than 2^8)."""
-    L, bs = 3000, 64
-    c = kv.KVCache.with_blocks(1, R, P, (L + bs - 1) // bs + 1, bs, quantized=True)
-    o = oracle.Pool(1, (L + bs - 1) // bs + 1, bs, R, P, True)
-    c.ensureCapacity(L)
-    rows = gen_seq_rows(oracle, 91, 0, 0, L, 0.0)
-    rows[1500:] *= np.float32(4.0)
-    rows[2900:] *= np.float32(3.0)
-    c.appendBatch(0, np.zeros(L, np.uint32), np.arange(L, dtype=np.uint32), rows)
-    tab = np.array(c.block_table, np.uint32)
+    """Scores that double from one 128-token tile to the next (a sawtooth of 4
+    tiles, gains 1, 2, 4, 8) inside items of several tiles: the tensor-core
+    kernel must rescale its TMEM accumulators whenever a head's max grows by
+    more than 2^14 (here from the third tile of a run on, ~27 -> ~54 in log2
+    units).  The batch (8 x 12,800 tokens, ~5 tiles per CTA) makes the plan give
+    every CTA multi-tile items, so most CTAs cross a doubling inside an item.
+    (The gains stop at 8: the query's two-digit encoding has an error relative
+    to |q|, so the score error grows with |k|; at gains of 128, scores near
+    1,000 log2 units, it reaches ~0.02 and the output error 6e-3.)"""
+    n, L, bs = 8, 12800, 64
+    nbs = (L + bs - 1) // bs
+    c = kv.KVCache.with_blocks(1, R, P, n * nbs + 1, bs, quantized=True)
+    o = oracle.Pool(1, n * nbs + 1, bs, R, P, True)
+    for _ in range(n - 1):
+        c.seq_create()
     t = np.arange(L)
-    o.put_rows(0, tab[t // bs], t % bs, rows)
-    q = np.random.default_rng(92).standard_normal((1, 20, W)).astype(np.float32)
-    got = c.mlaDecode(0, q, np.zeros(1, np.uint32), SCALE)
+    gain = np.float32(2.0) ** ((t // 128) % 4).astype(np.float32)
+    offs, tabs = [0], []
+    for s in range(n):
+        c.seq_ensure_capacity(s, L)
+        rows = gen_seq_rows(oracle, 91 + s, 0, s, L, 0.0) * gain[:, None]
+        c.appendBatch(0, np.full(L, s, np.uint32), t.astype(np.uint32), rows)
+        tab = np.array(c.seq_block_table(s), np.uint32)
+        o.put_rows(0, tab[t // bs], t % bs, rows)
+        tabs.extend(tab.tolist())
+        offs.append(len(tabs))
+    q = np.random.default_rng(92).standard_normal((n, 20, W)).astype(np.float32)
+    got = c.mlaDecode(0, q, np.arange(n, dtype=np.uint32), SCALE)
     assert c.last_decode_impl == kv.DECODE_TENSOR_CORE
-    want = o.attention(0, tab, L, q[0], SCALE)[None]
+    want = o.attention_batch(0, np.array(offs, np.uint32), np.array(tabs, np.uint32),
+                             np.full(n, L, np.uint32), q, SCALE, n_threads=8)
     assert rel_err_rows(got, want) <= REL_TOL
 
 
