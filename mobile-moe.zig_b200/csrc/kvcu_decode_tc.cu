@@ -188,7 +188,7 @@ __device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, vo
 // Per-warpgroup register budgets (setmaxnreg).  The block launches with 128
 // registers per thread (checked on the host before the first launch); the
 // split below never asks for more than that total, so every .inc completes.
-constexpr uint32_t LAUNCH_REGS = 128, ISSUE_REGS = 64, EPI_REGS = 176, CVT_REGS = 88;
+constexpr uint32_t LAUNCH_REGS = 128, ISSUE_REGS = 56, EPI_REGS = 184, CVT_REGS = 88;
 static_assert(128 * ISSUE_REGS + 256 * EPI_REGS + 128 * CVT_REGS <= NTHREADS * LAUNCH_REGS,
               "register split exceeds the launch allocation");
 template <uint32_t N>
@@ -742,49 +742,87 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         // Three Q8_0 blocks per TMEM round trip (18 blocks -> 6 groups); this
         // half reads its 2HH digit columns of each slot, per head pair
         // [digit0 h, digit0 h+1, digit1 h, digit1 h+1].
-        for (uint32_t gi = 0; gi < (uint32_t)NGRP; ++gi) {
+        // Software-pipelined over groups: the TMEM loads of group gi+1 are in
+        // flight while group gi is combined (two register sets, a and b).
+        uint32_t ra[3][2 * HH], rb[3][2 * HH];
+        auto grp_issue = [&](uint32_t gi, uint32_t(&r)[3][2 * HH]) -> bool {
           const uint32_t kk = g * NGRP + gi, slot = kk % QK_GROUPS;
-          if (!mbar_wait(bar(B_QK_FULL + slot), (kk / QK_GROUPS) & 1u, abort_flag, a.status)) {
-            ok = false;
-            break;
-          }
+          if (!mbar_wait(bar(B_QK_FULL + slot), (kk / QK_GROUPS) & 1u, abort_flag, a.status)) return false;
           tc_fence_after();
-          uint32_t r0[2 * HH], r1[2 * HH], r2[2 * HH];
           const uint32_t ta = tmem + lane_addr + GB * slot * NQ + hf * Cfg<HK>::NQH;
-          tmem_ld<2 * HH>(ta, r0);
-          tmem_ld<2 * HH>(ta + NQ, r1);
-          tmem_ld<2 * HH>(ta + 2 * NQ, r2);
+          tmem_ld<2 * HH>(ta, r[0]);
+          tmem_ld<2 * HH>(ta + NQ, r[1]);
+          tmem_ld<2 * HH>(ta + 2 * NQ, r[2]);
+          return true;
+        };
+        // the values are in registers: the slot can take the next group's MMAs now
+        auto grp_land = [&](uint32_t gi, uint32_t(&r)[3][2 * HH]) {
           tmem_wait_ld();
-          reg_fence(r0);
-          reg_fence(r1);
-          reg_fence(r2);
-          // the values are in registers: the slot can take the next group's MMAs now
+          reg_fence(r[0]);
+          reg_fence(r[1]);
+          reg_fence(r[2]);
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(bar(B_QK_EMPTY + slot));
+          if (lane == 0) mbar_arrive(bar(B_QK_EMPTY + (g * NGRP + gi) % QK_GROUPS));
+        };
+        // Per head: 256 x0 + x1 exactly in int32 (|x0| <= 32 * 127^2 < 2^19),
+        // one rounding to f32, then the block scale, two heads per packed
+        // f32x2 FMA (each lane is one fused multiply-add, as fmaf). Head pair p
+        // has digit-0 columns 4p, 4p+1 and digit-1 columns 4p+2, 4p+3.  (An
+        // exact conversion by the 1.5 * 2^23 bias, avoiding the int->float
+        // unit, measured 8% slower: it needs more instructions per value.)
+        auto grp_math = [&](uint32_t gi, const uint32_t(&r)[3][2 * HH]) {
           const float d0 = __half2float(__ushort_as_half(scrow[GB * gi]));
           const float d1 = __half2float(__ushort_as_half(scrow[GB * gi + 1]));
           const float d2 = __half2float(__ushort_as_half(scrow[GB * gi + 2]));
-          // Per head: 256 x0 + x1 exactly in int32 (|x0| <= 32 * 127^2 < 2^19),
-          // one rounding to f32, then the block scale, two heads per packed
-          // f32x2 FMA (each lane is one fused multiply-add, as fmaf). Head pair p
-          // has digit-0 columns 4p, 4p+1 and digit-1 columns 4p+2, 4p+3.  (An
-          // exact conversion by the 1.5 * 2^23 bias, avoiding the int->float
-          // unit, measured 8% slower: it needs more instructions per value.)
           const float2 dd0 = make_float2(d0, d0), dd1 = make_float2(d1, d1), dd2 = make_float2(d2, d2);
 #pragma unroll
           for (int p = 0; p < HH / 2; ++p) {
             const int c = 4 * p;
-            const float2 f0 = make_float2(__int2float_rn((int)r0[c] * 256 + (int)r0[c + 2]),
-                                          __int2float_rn((int)r0[c + 1] * 256 + (int)r0[c + 3]));
-            const float2 f1 = make_float2(__int2float_rn((int)r1[c] * 256 + (int)r1[c + 2]),
-                                          __int2float_rn((int)r1[c + 1] * 256 + (int)r1[c + 3]));
-            const float2 f2 = make_float2(__int2float_rn((int)r2[c] * 256 + (int)r2[c + 2]),
-                                          __int2float_rn((int)r2[c + 1] * 256 + (int)r2[c + 3]));
+            const float2 f0 = make_float2(__int2float_rn((int)r[0][c] * 256 + (int)r[0][c + 2]),
+                                          __int2float_rn((int)r[0][c + 1] * 256 + (int)r[0][c + 3]));
+            const float2 f1 = make_float2(__int2float_rn((int)r[1][c] * 256 + (int)r[1][c + 2]),
+                                          __int2float_rn((int)r[1][c + 1] * 256 + (int)r[1][c + 3]));
+            const float2 f2 = make_float2(__int2float_rn((int)r[2][c] * 256 + (int)r[2][c + 2]),
+                                          __int2float_rn((int)r[2][c + 1] * 256 + (int)r[2][c + 3]));
             acc2[p] = __ffma2_rn(dd0, f0, acc2[p]);
             acc2[p] = __ffma2_rn(dd1, f1, acc2[p]);
             acc2[p] = __ffma2_rn(dd2, f2, acc2[p]);
           }
+        };
+        static_assert(NGRP % 2 == 0, "groups are combined in pairs");
+        if constexpr (HH > 10) {
+          // 21-24 heads: the second register set does not fit, one group at a time
+          for (uint32_t gi = 0; gi < (uint32_t)NGRP && ok; ++gi) {
+            if (!grp_issue(gi, ra)) {
+              ok = false;
+              break;
+            }
+            grp_land(gi, ra);
+            grp_math(gi, ra);
+          }
+          if (!ok) break;
+        } else {
+        if (!grp_issue(0, ra)) {
+          ok = false;
+          break;
+        }
+        grp_land(0, ra);
+        for (uint32_t gp = 0; gp < (uint32_t)NGRP; gp += 2) {
+          if (!grp_issue(gp + 1, rb)) {
+            ok = false;
+            break;
+          }
+          grp_math(gp, ra);
+          grp_land(gp + 1, rb);
+          const bool more = gp + 2 < (uint32_t)NGRP;
+          if (more && !grp_issue(gp + 2, ra)) {
+            ok = false;
+            break;
+          }
+          grp_math(gp + 1, rb);
+          if (more) grp_land(gp + 2, ra);
+        }
         }
         if (!ok) break;
         // ---- online softmax over the tile (log2 domain)
