@@ -21,6 +21,7 @@ namespace {
 
 struct PoolArgs {
   uint32_t layer, num_blocks, block_size, kv_rank, rope_dim, nbk, nbp, nblk;
+  uint32_t bs_log2;  // log2(block_size) when it is a power of two, else 32
   float* kv;
   float* pe;
   int8_t* qs;
@@ -33,6 +34,9 @@ PoolArgs pool_args(kvcu_pool* p, uint32_t layer) {
   a.layer = layer;
   a.num_blocks = p->num_blocks;
   a.block_size = p->block_size;
+  a.bs_log2 = 32;
+  for (uint32_t k = 0; k < 32; ++k)
+    if ((1u << k) == p->block_size) a.bs_log2 = k;
   a.kv_rank = p->kv_rank;
   a.rope_dim = p->rope_dim;
   a.nbk = p->nbk;
@@ -66,7 +70,9 @@ __device__ __forceinline__ bool resolve_row(const PoolArgs& a, uint32_t s, uint3
     return false;
   }
   uint32_t t0 = toff[s], t1 = toff[s + 1];
-  uint32_t bi = pos / a.block_size;
+  // a shift and a mask for power-of-two block sizes (a uniform branch)
+  const uint32_t bi = a.bs_log2 < 32 ? pos >> a.bs_log2 : pos / a.block_size;
+  const uint32_t off = a.bs_log2 < 32 ? pos & (a.block_size - 1u) : pos % a.block_size;
   if (t1 < t0 || bi >= t1 - t0) {
     if (lane == 0) atomicOr(a.status, KVCU_STATUS_BAD_TABLE);
     return false;
@@ -76,7 +82,7 @@ __device__ __forceinline__ bool resolve_row(const PoolArgs& a, uint32_t s, uint3
     if (lane == 0) atomicOr(a.status, KVCU_STATUS_BAD_BLOCK);
     return false;
   }
-  *row = ((uint64_t)a.layer * a.num_blocks + blk) * a.block_size + pos % a.block_size;
+  *row = ((uint64_t)a.layer * a.num_blocks + blk) * a.block_size + off;
   return true;
 }
 
@@ -251,9 +257,16 @@ __global__ void __launch_bounds__(256) k_append_q8(PoolArgs a, uint32_t n_rows, 
   kvcu_pdl_wait();     // the previous kernel may still read the rows this one writes
   kvcu_pdl_trigger();  // a programmatically launched decode may start its prologue
   const uint64_t layer_rows = (uint64_t)a.num_blocks * a.block_size;
-  const uint64_t total = (uint64_t)n_rows * n_layers_call;
-  for (uint64_t ra = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; ra < total; ra += nwarps) {
-    const uint64_t li = ra / n_rows, r = ra - li * n_rows;
+  // (layer, row) pairs in layer-major order without a division per row: the
+  // warp's first pair, then steps of nwarps carried across layers
+  const uint32_t w0 = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, nw = (uint32_t)nwarps;
+  uint32_t li = w0 / n_rows, r = w0 - li * n_rows;
+  const uint32_t step_l = nw / n_rows, step_r = nw - step_l * n_rows;
+  for (; li < n_layers_call; li += step_l, r += step_r) {
+    if (r >= n_rows) {
+      r -= n_rows;
+      if (++li >= n_layers_call) break;
+    }
     const float* lat_r = latent + li * llat + r * ls;
     const float* rope_r = rope + li * lrope + r * ps;
     const uint32_t s = row_seq[r], pos = row_pos[r];
