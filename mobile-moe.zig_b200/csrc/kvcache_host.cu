@@ -226,6 +226,10 @@ struct kvcache {
   uint32_t* d_seq_ids = nullptr;
   size_t d_seq_ids_cap = 0;
   std::vector<uint32_t> plan_ids;
+  // the MLA step's plan (history lengths of its batch) is kept for the next
+  // layer of the same step: valid while no other plan ran on the workspace
+  std::vector<uint32_t> mla_plan_ids, mla_plan_hist;
+  uint64_t plan_serial = 0, mla_plan_serial = ~0ull;
   uint64_t plan_epoch = ~0ull, epoch = 0;
   uint64_t plan_tokens = 0;
   uint32_t last_launches = 0;
@@ -585,6 +589,7 @@ int ensure_ws(kvcache* c, uint32_t n, uint32_t n_heads, uint32_t n_layers = 1) {
   kvcu_decode_ws_set_impl(c->ws, c->decode_impl);
   c->plan_epoch = ~0ull;
   c->plan_ids.clear();
+  ++c->plan_serial;
   return KVCU_OK;
 }
 
@@ -622,6 +627,7 @@ int decode_impl(kvcache* c, uint32_t layer, uint32_t n, const uint32_t* seq_ids,
       c->plan_ids.assign(seq_ids, seq_ids + n);
     }
     rc = kvcu_decode_plan(c->ws, c->pool, n, c->d_seq_ids, (uint32_t)c->seqs.size(), c->d_lens, st);
+    ++c->plan_serial;
     if (rc) return rc;
     launches += 1;
     c->plan_epoch = c->epoch;
@@ -671,6 +677,7 @@ int attention_batch_impl(kvcache* c, uint32_t layer, uint32_t seq, uint32_t star
   const uint32_t n_seqs = (uint32_t)c->seqs.size();
   if (!rc)
     rc = kvcu_decode_plan_causal(c->ws, c->pool, n_pos, c->d_stepu, n_seqs, c->d_lens, c->d_stepu + n_pos, st);
+  ++c->plan_serial;
   c->plan_epoch = ~0ull;  // the cached decode plan no longer matches the workspace
   c->plan_ids.clear();
   if (!rc)
@@ -1186,8 +1193,18 @@ int kvcache_mla_step_dev(kvcache* c, uint32_t layer, uint32_t n, const uint32_t*
                      c->d_lens, st);
   if (rc) return rc;
   bump_lens(c, n, seq_ids, positions);  // the append kernel advanced d_lens identically
-  rc = kvcu_decode_plan(c->ws, c->pool, n, d_ids, n_seqs, d_hist, st);
-  c->plan_epoch = ~0ull;  // the cached decode plan no longer matches the workspace
+  // The plan depends only on the batch and its history lengths, which the
+  // layers of one step share: the first layer plans, the others reuse it.
+  const bool same_plan = c->mla_plan_serial == c->plan_serial && c->mla_plan_ids.size() == n &&
+                         std::equal(c->mla_plan_ids.begin(), c->mla_plan_ids.end(), seq_ids) &&
+                         std::equal(c->mla_plan_hist.begin(), c->mla_plan_hist.end(), positions);
+  if (!same_plan) {
+    rc = kvcu_decode_plan(c->ws, c->pool, n, d_ids, n_seqs, d_hist, st);
+    c->plan_epoch = ~0ull;  // the cached decode plan no longer matches the workspace
+    c->mla_plan_serial = rc ? ~0ull : ++c->plan_serial;
+    c->mla_plan_ids.assign(seq_ids, seq_ids + n);
+    c->mla_plan_hist.assign(positions, positions + n);
+  }
   if (!rc)
     rc = kvcu_mla_decode_lse(c->ws, c->pool, layer, n, d_ids, n_seqs, c->d_toff, c->d_tables, d_hist, q_abs,
                              n_heads, scale, latent, lse, st);
@@ -1196,7 +1213,7 @@ int kvcache_mla_step_dev(kvcache* c, uint32_t layer, uint32_t n, const uint32_t*
   // rows, gemm (prepare) + append + plan + decode + merge, gemm (finish). The
   // three host arrays above are pageable: each cudaMemcpyAsync returned only
   // after staging them, so they may go out of scope now.
-  c->last_launches = 2 + 1 + 1 + kvcu_decode_last_launches(c->ws) + 2;
+  c->last_launches = 2 + 1 + (same_plan ? 0 : 1) + kvcu_decode_last_launches(c->ws) + 2;
   return KVCU_OK;
 }
 

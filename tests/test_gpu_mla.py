@@ -111,3 +111,60 @@ def test_mla_step_rejects_repeated_sequence(kv):
     with pytest.raises(kv.KVCudaError):
         cache.mla_step_dev(0, [0, 0], [0, 1], z(2, H, QK_NOPE + P), z(2, R + P), z(R), EPS, BASE,
                            z(H * QK_NOPE, R), z(H * V_DIM, R), QK_NOPE, V_DIM, SCALE, z(2, H, V_DIM))
+
+
+@pytest.mark.parametrize("between", [False, True])
+def test_mla_step_layers_share_the_plan(kv, oracle, between):
+    """Two layers of one step with the same positions: the second layer reuses
+    the first layer's plan (one launch fewer), unless another decode planned on
+    the workspace in between. Both layers match the reference either way."""
+    import torch
+
+    import mla_ref
+
+    rng = np.random.default_rng(41)
+    hist = [0, 63, 300, 1500]
+    n, bs, layers = len(hist), 64, 2
+    cap = [L + 1 for L in hist]
+    nb = sum((c + bs - 1) // bs for c in cap) + 2
+    cache = kv.KVCache.with_blocks(layers, R, P, nb, bs, quantized=True)
+    for _ in range(n - 1):
+        cache.seq_create()
+    refs = []
+    for s, L in enumerate(hist):
+        cache.seq_ensure_capacity(s, cap[s])
+        oc = oracle.KVCache(layers, R, P, cap[s] + bs, bs)
+        oc.enableQuantization()
+        assert oc.ensureCapacity(cap[s]) == 0
+        for layer in range(layers):
+            if L:
+                rows = rng.standard_normal((L, R + P)).astype(np.float32)
+                cache.appendBatch(layer, np.full(L, s, np.uint32), np.arange(L, dtype=np.uint32), rows)
+                for p in range(L):
+                    assert oc.put(layer, p, rows[p, :R], rows[p, R:]) == 0
+        refs.append(oc)
+    dev = torch.device("cuda", 0)
+    t = lambda a: torch.from_numpy(a).to(dev)
+    ids = np.arange(n, dtype=np.uint32)
+    pos = np.array(hist, np.uint32)
+    w = (1.0 + 0.1 * rng.standard_normal(R)).astype(np.float32)
+    launches = []
+    for layer in range(layers):
+        q = rng.standard_normal((n, H, QK_NOPE + P)).astype(np.float32)
+        kv_a = rng.standard_normal((n, R + P)).astype(np.float32)
+        k_b = (rng.standard_normal((H * QK_NOPE, R)) / np.sqrt(R)).astype(np.float32)
+        v_b = (rng.standard_normal((H * V_DIM, R)) / np.sqrt(R)).astype(np.float32)
+        attn = torch.full((n, H, V_DIM), float("nan"), device=dev)
+        cache.mla_step_dev(layer, ids, pos, t(q), t(kv_a), t(w), EPS, BASE, t(k_b), t(v_b), QK_NOPE, V_DIM,
+                           SCALE, attn)
+        launches.append(cache.last_launches)
+        torch.cuda.synchronize()
+        assert cache.pool().status() == 0
+        got = attn.cpu().numpy()
+        want = np.stack([mla_ref.mla_attention(refs[b], layer, hist[b], q[b], kv_a[b], w, EPS, BASE, k_b, v_b,
+                                               QK_NOPE, P, V_DIM) for b in range(n)])
+        assert rel_err_rows(got, want) <= REL_TOL, layer
+        if between and layer == 0:
+            # a plain decode of layer 0 over the full lengths plans on the same workspace
+            cache.mlaDecode(0, rng.standard_normal((n, H, R + P)).astype(np.float32), ids, SCALE)
+    assert launches[1] == launches[0] - (0 if between else 1)
