@@ -1156,9 +1156,9 @@ int kvcache_mla_step_dev(kvcache* c, uint32_t layer, uint32_t n, const uint32_t*
   if (!rc) rc = cow_for_write(c, n, seq_ids, positions, st);
   if (rc) return rc;
   const uint32_t R = c->kv_rank, Wd = c->row_width(), n_seqs = (uint32_t)c->seqs.size();
-  // scratch: q_abs [n][H][W], rows [n][W], latent [n][H][R], lse [n][H]
+  // scratch: q_abs [n][H][W], rows [n][W], latent [n][H][R], lse [n][H], merge weights [n][H][3]
   const size_t q_abs_n = (size_t)n * n_heads * Wd, rows_n = (size_t)n * Wd, lat_n = (size_t)n * n_heads * R;
-  rc = ensure_dev(&c->d_step, &c->d_step_cap, q_abs_n + rows_n + lat_n + (size_t)n * n_heads);
+  rc = ensure_dev(&c->d_step, &c->d_step_cap, q_abs_n + rows_n + lat_n + (size_t)n * n_heads * 4);
   if (!rc) rc = ensure_dev(&c->d_stepu, &c->d_stepu_cap, 2 * (size_t)n + n_seqs);
   if (!rc) rc = sync_tables(c, st);
   if (!rc) rc = sync_lens(c, st);
@@ -1168,6 +1168,7 @@ int kvcache_mla_step_dev(kvcache* c, uint32_t layer, uint32_t n, const uint32_t*
   float* rows = q_abs + q_abs_n;
   float* latent = rows + rows_n;
   float* lse = latent + lat_n;
+  float* mrg_w = lse + (size_t)n * n_heads;  // [n][H][3] merge weights
   uint32_t* d_ids = c->d_stepu;
   uint32_t* d_pos = d_ids + n;
   uint32_t* d_hist = d_pos + n;
@@ -1208,7 +1209,9 @@ int kvcache_mla_step_dev(kvcache* c, uint32_t layer, uint32_t n, const uint32_t*
   if (!rc)
     rc = kvcu_mla_decode_lse(c->ws, c->pool, layer, n, d_ids, n_seqs, c->d_toff, c->d_tables, d_hist, q_abs,
                              n_heads, scale, latent, lse, st);
-  if (!rc) rc = kvcu_mla_finish(c->pool, n, n_heads, v_dim, q_abs, rows, latent, lse, scale, v_b_dev, attn_dev, st);
+  if (!rc)
+    rc = kvcu_mla_finish_fused(c->pool, n, n_heads, v_dim, q_abs, rows, latent, lse, mrg_w, scale, v_b_dev, attn_dev,
+                               st);
   if (rc) return rc;
   // rows, gemm (prepare) + append + plan + decode + merge, gemm (finish). The
   // three host arrays above are pageable: each cudaMemcpyAsync returned only

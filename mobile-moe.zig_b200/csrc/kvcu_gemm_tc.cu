@@ -54,6 +54,8 @@ struct GemmArgs {
   uint32_t ldc;
   uint64_t c_hs;
   uint32_t* status;
+  kvcu_gemm_merge mrg;  // mrg.w == nullptr: plain A
+  uint32_t heads;
 };
 
 __device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
@@ -96,6 +98,7 @@ __global__ void __launch_bounds__(NTHR, 1) k_head_gemm_tc(GemmArgs g) {
   const uint32_t z = blockIdx.z, m0 = blockIdx.y * TM, n0 = blockIdx.x * NT;
   const float* A = g.A + z * g.a_hs;
   const float* B = g.B + z * g.b_hs;
+  const bool merge = g.mrg.w != nullptr;  // uniform
   float* C = g.C + z * g.c_hs;
   auto bar = [&](int i) { return sbase + L::OFF_BAR + 8u * (uint32_t)i; };
   if (tid == 0) {
@@ -122,13 +125,32 @@ __global__ void __launch_bounds__(NTHR, 1) k_head_gemm_tc(GemmArgs g) {
   // current one is stored, synchronised and multiplied.
   constexpr int NA = TM * 8 / NTHR, NB = NT * 8 / NTHR;
   float4 pa[NA], pb[NB];
+  // merge: the rows' weights once, and the newest token's latent beside A
+  float4 px[NA];
+  float mw[NA][3];
+  if (merge) {
+#pragma unroll
+    for (int i = 0; i < NA; ++i) {
+      const uint32_t r = (tid + NTHR * i) >> 3;
+      mw[i][0] = mw[i][1] = mw[i][2] = 0.f;
+      if (m0 + r < g.M) {
+        const float* wr = g.mrg.w + ((uint64_t)(m0 + r) * g.heads + z) * 3;
+        mw[i][0] = __ldg(wr);
+        mw[i][1] = __ldg(wr + 1);
+        mw[i][2] = __ldg(wr + 2);
+      }
+    }
+  }
   auto load_slice = [&](uint32_t c) {
     const uint32_t k0 = c * TK;
 #pragma unroll
     for (int i = 0; i < NA; ++i) {
       const uint32_t e = tid + NTHR * i, r = e >> 3, ch = e & 7u;
-      pa[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (m0 + r < g.M) pa[i] = __ldg(reinterpret_cast<const float4*>(A + (uint64_t)(m0 + r) * g.lda + k0 + 4 * ch));
+      pa[i] = px[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (m0 + r >= g.M) continue;
+      pa[i] = __ldg(reinterpret_cast<const float4*>(A + (uint64_t)(m0 + r) * g.lda + k0 + 4 * ch));
+      if (merge)
+        px[i] = __ldg(reinterpret_cast<const float4*>(g.mrg.rows + (uint64_t)(m0 + r) * g.mrg.ldr + k0 + 4 * ch));
     }
 #pragma unroll
     for (int i = 0; i < NB; ++i) {
@@ -154,7 +176,16 @@ __global__ void __launch_bounds__(NTHR, 1) k_head_gemm_tc(GemmArgs g) {
 #pragma unroll
     for (int i = 0; i < NA; ++i) {
       const uint32_t e = tid + NTHR * i;
-      put4(a_hi, a_lo, e >> 3, e & 7u, pa[i]);
+      float4 v = pa[i];
+      if (merge) {
+        // the MLA step's merge, in the order of the in-place merge kernel (the
+        // history term is dropped, not multiplied, where its weight is 0)
+        const float wh = mw[i][0], wc = mw[i][1], inv = mw[i][2];
+        const float4 h = wh > 0.f ? make_float4(v.x * wh, v.y * wh, v.z * wh, v.w * wh) : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float4 x = px[i];
+        v = make_float4((h.x + x.x * wc) * inv, (h.y + x.y * wc) * inv, (h.z + x.z * wc) * inv, (h.w + x.w * wc) * inv);
+      }
+      put4(a_hi, a_lo, e >> 3, e & 7u, v);
     }
 #pragma unroll
     for (int i = 0; i < NB; ++i) {
@@ -258,12 +289,15 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 // the caller can use the CUDA-core kernel instead.
 int kvcu_launch_head_gemm_tc(bool trans_b, uint32_t heads, uint32_t M, uint32_t N, uint32_t K, const float* A,
                              uint32_t lda, uint64_t a_hs, const float* B, uint32_t ldb, uint64_t b_hs, float* C,
-                             uint32_t ldc, uint64_t c_hs, uint32_t* status, cudaStream_t st) {
+                             uint32_t ldc, uint64_t c_hs, uint32_t* status, cudaStream_t st,
+                             const kvcu_gemm_merge* mrg) {
   if (M == 0 || heads == 0) return KVCU_OK;
   if (N % 128 != 0 || K % TK != 0 || K == 0 || lda % 4 || ldb % 4 || ldc % 4 || a_hs % 4 || b_hs % 4 || c_hs % 4 ||
-      !aligned16(A) || !aligned16(B) || !aligned16(C) || !status)
+      !aligned16(A) || !aligned16(B) || !aligned16(C) || !status ||
+      (mrg && (!mrg->w || mrg->ldr % 4 || !aligned16(mrg->rows))))
     return KVCU_ERR_UNSUPPORTED;
-  GemmArgs g{M, N, K, A, lda, a_hs, B, ldb, b_hs, C, ldc, c_hs, status};
+  GemmArgs g{M, N, K, A, lda, a_hs, B, ldb, b_hs, C, ldc, c_hs, status,
+             mrg ? *mrg : kvcu_gemm_merge{nullptr, 0, nullptr}, heads};
   // one CTA per SM (shared memory): pick the N tile whose waves of CTAs cover
   // the fewest columns per SM
   const uint64_t sms = (uint64_t)kvcu_current_sm_count(), mt = (M + TM - 1) / TM;

@@ -132,9 +132,25 @@ int kvcu_pool_read_checkpoint_staged(kvcu_pool* p, uint64_t offset, uint64_t nby
 // ---- per-head GEMM on the tensor cores, 3xTF32 (kvcu_gemm_tc.cu) ----
 // KVCU_ERR_UNSUPPORTED (nothing launched) unless N % 128 == 0, K % 32 == 0 and
 // every row and pointer is 16-byte aligned.
+// With `mrg`, the A operand of head z is the log-sum-exp merge of the MLA
+// step's newest token into the history output, formed while A is loaded:
+// A'[m][k] = (A[m][k] * wh + rows[m * ldr + k] * wc) * inv, (wh, wc, inv) =
+// w[(m * heads + z) * 3 ..]; the history term is dropped (not multiplied)
+// where wh == 0, so a NaN there does not reach the product.
+struct kvcu_gemm_merge {
+  const float* rows;
+  uint32_t ldr;
+  const float* w;
+};
 int kvcu_launch_head_gemm_tc(bool trans_b, uint32_t heads, uint32_t M, uint32_t N, uint32_t K, const float* A,
                              uint32_t lda, uint64_t a_hs, const float* B, uint32_t ldb, uint64_t b_hs, float* C,
-                             uint32_t ldc, uint64_t c_hs, uint32_t* status, cudaStream_t st);
+                             uint32_t ldc, uint64_t c_hs, uint32_t* status, cudaStream_t st,
+                             const kvcu_gemm_merge* mrg = nullptr);
+// kvcu_mla_finish with scratch w [n][n_heads][3] for the merge weights, so the
+// v_b GEMM merges while it loads (kvcu_mla.cu); stream-ordered on st.
+int kvcu_mla_finish_fused(kvcu_pool* pool, uint32_t n, uint32_t n_heads, uint32_t v_dim, const float* q_abs,
+                          const float* rows, float* latent, const float* lse, float* w, float scale,
+                          const float* v_b, float* attn, cudaStream_t st);
 // ---- allocation-free decode (kvcu_noalloc.cu) ----
 // Resolve (and so reserve) the fixed decode scratch on `device`, which must be
 // current; kvcu_init calls it.

@@ -19,7 +19,9 @@
 //   kvcu_append(rows) at pos; kvcu_mla_decode_lse over p < pos (the history)
 //   kvcu_mla_finish   merges the newest token as the reference treats it
 //                     (unquantized c, k_pe as the cache holds it), then v_b
-//                     k_mla_merge + k_head_gemm
+//                     k_mla_merge + k_head_gemm; the cache's own step uses
+//                     k_mla_merge_w + a v_b GEMM that applies the merge weights
+//                     while it loads the latent (kvcu_mla_finish_fused)
 // The two per-head products are small f32 GEMMs (k_b: n x qk_nope x R, v_b:
 // n x R x v_dim per head), ~1.3 GFLOP each at a 512-sequence batch. They run
 // on the tensor cores as 3xTF32 (k_head_gemm_tc, f32-level error) where the
@@ -195,10 +197,84 @@ int launch_head_gemm(uint32_t heads, uint32_t M, uint32_t N, uint32_t K, const f
   return launch_head_gemm_cc<TRANS_B>(heads, M, N, K, A, lda, a_hs, B, ldb, b_hs, C, ldc, c_hs, st);
 }
 
-// One CTA per (entry, head): the newest token's score with the unquantized
-// latent and k_pe as the cache holds it, then its log-sum-exp merge into the
-// history's normalised output (in place).
+// The MLA step's merge of the newest token into the history output, in two
+// parts.  k_mla_merge_w, one CTA per entry: the newest token's k_pe as the
+// cache holds it (once for all heads) and its unquantized latent go to shared
+// memory, then one warp per head forms the token's score and the log-sum-exp
+// weights (wh, wc, inv) of out = (history * wh + latent * wc) * inv.  The
+// weights are applied by the v_b GEMM while it loads its A operand, or, where
+// that kernel does not fit the shapes, by k_mla_merge_apply in place.
 constexpr int MERGE_THREADS = 128;
+__global__ void __launch_bounds__(MERGE_THREADS)
+    k_mla_merge_w(uint32_t H, uint32_t R, uint32_t P, int kpe_q8, const float* __restrict__ q_abs,
+                  const float* __restrict__ rows, const float* __restrict__ lse, float scale,
+                  float* __restrict__ w) {
+  extern __shared__ float msh[];  // [R] latent of the newest token, then [P] its k_pe
+  float* cs = msh;
+  float* kpe = msh + R;
+  const uint32_t b = blockIdx.x, tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
+  const float* row = rows + (uint64_t)b * (R + P);
+  for (uint32_t c = tid; c < R; c += blockDim.x) cs[c] = row[c];
+  // k_pe of the newest token as stored: the Q8_0 round trip of the append
+  // (d = amax/127, f16 scale, clamp(round(x/d)), dequant f16(d) * q)
+  if (warp == 0) {
+    for (uint32_t blk = 0; blk * 32 < P; ++blk) {
+      const uint32_t e = blk * 32 + lane;
+      const float v = e < P ? row[R + e] : 0.f;
+      float out = v;
+      if (kpe_q8) {
+        float amax = fabsf(v);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        const float d = kvcu::q8_scale(amax);
+        const int8_t qv = d > 0.f ? kvcu::q8_value(v, d) : (int8_t)0;
+        out = __fmul_rn(kvcu::f16_to_f32(kvcu::f32_to_f16(d)), (float)qv);
+      }
+      if (e < P) kpe[e] = out;
+    }
+  }
+  __syncthreads();
+  for (uint32_t h = warp; h < H; h += blockDim.x / 32) {
+    const float* qa = q_abs + ((uint64_t)b * H + h) * (R + P);
+    float dot = 0.f;
+#pragma unroll 4
+    for (uint32_t c = lane; c < R; c += 32) dot = fmaf(qa[c], cs[c], dot);
+    for (uint32_t r = lane; r < P; r += 32) dot = fmaf(qa[R + r], kpe[r], dot);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+    if (lane == 0) {
+      const float s = dot * scale;
+      const float lh = lse[(uint64_t)b * H + h];
+      const float m = fmaxf(lh, s);
+      const float wh = lh == -INFINITY ? 0.f : expf(lh - m);
+      const float wc = expf(s - m);
+      float* wr = w + ((uint64_t)b * H + h) * 3;
+      wr[0] = wh;
+      wr[1] = wc;
+      wr[2] = 1.0f / (wh + wc);
+    }
+  }
+}
+
+// The merge in place, for the CUDA-core GEMM: one CTA per (entry, head).
+__global__ void __launch_bounds__(MERGE_THREADS)
+    k_mla_merge_apply(uint32_t H, uint32_t R, uint32_t P, const float* __restrict__ rows, const float* __restrict__ w,
+                      float* __restrict__ latent) {
+  const uint32_t b = blockIdx.x / H, h = blockIdx.x % H;
+  const float* row = rows + (uint64_t)b * (R + P);
+  const float* wr = w + ((uint64_t)b * H + h) * 3;
+  const float wh = wr[0], wc = wr[1], inv = wr[2];
+  float* lat = latent + ((uint64_t)b * H + h) * R;
+  for (uint32_t c = threadIdx.x; c < R; c += blockDim.x) {
+    const float hv = wh > 0.f ? lat[c] * wh : 0.f;
+    lat[c] = (hv + row[c] * wc) * inv;
+  }
+}
+
+// The whole merge in place, one CTA per (entry, head), for kvcu_mla_finish,
+// whose caller passes no room for the weights: the newest token's score with
+// the unquantized latent and k_pe as the cache holds it, then its log-sum-exp
+// merge into the history's normalised output.
 __global__ void __launch_bounds__(MERGE_THREADS)
     k_mla_merge(uint32_t H, uint32_t R, uint32_t P, int kpe_q8, const float* __restrict__ q_abs,
                 const float* __restrict__ rows, float* __restrict__ latent, const float* __restrict__ lse,
@@ -311,6 +387,39 @@ extern "C" int kvcu_mla_finish(kvcu_pool* pool, uint32_t n, uint32_t n_heads, ui
   // attn[b][h][j] = latent[b][h] (n x R) x v_b_h^T, v_b_h = v_b[h*v_dim .. +v_dim][0:R]
   return launch_head_gemm<true>(n_heads, n, v_dim, R, latent, n_heads * R, R, v_b, R, (uint64_t)v_dim * R,
                                 attn, n_heads * v_dim, v_dim, pool->status, st);
+}
+
+// kvcu_mla_finish with scratch for the merge weights w [n][H][3]: the weights
+// kernel, then the v_b GEMM that merges its A operand as it loads it (no pass
+// over the latent in between); the in-place merge and the CUDA-core GEMM where
+// the tensor-core kernel does not fit the shapes.
+int kvcu_mla_finish_fused(kvcu_pool* pool, uint32_t n, uint32_t n_heads, uint32_t v_dim, const float* q_abs,
+                          const float* rows, float* latent, const float* lse, float* w, float scale,
+                          const float* v_b, float* attn, cudaStream_t st) {
+  if (!valid_dims(pool, n_heads, v_dim)) {
+    kvcu_set_error("kvcu_mla_finish: unsupported n_heads %u / v_dim %u / pool dims", n_heads, v_dim);
+    return KVCU_ERR_INVALID_ARG;
+  }
+  if (!n) return KVCU_OK;
+  if (!q_abs || !rows || !latent || !lse || !w || !v_b || !attn) return KVCU_ERR_INVALID_ARG;
+  DevScope d(pool->device);
+  if (d.rc) return d.rc;
+  const uint32_t R = pool->kv_rank, P = pool->rope_dim;
+  if ((uint64_t)(R + P) * sizeof(float) > 48u * 1024u)  // the weights kernel's shared latent and k_pe
+    return kvcu_mla_finish(pool, n, n_heads, v_dim, q_abs, rows, latent, lse, scale, v_b, attn, st);
+  k_mla_merge_w<<<n, MERGE_THREADS, (R + P) * sizeof(float), st>>>(n_heads, R, P, pool->quantized ? 1 : 0, q_abs,
+                                                                    rows, lse, scale, w);
+  int rc = kvcu_check_cuda(cudaGetLastError(), "mla merge launch");
+  if (rc) return rc;
+  const kvcu_gemm_merge mrg{rows, R + P, w};
+  rc = kvcu_launch_head_gemm_tc(true, n_heads, n, v_dim, R, latent, n_heads * R, R, v_b, R, (uint64_t)v_dim * R,
+                                attn, n_heads * v_dim, v_dim, pool->status, st, &mrg);
+  if (rc != KVCU_ERR_UNSUPPORTED) return rc;
+  k_mla_merge_apply<<<n * n_heads, MERGE_THREADS, 0, st>>>(n_heads, R, P, rows, w, latent);
+  rc = kvcu_check_cuda(cudaGetLastError(), "mla merge launch");
+  if (rc) return rc;
+  return launch_head_gemm_cc<true>(n_heads, n, v_dim, R, latent, n_heads * R, R, v_b, R, (uint64_t)v_dim * R, attn,
+                                   n_heads * v_dim, v_dim, st);
 }
 
 // Per-head batched GEMM entry point (the step's two contractions, exposed so a
