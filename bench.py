@@ -581,6 +581,52 @@ def multi_gpu_check(kvcu, torch, dist, dev, local_rank, rank, world, parts, lens
                          "seeded generator"}
 
 
+def bind_to_gpu_node(torch, dev_index):
+    """Run this process on the CPUs of the NUMA node that the GPU's PCIe root
+    hangs off, so that the pinned host buffers it touches first afterwards (q,
+    out, rows, the cache's staging) are local to the GPU: with 8 ranks, buffers
+    on the other socket send every host<->device byte over the socket link.
+    Best effort; returns (node, previous CPU set) or (None, None)."""
+    try:
+        prev = os.sched_getaffinity(0)
+        p = torch.cuda.get_device_properties(dev_index)
+    except (OSError, AttributeError, RuntimeError, AssertionError):
+        return None, None
+    node, cpus = None, set()
+    try:  # the kernel's view: the device's NUMA node and that node's CPUs
+        bus = f"{p.pci_domain_id:04x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+        with open(f"/sys/bus/pci/devices/{bus}/numa_node") as f:
+            node = int(f.read().strip())
+        if node >= 0:
+            with open(f"/sys/devices/system/node/node{node}/cpulist") as f:
+                for part in f.read().strip().split(","):
+                    lo, _, hi = part.partition("-")
+                    cpus.update(range(int(lo), int(hi or lo) + 1))
+    except (OSError, ValueError):
+        node, cpus = None, set()
+    if not cpus:  # else the driver's view (a read-only NVML query): the device's ideal CPU set
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            try:
+                h = pynvml.nvmlDeviceGetHandleByPciBusId(
+                    f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0")
+                words = pynvml.nvmlDeviceGetCpuAffinity(h, (os.cpu_count() + 63) // 64)
+                for w, word in enumerate(words):
+                    cpus.update(64 * w + b for b in range(64) if (int(word) >> b) & 1)
+                node = "nvml"
+            finally:
+                pynvml.nvmlShutdown()
+        except Exception:  # no NVML binding or no answer: leave the process as it is
+            return None, None
+    cpus &= prev
+    if not cpus or cpus == prev:
+        return (node if cpus else None), None
+    os.sched_setaffinity(0, cpus)
+    return node, prev
+
+
 def physical_gpu(local_rank):
     vis = os.environ.get("CUDA_VISIBLE_DEVICES")
     if vis:
@@ -598,6 +644,7 @@ def run_ours(args, rank, world, local_rank):
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
+    numa_node, all_cpus = bind_to_gpu_node(torch, local_rank)
     kvcu.init(local_rank)
     NL = args.layers
     lens_all = config5_lengths(n=args.seqs)
@@ -817,6 +864,8 @@ def run_ours(args, rank, world, local_rank):
         ckpt["all_ranks_bit_exact"] = bool(ok.item() == 1.0)
     traffic_per_tok = read_traffic_profile()
     if rank == 0:
+        if all_cpus:
+            os.sched_setaffinity(0, all_cpus)  # the CPU baseline uses every host core
         cores = host_cores()
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
@@ -845,6 +894,7 @@ def run_ours(args, rank, world, local_rank):
                     "d2h_bytes_per_step": d2h,
                     "call": "kvcache_append_decode_layers: one host-buffer call per step (all layers), one "
                             "synchronise",
+                    "host_numa_node": numa_node,
                     "host_buffers": ("pinned; q read and out written over PCIe by the kernels"
                                      if e2e_mapped else "copied in and out around the kernels")},
             "step_form": ("all layers of a step in one append launch and one persistent decode launch "
