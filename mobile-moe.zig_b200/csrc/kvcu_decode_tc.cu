@@ -649,6 +649,54 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       ++esync;
       return r;
     };
+    // ---- query -> two int8 digits per element (x = s_h * (d0 + d1/256)), per-head
+    // scale; each half's 4 warps encode that half's heads.  The next item's
+    // query is staged as soon as this item's last P is out (its QK MMAs are all
+    // done then), so the next item's first QK overlaps this item's drain.
+    uint32_t staged_u = 0xFFFFFFFFu;
+    auto stage_q = [&](const Unit& su, const Item& si) -> bool {
+      const float* qb = a.q + su.li * a.q_lstride + (uint64_t)si.b * H * W;
+      for (uint32_t hl = ew & 3u; hl < (uint32_t)HH; hl += 4) {
+        const uint32_t h = h0 + hl;
+        float amax = 0.f;
+        float v[18];
+#pragma unroll
+        for (int j = 0; j < 18; ++j) {
+          v[j] = h < H ? qb[(uint64_t)h * W + lane + 32 * j] : 0.f;
+          amax = fmaxf(amax, fabsf(v[j]));
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        const float sh = amax > 0.f ? amax / 127.0f : 1.0f;
+        const float inv = 1.0f / sh;
+        const uint32_t qrow = hf * Cfg<HK>::NQH + 4u * (hl >> 1) + (hl & 1u);  // digit-0 row
+#pragma unroll
+        for (int j = 0; j < 18; ++j) {
+          const uint32_t kcol = lane + 32u * j;
+          const float x = v[j] * inv;
+          const float d0 = fminf(fmaxf(rintf(x), -127.f), 127.f);
+          const float d1 = fminf(fmaxf(rintf((x - d0) * 256.f), -127.f), 127.f);
+          uint8_t* base;
+          uint32_t o0, o1;
+          if (kcol < 512) {
+            base = smem + OFF_QD + (kcol >> 7) * QD_LAT_BYTES;
+            o0 = sw128_off(qrow, kcol & 127u);
+            o1 = sw128_off(qrow + 2u, kcol & 127u);
+          } else {
+            base = smem + OFF_QD_ROPE;
+            o0 = sw64_off(qrow, kcol - 512u);
+            o1 = sw64_off(qrow + 2u, kcol - 512u);
+          }
+          base[o0] = (uint8_t)(int8_t)(int)d0;
+          base[o1] = (uint8_t)(int8_t)(int)d1;
+        }
+        if (lane == 0) qscale[h] = sh * (1.0f / 256.0f) * a.scale_log2;
+      }
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(B_Q_FULL));
+      return epi_sync();  // this half's qscale visible to its 4 warps
+    };
     volatile uint32_t* cur_item = reinterpret_cast<volatile uint32_t*>(smem + OFF_CUR_ITEM);
     for (uint32_t u = 0; u < n_units && ok; ++u) {
       if (ew == 0 && lane == 0) *cur_item = u;
@@ -673,50 +721,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         if (single && lse_l && ew == 0 && lane < H) lse_l[(uint64_t)im.b * H + lane] = -INFINITY;
         continue;
       }
-      // ---- query -> two int8 digits per element (x = s_h * (d0 + d1/256)), per-head
-      // scale; each half's 4 warps encode that half's heads
-      {
-        const float* qb = a.q + un.li * a.q_lstride + (uint64_t)im.b * H * W;
-        for (uint32_t hl = ew & 3u; hl < (uint32_t)HH; hl += 4) {
-          const uint32_t h = h0 + hl;
-          float amax = 0.f;
-          float v[18];
-#pragma unroll
-          for (int j = 0; j < 18; ++j) {
-            v[j] = h < H ? qb[(uint64_t)h * W + lane + 32 * j] : 0.f;
-            amax = fmaxf(amax, fabsf(v[j]));
-          }
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-          const float sh = amax > 0.f ? amax / 127.0f : 1.0f;
-          const float inv = 1.0f / sh;
-          const uint32_t qrow = hf * Cfg<HK>::NQH + 4u * (hl >> 1) + (hl & 1u);  // digit-0 row
-#pragma unroll
-          for (int j = 0; j < 18; ++j) {
-            const uint32_t kcol = lane + 32u * j;
-            const float x = v[j] * inv;
-            const float d0 = fminf(fmaxf(rintf(x), -127.f), 127.f);
-            const float d1 = fminf(fmaxf(rintf((x - d0) * 256.f), -127.f), 127.f);
-            uint8_t* base;
-            uint32_t o0, o1;
-            if (kcol < 512) {
-              base = smem + OFF_QD + (kcol >> 7) * QD_LAT_BYTES;
-              o0 = sw128_off(qrow, kcol & 127u);
-              o1 = sw128_off(qrow + 2u, kcol & 127u);
-            } else {
-              base = smem + OFF_QD_ROPE;
-              o0 = sw64_off(qrow, kcol - 512u);
-              o1 = sw64_off(qrow + 2u, kcol - 512u);
-            }
-            base[o0] = (uint8_t)(int8_t)(int)d0;
-            base[o1] = (uint8_t)(int8_t)(int)d1;
-          }
-          if (lane == 0) qscale[h] = sh * (1.0f / 256.0f) * a.scale_log2;
+      if (staged_u != u) {
+        if (!stage_q(un, im)) {
+          ok = false;
+          break;
         }
-        fence_proxy_async();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(B_Q_FULL));
-        if (!epi_sync()) break;  // this half's qscale visible to its 4 warps
+        staged_u = u;
       }
       // running reference max per head (log2 domain), identical in the 4 warps of the half
       float mref[HH];
@@ -917,6 +927,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         fence_proxy_async();
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(B_P_FULL));
+      }
+      if (!ok) break;
+      for (uint32_t u2 = u + 1; u2 < n_units; ++u2) {
+        const Unit un2 = unit_of(u2, it_begin, cnt);
+        const Item im2 = load_item(a, un2.it);
+        if (im2.ntiles == 0) continue;
+        if (!stage_q(un2, im2)) ok = false;
+        staged_u = u2;
+        break;
       }
       if (!ok) break;
       // ---- item end: l (every TMEM lane holds it), drain O, write the output or the partial
