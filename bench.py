@@ -798,6 +798,12 @@ def run_ours(args, rank, world, local_rank):
                          "a model's layer loop calls the cache"}
 
     # ---- e2e through the host-buffer API (pinned host memory, copies inside)
+    # Measured on this pool's 8-GPU boxes (config 5, e2e ctx-tokens/s): N=4 in place 10.6 G, q by DMA
+    # 9.8 G; N=8 in place 8.5 G, q by DMA 13.2 G, both by DMA 10.8 G. With 8 ranks the kernels' own
+    # reads of q over the shared host links fall behind one large DMA per step.
+    host_io = args.host_io if args.host_io != "scale" else ("copy_in" if world >= 8 else "auto")
+    cache.set_host_io({"auto": cache.HOST_IO_AUTO, "copy": cache.HOST_IO_COPY,
+                       "copy_in": cache.HOST_IO_COPY_IN}[host_io])
     q_host = qs.cpu().pin_memory()
     out_host = torch.empty((NL, n, H, R), dtype=torch.float32).pin_memory()
     rows_host = torch.empty((NL, n, W), dtype=torch.float32).pin_memory()
@@ -895,7 +901,10 @@ def run_ours(args, rank, world, local_rank):
                     "call": "kvcache_append_decode_layers: one host-buffer call per step (all layers), one "
                             "synchronise",
                     "host_numa_node": numa_node,
-                    "host_buffers": ("pinned; q read and out written over PCIe by the kernels"
+                    "host_io": host_io,
+                    "host_buffers": ("pinned; q copied in by DMA, out written over PCIe by the kernels"
+                                     if host_io == "copy_in" else
+                                     "pinned; q read and out written over PCIe by the kernels"
                                      if e2e_mapped else "copied in and out around the kernels")},
             "step_form": ("all layers of a step in one append launch and one persistent decode launch "
                           "(kvcache_append_layers_dev + kvcache_mla_decode_layers_dev); per_layer below is the same "
@@ -943,6 +952,9 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--host-io", choices=["scale", "auto", "copy", "copy_in"], default="scale",
+                    help="how the host-buffer calls of the e2e figure move q / out (kvcache_set_host_io); "
+                         "scale: q read in place by the kernels below 8 ranks, copied by DMA from 8 on")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--e2e-warmup", type=int, default=1)
     ap.add_argument("--mla-steps", type=int, default=2, help="timed whole-MLA-step passes (after one untimed)")

@@ -464,6 +464,17 @@ int kvcache_mla_attention_batch_dev(kvcache* c, uint32_t layer, uint32_t seq, ui
 /* 1 when the last kvcache_mla_decode used its buffers in place (pinned,
  * mapped), 0 when it copied. */
 int kvcache_last_decode_mapped(const kvcache* c);
+/* How the host-buffer decode calls move q and out: KVCACHE_HOST_IO_AUTO (the
+ * default) reads q and writes out in place over PCIe from the kernels when the
+ * buffers are pinned and mapped, else copies; KVCACHE_HOST_IO_COPY always
+ * copies them by DMA before and after the kernels; KVCACHE_HOST_IO_COPY_IN
+ * makes kvcache_append_decode_layers copy q by DMA and let the kernels write
+ * out in place (the other host-buffer calls copy both ways in this mode).  When many GPUs share the host's PCIe and memory, large DMA
+ * transfers can move the bytes faster than the kernels' own reads. */
+#define KVCACHE_HOST_IO_AUTO 0
+#define KVCACHE_HOST_IO_COPY 1
+#define KVCACHE_HOST_IO_COPY_IN 2
+int kvcache_set_host_io(kvcache* c, int mode);
 /* One MLA decode step of layer `layer` for a batch of sequences (the batched
  * form of src/inference.zig:492-660): each entry b appends its new token at
  * positions[b] (host array; each sequence at most once) and attends over

@@ -235,6 +235,7 @@ struct kvcache {
   uint32_t last_launches = 0;
   int decode_impl = KVCU_DECODE_AUTO;
   int last_mapped = 0;  // the last host-buffer decode read q / wrote out in place (pinned, mapped)
+  int host_io = KVCACHE_HOST_IO_AUTO;
   // background save (kvcache_save_to_file_v2_async): the job in flight, and its
   // device staging and two pinned host buffers, kept for the next save
   kvcache_save* active_save = nullptr;
@@ -707,7 +708,7 @@ int kvcache_mla_attention_batch(kvcache* c, uint32_t layer, uint32_t seq, uint32
   if (!n_pos) return KVCU_OK;
   DevScope d(c->device);
   const size_t qn = (size_t)n_pos * n_heads * c->row_width(), on = (size_t)n_pos * n_heads * c->kv_rank;
-  const void* q_map = mapped_host_range(q, qn * 4);
+  const void* q_map = c->host_io == KVCACHE_HOST_IO_AUTO ? mapped_host_range(q, qn * 4) : nullptr;
   void* out_map = q_map ? mapped_host_range(out, on * 4) : nullptr;
   int rc;
   if (q_map && out_map) {
@@ -1066,8 +1067,19 @@ int kvcache_append_decode_layers(kvcache* c, uint32_t layer, uint32_t n_layers, 
   uint32_t launches = 1;
   // ---- the decode of every layer: q / out in place when pinned and mapped, else copied
   const uint64_t qs = (uint64_t)n * n_heads * Wd, os = (uint64_t)n * n_heads * c->kv_rank;
-  const void* q_map = mapped_host_range(q, (size_t)n_layers * qs * 4);
+  const void* q_map =
+      c->host_io == KVCACHE_HOST_IO_AUTO ? mapped_host_range(q, (size_t)n_layers * qs * 4) : nullptr;
   void* out_map = q_map ? mapped_host_range(out, (size_t)n_layers * os * 4) : nullptr;
+  if (c->host_io == KVCACHE_HOST_IO_COPY_IN) {
+    // q by DMA before the kernels, out written in place by them
+    out_map = mapped_host_range(out, (size_t)n_layers * os * 4);
+    if (out_map) {
+      rc = ensure_dev(&c->d_f, &c->d_f_cap, (size_t)n_layers * qs);
+      if (rc) return rc;
+      KVCU_CUDA(cudaMemcpyAsync(c->d_f, q, (size_t)n_layers * qs * 4, cudaMemcpyHostToDevice, st));
+      q_map = c->d_f;
+    }
+  }
   c->last_mapped = (q_map && out_map) ? 1 : 0;
   if (c->last_mapped) {
     rc = decode_impl(c, layer, n, seq_ids, static_cast<const float*>(q_map), n_heads, scale,
@@ -1113,7 +1125,7 @@ int kvcache_mla_decode(kvcache* c, uint32_t layer, uint32_t n, const uint32_t* s
   const size_t qn = (size_t)n * n_heads * c->row_width(), on = (size_t)n * n_heads * c->kv_rank;
   // Pinned, mapped host buffers that hold the whole q / out: the kernels read
   // q and write out over the bus themselves, overlapped with the decode.
-  const void* q_map = mapped_host_range(q, qn * 4);
+  const void* q_map = c->host_io == KVCACHE_HOST_IO_AUTO ? mapped_host_range(q, qn * 4) : nullptr;
   void* out_map = q_map ? mapped_host_range(out, on * 4) : nullptr;
   c->last_mapped = (q_map && out_map) ? 1 : 0;
   if (c->last_mapped) {
@@ -1223,6 +1235,12 @@ int kvcache_mla_step_dev(kvcache* c, uint32_t layer, uint32_t n, const uint32_t*
 uint32_t kvcache_last_launches(const kvcache* c) { return c ? c->last_launches : 0; }
 
 int kvcache_last_decode_mapped(const kvcache* c) { return c ? c->last_mapped : 0; }
+
+int kvcache_set_host_io(kvcache* c, int mode) {
+  if (!c || mode < KVCACHE_HOST_IO_AUTO || mode > KVCACHE_HOST_IO_COPY_IN) return KVCU_ERR_INVALID_ARG;
+  c->host_io = mode;
+  return KVCU_OK;
+}
 
 int kvcache_set_decode_impl(kvcache* c, int impl) {
   if (!c || impl < KVCU_DECODE_AUTO || impl > KVCU_DECODE_TENSOR_CORE) return KVCU_ERR_INVALID_ARG;

@@ -142,6 +142,7 @@ _SIGS = {
                                     _u32, _u32, _f32, _vp, _vp]),
     "kvcache_last_launches": (_u32, [_vp]),
     "kvcache_last_decode_mapped": (_i32, [_vp]),
+    "kvcache_set_host_io": (_i32, [_vp, _i32]),
     "kvcache_set_decode_impl": (_i32, [_vp, _i32]),
     "kvcache_last_decode_impl": (_i32, [_vp]),
     "kvcache_save_to_file_v2": (_i32, [_vp, _cp]),
@@ -712,6 +713,14 @@ class KVCache:
 
     def set_decode_impl(self, impl):
         check(lib().kvcache_set_decode_impl(self._h, impl), "set_decode_impl")
+
+    HOST_IO_AUTO, HOST_IO_COPY, HOST_IO_COPY_IN = 0, 1, 2
+
+    def set_host_io(self, mode):
+        """kvcache_set_host_io: HOST_IO_AUTO (q / out in place over PCIe when pinned
+        and mapped), HOST_IO_COPY (DMA copies around the kernels) or HOST_IO_COPY_IN
+        (q by DMA, out in place; the multi-layer call)."""
+        check(lib().kvcache_set_host_io(self._h, mode), "set_host_io")
 
     @property
     def last_decode_impl(self):

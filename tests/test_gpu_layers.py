@@ -111,7 +111,8 @@ def test_append_layers_matches_per_layer_appends(kv, quant):
     pb.close()
 
 
-def test_append_decode_layers_host_buffers_match_per_layer_calls(kv):
+@pytest.mark.parametrize("host_io", [0, 1, 2])  # q / out in place over PCIe, DMA copies, q by DMA
+def test_append_decode_layers_host_buffers_match_per_layer_calls(kv, host_io):
     import torch
 
     lens = [40, 300, 5000, 12000, 3]
@@ -140,7 +141,9 @@ def test_append_decode_layers_host_buffers_match_per_layer_calls(kv):
         for layer in range(nl):
             a.appendBatch(layer, ids, pos, rows[layer].numpy())
             a.mlaDecode_ptr(layer, n, ids, q[layer].data_ptr(), H, SCALE, want[layer].data_ptr())
+        b.set_host_io(host_io)
         b.appendDecodeLayers_ptr(0, nl, n, ids, pos, rows.data_ptr(), q.data_ptr(), H, SCALE, got.data_ptr())
+        assert b.last_decode_mapped == (host_io != kv.KVCache.HOST_IO_COPY)
         assert torch.equal(got, want), step
         assert all(b.seq_len(i) == a.seq_len(i) == lens[i] + step + 1 for i in range(n))
     for c in caches:
