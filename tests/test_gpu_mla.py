@@ -168,3 +168,43 @@ def test_mla_step_layers_share_the_plan(kv, oracle, between):
             # a plain decode of layer 0 over the full lengths plans on the same workspace
             cache.mlaDecode(0, rng.standard_normal((n, H, R + P)).astype(np.float32), ids, SCALE)
     assert launches[1] == launches[0] - (0 if between else 1)
+
+
+def test_mla_finish_public_entry_matches_float64(kv):
+    """kvcu_mla_finish (the C-ABI call a caller with its own scratch uses: the
+    in-place merge, then the v_b product) against float64 on the same inputs:
+    the newest token's score with its latent and k_pe (an f32 pool keeps k_pe
+    as given), the log-sum-exp merge into the history output, and v_b. One entry
+    has an empty history (lse = -inf), so its output is the newest token alone."""
+    import torch
+
+    n, v_dim = 6, V_DIM
+    pool = kv.DevicePool(0, 1, 4, 16, R, P, False)
+    try:
+        g = torch.Generator(device="cuda").manual_seed(43)
+        dev = torch.device("cuda", 0)
+        q_abs = torch.randn((n, H, R + P), device=dev, generator=g) * 0.05
+        rows = torch.randn((n, R + P), device=dev, generator=g)
+        latent = torch.randn((n, H, R), device=dev, generator=g)
+        lse = torch.randn((n, H), device=dev, generator=g) * 3.0
+        lse[2] = float("-inf")
+        v_b = torch.randn((H * v_dim, R), device=dev, generator=g) / R ** 0.5
+        attn = torch.full((n, H, v_dim), float("nan"), device=dev)
+        lat64, rows64, q64, lse64 = latent.double(), rows.double(), q_abs.double(), lse.double()
+        s = (q64 * rows64[:, None, :]).sum(-1) * SCALE
+        m = torch.maximum(lse64, s)
+        wh = torch.where(torch.isinf(lse64), torch.zeros_like(m), torch.exp(lse64 - m))
+        wc = torch.exp(s - m)
+        merged = (lat64 * wh[..., None] + rows64[:, None, :R] * wc[..., None]) / (wh + wc)[..., None]
+        want = torch.einsum("bhr,hjr->bhj", merged, v_b.double().view(H, v_dim, R))
+        torch.cuda.synchronize()
+        rc = kv.lib().kvcu_mla_finish(pool.handle, n, H, v_dim, q_abs.data_ptr(), rows.data_ptr(),
+                                      latent.data_ptr(), lse.data_ptr(), SCALE, v_b.data_ptr(), attn.data_ptr(),
+                                      None)
+        torch.cuda.synchronize()
+        assert rc == 0
+        assert pool.status() == 0
+        err = ((attn.double() - want).abs().amax() / want.abs().amax()).item()
+        assert err <= 2e-5, err
+    finally:
+        pool.close()
