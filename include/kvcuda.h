@@ -237,16 +237,32 @@ int kvcu_mla_finish(kvcu_pool* pool, uint32_t n, uint32_t n_heads, uint32_t v_di
  * lengths are the same for every layer of a step): layers [layer, layer +
  * n_layers) of the pool, layer+i reading q + i*q_layer_stride and writing
  * out + i*out_layer_stride (strides in floats).  The tensor-core path runs
- * them as ONE persistent launch (every CTA takes its plan range once per
- * layer) plus one combine, so the per-launch fill and drain are paid once per
- * step instead of once per layer.  It suits work whose layers' queries are
- * all known up front (a benchmark step, re-scoring a cached context, layer-
- * parallel checks); a model's decode, where layer l+1's query depends on
- * layer l's output (src/inference.zig:279-373), calls kvcu_mla_decode per
- * layer.  The workspace must come from kvcu_decode_ws_create_layers with
- * max_layers >= n_layers. */
+ * them as ONE persistent launch plus one combine, so the per-launch fill and
+ * drain are paid once per step instead of once per layer.  With a one-layer
+ * plan (kvcu_decode_plan) every CTA takes its plan range once per layer; with
+ * a plan from kvcu_decode_plan_layers for the same n_layers, every CTA takes
+ * one range of the list of all (layer, entry) pairs.  It suits work whose
+ * layers' queries are all known up front (a benchmark step, re-scoring a
+ * cached context, layer-parallel checks); a model's decode, where layer l+1's
+ * query depends on layer l's output (src/inference.zig:279-373), calls
+ * kvcu_mla_decode per layer.  The workspace must come from
+ * kvcu_decode_ws_create_layers with max_layers >= n_layers. */
 kvcu_decode_ws* kvcu_decode_ws_create_layers(int device, uint32_t max_batch, uint32_t max_heads,
                                              uint32_t max_layers);
+/* The plan for one kvcu_mla_decode_layers call of n_layers layers (no
+ * counterpart in the reference, which decodes layer by layer): the n_layers x n
+ * (layer, entry) pairs are laid end to end and cut into equal-cost CTA ranges
+ * as one list, so the whole launch splits at most (CTAs - 1) of them, where a
+ * one-layer plan repeated per layer splits up to (CTAs - 1) in every layer.
+ * Fewer split entries mean fewer item set-ups per CTA and fewer outputs left
+ * for the combine kernel after the decode (the ones that cross PCIe last when
+ * `out` is host memory).  Valid only for kvcu_mla_decode_layers with the same
+ * n_layers on the tensor-core path (Q8_0 pool, <= 24 heads); kvcu_mla_decode,
+ * and a call with another layer count, return KVCU_ERR_INVALID_ARG until the
+ * next one-layer plan.  n_layers = 1 gives the one-layer plan.  Needs
+ * max_layers >= n_layers. */
+int kvcu_decode_plan_layers(kvcu_decode_ws* ws, const kvcu_pool* pool, uint32_t n, const uint32_t* seq_ids,
+                            uint32_t n_seqs, const uint32_t* lens, uint32_t n_layers, void* stream);
 int kvcu_mla_decode_layers(kvcu_decode_ws* ws, kvcu_pool* pool, uint32_t layer, uint32_t n_layers, uint32_t n,
                            const uint32_t* seq_ids, uint32_t n_seqs, const uint32_t* table_offsets,
                            const uint32_t* tables, const uint32_t* lens, const float* q, uint64_t q_layer_stride,

@@ -232,6 +232,7 @@ struct kvcache {
   uint64_t plan_serial = 0, mla_plan_serial = ~0ull;
   uint64_t plan_epoch = ~0ull, epoch = 0;
   uint64_t plan_tokens = 0;
+  uint32_t plan_layers = 0;  // layers the cached plan lists as one (1: a one-layer plan)
   uint32_t last_launches = 0;
   int decode_impl = KVCU_DECODE_AUTO;
   int last_mapped = 0;  // the last host-buffer decode read q / wrote out in place (pinned, mapped)
@@ -619,7 +620,13 @@ int decode_impl(kvcache* c, uint32_t layer, uint32_t n, const uint32_t* seq_ids,
   for (uint32_t b = 0; b < n; ++b) tokens += c->seqs[seq_ids[b]].len;
   const bool same_ids = c->plan_ids.size() == n &&
                         std::equal(c->plan_ids.begin(), c->plan_ids.end(), seq_ids);
-  if (!same_ids || c->plan_epoch != c->epoch || tokens > c->plan_tokens + c->plan_tokens / 8) {
+  // A multi-layer call on the tensor-core path balances all its (layer, entry)
+  // pairs as one list, which splits far fewer entries than one layer's plan
+  // repeated per layer.
+  const uint32_t plan_layers =
+      n_layers > 1 && kvcu_decode_layers_fused(c->ws, c->pool, n, n_heads) ? n_layers : 1u;
+  if (!same_ids || c->plan_epoch != c->epoch || c->plan_layers != plan_layers ||
+      tokens > c->plan_tokens + c->plan_tokens / 8) {
     rc = ensure_dev(&c->d_seq_ids, &c->d_seq_ids_cap, std::max<uint32_t>(n, 1));
     if (rc) return rc;
     if (!same_ids) {
@@ -627,12 +634,17 @@ int decode_impl(kvcache* c, uint32_t layer, uint32_t n, const uint32_t* seq_ids,
       KVCU_CUDA(cudaStreamSynchronize(st));
       c->plan_ids.assign(seq_ids, seq_ids + n);
     }
-    rc = kvcu_decode_plan(c->ws, c->pool, n, c->d_seq_ids, (uint32_t)c->seqs.size(), c->d_lens, st);
+    rc = kvcu_decode_plan_layers(c->ws, c->pool, n, c->d_seq_ids, (uint32_t)c->seqs.size(), c->d_lens,
+                                 plan_layers, st);
     ++c->plan_serial;
-    if (rc) return rc;
+    if (rc) {
+      c->plan_epoch = ~0ull;
+      return rc;
+    }
     launches += 1;
     c->plan_epoch = c->epoch;
     c->plan_tokens = tokens;
+    c->plan_layers = plan_layers;
   }
   if (n_layers == 1)
     rc = kvcu_mla_decode(c->ws, c->pool, layer, n, c->d_seq_ids, (uint32_t)c->seqs.size(), c->d_toff,

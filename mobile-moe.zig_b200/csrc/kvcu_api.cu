@@ -370,18 +370,22 @@ kvcu_decode_ws* kvcu_decode_ws_create_layers(int device, uint32_t max_batch, uin
   ws->max_heads = max_heads;
   ws->max_layers = max_layers;
   int rc = kvcu_decode_setup(ws);
-  // items <= batch + ranges - 1 (each cut between CTA ranges splits at most one entry)
+  // items <= batch + ranges - 1 per layer (each cut between CTA ranges splits
+  // at most one entry); a layered plan numbers up to max_layers layers' items
   ws->max_ranges = (uint32_t)ws->decode_ctas;
   ws->max_items = max_batch + ws->max_ranges + 1u;
-  const uint64_t mi = ws->max_items;
-  if (!rc) rc = kvcu_check_cuda(cudaMalloc(&ws->items, mi * sizeof(kvcu_item)), "cudaMalloc(items)");
+  const uint64_t mi = ws->max_items, ml = (uint64_t)max_layers;
+  if (!rc && ml * mi > 0x7FFFFFFFull) {
+    kvcu_set_error("kvcu_decode_ws_create: %u layers x %u batch entries is too large", max_layers, max_batch);
+    rc = KVCU_ERR_INVALID_ARG;
+  }
+  if (!rc) rc = kvcu_check_cuda(cudaMalloc(&ws->items, ml * mi * sizeof(kvcu_item)), "cudaMalloc(items)");
   if (!rc) rc = kvcu_check_cuda(cudaMalloc(&ws->meta, 4 * sizeof(uint32_t)), "cudaMalloc(meta)");
   if (!rc)
     rc = kvcu_check_cuda(cudaMalloc(&ws->ranges, (ws->max_ranges + 1ull) * sizeof(uint32_t)),
                          "cudaMalloc(ranges)");
-  if (!rc) rc = kvcu_check_cuda(cudaMalloc(&ws->seq_first, max_batch * 4ull), "cudaMalloc");
-  if (!rc) rc = kvcu_check_cuda(cudaMalloc(&ws->seq_count, max_batch * 4ull), "cudaMalloc");
-  const uint64_t ml = (uint64_t)max_layers;
+  if (!rc) rc = kvcu_check_cuda(cudaMalloc(&ws->seq_first, ml * max_batch * 4ull), "cudaMalloc");
+  if (!rc) rc = kvcu_check_cuda(cudaMalloc(&ws->seq_count, ml * max_batch * 4ull), "cudaMalloc");
   if (!rc) rc = kvcu_check_cuda(cudaMalloc(&ws->part_o, ml * mi * max_heads * 512ull * 4), "cudaMalloc");
   if (!rc) rc = kvcu_check_cuda(cudaMalloc(&ws->part_ml, ml * mi * max_heads * 2ull * 4), "cudaMalloc");
   if (!rc) rc = kvcu_check_cuda(cudaMemset(ws->meta, 0, 4 * sizeof(uint32_t)), "cudaMemset");
@@ -418,6 +422,25 @@ int kvcu_decode_plan(kvcu_decode_ws* ws, const kvcu_pool* p, uint32_t n, const u
   DeviceGuard g(p->device);
   if (g.rc) return g.rc;
   return kvcu_launch_plan(ws, p, n, seq_ids, n_seqs, lens, (cudaStream_t)stream);
+}
+
+int kvcu_decode_plan_layers(kvcu_decode_ws* ws, const kvcu_pool* p, uint32_t n, const uint32_t* seq_ids,
+                            uint32_t n_seqs, const uint32_t* lens, uint32_t n_layers, void* stream) {
+  if (!ws || !valid_pool(p)) return KVCU_ERR_INVALID_ARG;
+  if (n > ws->max_batch) {
+    kvcu_set_error("kvcu_decode_plan_layers: batch %u exceeds workspace capacity %u", n, ws->max_batch);
+    return KVCU_ERR_INVALID_ARG;
+  }
+  if (n_layers == 0 || n_layers > ws->max_layers) {
+    kvcu_set_error("kvcu_decode_plan_layers: %u layers, the workspace holds %u", n_layers, ws->max_layers);
+    return KVCU_ERR_INVALID_ARG;
+  }
+  if (ws->device != p->device) return KVCU_ERR_INVALID_ARG;
+  if (n && !lens) return KVCU_ERR_INVALID_ARG;
+  DeviceGuard g(p->device);
+  if (g.rc) return g.rc;
+  return kvcu_launch_plan_target(ws, p, n, seq_ids, n_seqs, lens, (uint32_t)ws->decode_ctas, (cudaStream_t)stream,
+                                 nullptr, n_layers);
 }
 
 int kvcu_mla_decode(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint32_t n,

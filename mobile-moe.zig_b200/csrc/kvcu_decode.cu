@@ -82,6 +82,12 @@ __device__ __forceinline__ float warp_sum(float v) {
 // split. Items are numbered in batch order; CTA c runs items
 // [ranges[c], ranges[c+1]).
 //
+// A layered plan (n_layers = L > 1) lays the L x n (layer, entry) pairs of one
+// multi-layer decode on the line as plan entries e = layer * n + b, so the
+// whole launch splits at most G - 1 of them; a one-layer plan, repeated by a
+// multi-layer decode for each layer, splits up to G - 1 in every layer. Every
+// item records its layer offset, and seq_first / seq_count are indexed by e.
+//
 // Items start at multiples of `align` (= max(128, block size)), so every
 // 128-token tile of the tensor-core kernel covers whole physical blocks (or a
 // 128-row-aligned part of one). An entry's last item is open-ended: decode
@@ -99,7 +105,7 @@ __device__ __forceinline__ unsigned long long ceil_div_u64(unsigned long long x,
 
 // entry_lens (nullable): entry b attends min(entry_lens[b], lens[seq]) positions
 // instead of the sequence's whole length (causal multi-query attention).
-__global__ void __launch_bounds__(1024) k_plan(uint32_t n, const uint32_t* __restrict__ seq_ids,
+__global__ void __launch_bounds__(1024) k_plan(uint32_t n, uint32_t n_layers, const uint32_t* __restrict__ seq_ids,
                                                uint32_t n_seqs, const uint32_t* __restrict__ lens,
                                                const uint32_t* __restrict__ entry_lens,
                                                uint32_t max_ranges, uint32_t align, uint32_t max_items,
@@ -121,15 +127,17 @@ __global__ void __launch_bounds__(1024) k_plan(uint32_t n, const uint32_t* __res
     s_ccarry = 0;
   }
   __syncthreads();
-  auto units_of = [&](uint32_t b) -> uint32_t {
+  const uint32_t N = n * n_layers;  // plan entries e = layer * n + b
+  auto units_of = [&](uint32_t e) -> uint32_t {
+    const uint32_t b = e % n;  // only called for e < N, so n > 0
     const uint32_t s = seq_ids ? seq_ids[b] : b;
     uint32_t len = s < n_seqs ? lens[s] : 0u;
     if (entry_lens) len = min(len, entry_lens[b]);
     return (uint32_t)ceil_div_u64(len, align);
   };
   unsigned long long local = 0;
-  for (uint32_t b = tid; b < n; b += blockDim.x)
-    local += (unsigned long long)PLAN_UNIT * units_of(b) + PLAN_ITEM;
+  for (uint32_t e = tid; e < N; e += blockDim.x)
+    local += (unsigned long long)PLAN_UNIT * units_of(e) + PLAN_ITEM;
   atomicAdd(&s_total, local);
   __syncthreads();
   const unsigned long long T = s_total;
@@ -138,10 +146,10 @@ __global__ void __launch_bounds__(1024) k_plan(uint32_t n, const uint32_t* __res
   if (g > max_ranges) g = max_ranges;
   if (g < 1) g = 1;
   const uint32_t G = (uint32_t)g;
-  for (uint32_t base = 0; base < n; base += blockDim.x) {
-    const uint32_t b = base + tid;
-    const bool valid = b < n;
-    const uint32_t U = valid ? units_of(b) : 0u;
+  for (uint32_t base = 0; base < N; base += blockDim.x) {
+    const uint32_t e = base + tid;
+    const bool valid = e < N;
+    const uint32_t U = valid ? units_of(e) : 0u;
     const unsigned long long cost = valid ? (unsigned long long)PLAN_UNIT * U + PLAN_ITEM : 0ull;
     // block-wide exclusive scan of the cost
     unsigned long long xc = cost;
@@ -201,8 +209,9 @@ __global__ void __launch_bounds__(1024) k_plan(uint32_t n, const uint32_t* __res
     __syncthreads();
     const uint32_t first = s_carry + (wid ? s_warp[wid - 1] : 0u) + x - cnt;
     if (valid) {
-      seq_first[b] = first;
-      seq_count[b] = cnt;
+      seq_first[e] = first;
+      seq_count[e] = cnt;
+      const uint32_t layer = e / n;
       // item k covers units [u_k, u_{k+1}); u_0 = 0, the last one is open
       uint32_t k = 0, u_start = 0;
       for (uint32_t c = c_lo; c <= c_hi; ++c) {
@@ -217,10 +226,10 @@ __global__ void __launch_bounds__(1024) k_plan(uint32_t n, const uint32_t* __res
         if (c < c_hi && !u) continue;
         if (first + k < max_items) {
           kvcu_item it;
-          it.b = b;
+          it.b = e - layer * n;
           it.start = u_start * align;
           it.end = (c == c_hi) ? 0xFFFFFFFFu : u * align;
-          it.pad = 0;
+          it.layer = layer;
           items[first + k] = it;
         }
         ++k;
@@ -474,9 +483,12 @@ __global__ void __launch_bounds__(NT, 1) k_decode(DecodeArgs a) {
 // (ranges[c] == seq_first[b] + 1), so the cuts 1 .. G-1 enumerate the split
 // entries without a list; entries decoded as one item were written by the
 // decode kernel.  A fixed grid of warps strides over the (G-1) x H tasks.
-// Several layers decoded with one plan (n_layers_call > 1): layer i's
-// partials sit at item index i * part_lstride + item and its output / lse at
-// + i * out_lstride / lse_lstride floats; the tasks of all layers share the grid.
+// Several layers decoded with one one-layer plan (task_layers > 1): the tasks
+// of layer i read partials at item index i * part_lstride + item; the tasks of
+// all layers share the grid.  A layered plan (task_layers = 1) holds every
+// layer's items in one list, and each item carries its layer offset.  Entry
+// b's output / lse of layer offset l sit at + l * out_lstride / lse_lstride
+// floats, and its item range at plan entry l * plan_n + b.
 constexpr int COMBINE_WARPS = 4;
 __global__ void __launch_bounds__(32 * COMBINE_WARPS) k_combine(uint32_t H, uint32_t ws_heads,
                                                                 const uint32_t* __restrict__ meta,
@@ -487,26 +499,29 @@ __global__ void __launch_bounds__(32 * COMBINE_WARPS) k_combine(uint32_t H, uint
                                                                 const float* __restrict__ part_o_all,
                                                                 const float* __restrict__ part_ml_all,
                                                                 float* __restrict__ out_all, float* __restrict__ lse_all,
-                                                                uint32_t n_layers_call, uint64_t part_lstride,
-                                                                uint64_t out_lstride, uint64_t lse_lstride) {
+                                                                uint32_t task_layers, uint32_t plan_n,
+                                                                uint64_t part_lstride, uint64_t out_lstride,
+                                                                uint64_t lse_lstride) {
   kvcu_pdl_wait();     // launched programmatically after the decode kernel
   kvcu_pdl_trigger();  // the next layer's append may start launching
   const uint32_t n_items = meta[0], G = meta[1];
   const uint32_t lane = threadIdx.x & 31u;
   const uint32_t per_layer = G > 1 ? (G - 1) * H : 0u;
-  const uint32_t tasks = per_layer * n_layers_call;
+  const uint32_t tasks = per_layer * task_layers;
   for (uint32_t t = blockIdx.x * COMBINE_WARPS + (threadIdx.x >> 5); t < tasks;
        t += gridDim.x * COMBINE_WARPS) {
-    const uint32_t li = t / per_layer, tl = t - li * per_layer;
-    const float* part_o = part_o_all + li * part_lstride * ws_heads * R;
-    const float* part_ml = part_ml_all + li * part_lstride * ws_heads * 2;
-    float* out = out_all + li * out_lstride;
-    float* lse = lse_all ? lse_all + li * lse_lstride : nullptr;
+    const uint32_t lt = t / per_layer, tl = t - lt * per_layer;
+    const float* part_o = part_o_all + lt * part_lstride * ws_heads * R;
+    const float* part_ml = part_ml_all + lt * part_lstride * ws_heads * 2;
     const uint32_t c = 1 + tl / H, h = tl % H;
     const uint32_t i = ranges[c];
     if (i == 0 || i >= n_items) continue;
-    const uint32_t b = items[i].b;
-    const uint32_t cnt = seq_count[b], first = seq_first[b];
+    const kvcu_item ki = items[i];
+    const uint32_t b = ki.b, li = lt + ki.layer;
+    float* out = out_all + li * out_lstride;
+    float* lse = lse_all ? lse_all + li * lse_lstride : nullptr;
+    const uint32_t e = ki.layer * plan_n + b;
+    const uint32_t cnt = seq_count[e], first = seq_first[e];
     if (cnt <= 1 || first + 1 != i) continue;  // no split here, or not the entry's first cut
     float m = -INFINITY;
     for (uint32_t k = 0; k < cnt; ++k) m = fmaxf(m, part_ml[((uint64_t)(first + k) * ws_heads + h) * 2]);
@@ -539,12 +554,14 @@ __global__ void __launch_bounds__(32 * COMBINE_WARPS) k_combine(uint32_t H, uint
   }
 }
 
-int launch_combine(kvcu_decode_ws* ws, uint32_t n_heads, float* out, float* lse, cudaStream_t st,
+int launch_combine(kvcu_decode_ws* ws, uint32_t n_heads, uint32_t n, float* out, float* lse, cudaStream_t st,
                    uint32_t n_layers_call = 1, uint64_t out_lstride = 0, uint64_t lse_lstride = 0) {
   // the plan makes at most min(max_ranges, decode CTAs) ranges
   uint32_t G = ws->max_ranges;
   if (ws->decode_ctas > 0 && (uint32_t)ws->decode_ctas < G) G = (uint32_t)ws->decode_ctas;
-  const uint32_t tasks = (G > 1 ? G - 1 : 1) * n_heads * n_layers_call;
+  // a layered plan's cuts already cover every layer
+  const uint32_t task_layers = ws->plan_layers > 1 ? 1u : n_layers_call;
+  const uint32_t tasks = (G > 1 ? G - 1 : 1) * n_heads * task_layers;
   uint32_t grid = (tasks + COMBINE_WARPS - 1) / COMBINE_WARPS;
   const uint32_t cap = 8u * (uint32_t)(ws->num_sms > 0 ? ws->num_sms : 148);
   if (grid > cap) grid = cap;
@@ -553,7 +570,7 @@ int launch_combine(kvcu_decode_ws* ws, uint32_t n_heads, float* out, float* lse,
                                          ws->max_heads, (const uint32_t*)ws->meta, (const uint32_t*)ws->ranges,
                                          (const kvcu_item*)ws->items, (const uint32_t*)ws->seq_first,
                                          (const uint32_t*)ws->seq_count, (const float*)ws->part_o,
-                                         (const float*)ws->part_ml, out, lse, n_layers_call,
+                                         (const float*)ws->part_ml, out, lse, task_layers, n,
                                          (uint64_t)ws->max_items, out_lstride, lse_lstride),
                          "combine kernel launch");
 }
@@ -607,26 +624,47 @@ int kvcu_launch_plan(kvcu_decode_ws* ws, const kvcu_pool* p, uint32_t n, const u
   return kvcu_launch_plan_target(ws, p, n, seq_ids, n_seqs, lens, (uint32_t)ws->decode_ctas, st, entry_lens);
 }
 
-// The plan with at most `ranges` CTA ranges. It makes at most n + ranges - 1
-// items, so ws->max_items >= n + ranges keeps every item; the decode grid
-// (ws->decode_ctas) must be >= ranges.
+// The plan with at most `ranges` CTA ranges. It makes at most n * n_layers +
+// ranges - 1 items, so ws->max_items >= n + ranges per layer keeps every item;
+// the decode grid (ws->decode_ctas) must be >= ranges.  n_layers > 1 (a
+// layered plan) needs ws->max_layers >= n_layers: the items, the per-entry
+// ranges and the partials then use the room of that many layers.
 int kvcu_launch_plan_target(kvcu_decode_ws* ws, const kvcu_pool* p, uint32_t n,
                             const uint32_t* seq_ids, uint32_t n_seqs, const uint32_t* lens,
-                            uint32_t ranges, cudaStream_t st, const uint32_t* entry_lens) {
+                            uint32_t ranges, cudaStream_t st, const uint32_t* entry_lens, uint32_t n_layers) {
+  if (n_layers < 1 || (n_layers > 1 && n_layers > ws->max_layers)) {
+    kvcu_set_error("decode plan: %u layers, the workspace holds %u", n_layers, ws->max_layers);
+    return KVCU_ERR_INVALID_ARG;
+  }
   const uint32_t align = p->block_size > 128u ? p->block_size : 128u;
   if (ranges > ws->max_ranges) ranges = ws->max_ranges;
   if (ranges > (uint32_t)ws->decode_ctas) ranges = (uint32_t)ws->decode_ctas;
   if (ranges < 1) ranges = 1;
   ws->entry_lens = entry_lens;  // the decodes that use this plan read the same per-entry lengths
-  k_plan<<<1, 1024, 0, st>>>(n, seq_ids, n_seqs, lens, entry_lens, ranges, align, ws->max_items, ws->items,
-                             ws->meta, ws->ranges, ws->seq_first, ws->seq_count);
-  return kvcu_check_cuda(cudaGetLastError(), "plan kernel launch");
+  k_plan<<<1, 1024, 0, st>>>(n, n_layers, seq_ids, n_seqs, lens, entry_lens, ranges, align,
+                             ws->max_items * n_layers, ws->items, ws->meta, ws->ranges, ws->seq_first,
+                             ws->seq_count);
+  const int rc = kvcu_check_cuda(cudaGetLastError(), "plan kernel launch");
+  // after a failed launch the device holds an older plan of unknown shape: no
+  // decode may use it until a plan succeeds
+  ws->plan_layers = rc ? 0xFFFFFFFFu : n_layers;
+  return rc;
+}
+
+bool kvcu_decode_layers_fused(const kvcu_decode_ws* ws, const kvcu_pool* p, uint32_t n, uint32_t n_heads) {
+  return kvcu_decode_tc_supported(p, n_heads) && n_heads <= ws->max_heads && n <= ws->max_batch &&
+         ws->impl != KVCU_DECODE_CUDA_CORE;
 }
 
 int kvcu_launch_decode(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint32_t n,
                        const uint32_t* seq_ids, uint32_t n_seqs, const uint32_t* toff,
                        const uint32_t* tables, const uint32_t* lens, const float* q,
                        uint32_t n_heads, float scale, float* out, float* lse, cudaStream_t st) {
+  if (ws->plan_layers > 1) {
+    kvcu_set_error("mla_decode: the workspace's plan covers %u layers as one list; a one-layer decode "
+                   "needs kvcu_decode_plan", ws->plan_layers);
+    return KVCU_ERR_INVALID_ARG;
+  }
   const bool tc_ok = kvcu_decode_tc_supported(p, n_heads) && n_heads <= ws->max_heads &&
                      n <= ws->max_batch;
   if (ws->impl == KVCU_DECODE_TENSOR_CORE && !tc_ok) {
@@ -640,7 +678,7 @@ int kvcu_launch_decode(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint32_
     int rc = kvcu_launch_decode_tc(ws, p, layer, 1, n, seq_ids, n_seqs, toff, tables, lens, q, 0, n_heads,
                                    scale, out, 0, lse, 0, st);
     if (rc) return rc;
-    rc = launch_combine(ws, n_heads, out, lse, st);
+    rc = launch_combine(ws, n_heads, n, out, lse, st);
     if (rc) return rc;
     ws->last_launches = 2;
     ws->last_impl = KVCU_DECODE_TENSOR_CORE;
@@ -694,7 +732,7 @@ int kvcu_launch_decode(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint32_
   a.entry_lens = ws->entry_lens;
   int rc = p->quantized ? launch_decode_q<true>(ws, a, st) : launch_decode_q<false>(ws, a, st);
   if (rc) return rc;
-  rc = launch_combine(ws, n_heads, out, lse, st);
+  rc = launch_combine(ws, n_heads, n, out, lse, st);
   if (rc) return rc;
   ws->last_launches = 2;
   return KVCU_OK;
@@ -709,15 +747,21 @@ int kvcu_launch_decode_layers(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, 
     kvcu_set_error("mla_decode: %u layers in one call, the workspace holds %u", n_layers_call, ws->max_layers);
     return KVCU_ERR_INVALID_ARG;
   }
-  const bool tc_ok = kvcu_decode_tc_supported(p, n_heads) && n_heads <= ws->max_heads && n <= ws->max_batch;
-  if (n_layers_call > 1 && tc_ok && ws->impl != KVCU_DECODE_CUDA_CORE) {
-    // one persistent launch for all layers: every CTA runs its plan range once per layer
+  const bool fused = kvcu_decode_layers_fused(ws, p, n, n_heads);
+  if (ws->plan_layers > 1 && (ws->plan_layers != n_layers_call || !fused)) {
+    kvcu_set_error("mla_decode: the workspace's plan covers %u layers as one list, the call %u layers%s",
+                   ws->plan_layers, n_layers_call, fused ? "" : " on the CUDA-core path (one-layer plans only)");
+    return KVCU_ERR_INVALID_ARG;
+  }
+  if (n_layers_call > 1 && fused) {
+    // one persistent launch for all layers: every CTA runs its plan range once
+    // per layer, or once in all with a layered plan
     ws->last_launches = 0;
     if (n == 0) return KVCU_OK;
     int rc = kvcu_launch_decode_tc(ws, p, layer, n_layers_call, n, seq_ids, n_seqs, toff, tables, lens, q,
                                    q_lstride, n_heads, scale, out, out_lstride, lse, lse_lstride, st);
     if (rc) return rc;
-    rc = launch_combine(ws, n_heads, out, lse, st, n_layers_call, out_lstride, lse_lstride);
+    rc = launch_combine(ws, n_heads, n, out, lse, st, n_layers_call, out_lstride, lse_lstride);
     if (rc) return rc;
     ws->last_launches = 2;
     ws->last_impl = KVCU_DECODE_TENSOR_CORE;

@@ -134,10 +134,13 @@ struct TcArgs {
   float* part_ml;
   uint32_t ws_heads;
   float* lse;  // optional [n][H] log-sum-exp (natural log) of single-item entries
-  // Layers [layer, layer + n_layers_call) in one launch, all with the same plan:
-  // layer layer+i reads q + i*q_lstride and writes out + i*out_lstride (floats),
-  // its partials at item index i*part_lstride + item, its lse at + i*lse_lstride.
-  uint32_t n_layers_call;
+  // Layers [layer, layer + n_layers_call) in one launch: layer layer+i reads
+  // q + i*q_lstride and writes out + i*out_lstride (floats), its lse at
+  // + i*lse_lstride.  A one-layer plan runs once per layer (unit_layers =
+  // n_layers_call), layer i's partials at item index i*part_lstride + item; a
+  // layered plan runs once (unit_layers = 1), each item carrying its layer
+  // offset, and plan entry layer*n + b holds entry b's item count.
+  uint32_t n_layers_call, unit_layers;
   uint64_t q_lstride, out_lstride, part_lstride, lse_lstride;
   const uint32_t* entry_lens;  // optional per-entry attended length (capped by lens[seq]); from the plan
   long long wait_limit;        // clocks a bounded wait may take before the CTA gives up
@@ -145,13 +148,14 @@ struct TcArgs {
 };
 
 // Work unit u of a CTA whose plan range holds `cnt` items from `it_begin`:
-// layer offset li = u / cnt, item it_begin + u % cnt (layer-major, so each
-// layer's items run in plan order).
+// repeat li = u / cnt, item it_begin + u % cnt (layer-major, so each layer's
+// items run in plan order).  With a layered plan there is one repeat (li = 0)
+// and the item gives the layer.
 struct Unit {
   uint32_t li, it;
 };
 __device__ __forceinline__ Unit unit_of(uint32_t u, uint32_t it_begin, uint32_t cnt) {
-  const uint32_t li = u / cnt;  // callers only ask for u < n_layers_call * cnt, so cnt > 0
+  const uint32_t li = u / cnt;  // callers only ask for u < unit_layers * cnt, so cnt > 0
   return Unit{li, it_begin + (u - li * cnt)};
 }
 
@@ -305,12 +309,16 @@ __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a, uint64_t b,
 struct Item {
   uint32_t b, s, t0, t1, tok0, tok1;  // entry, sequence, table range, token range
   uint32_t ntiles;
+  uint32_t li;  // layer offset from the call's first layer
+  uint32_t e;   // plan entry (item count in seq_count)
 };
 
-__device__ __forceinline__ Item load_item(const TcArgs& a, uint32_t it) {
-  const kvcu_item ki = a.items[it];
+__device__ __forceinline__ Item load_item(const TcArgs& a, const Unit& un) {
+  const kvcu_item ki = a.items[un.it];
   Item r;
   r.b = ki.b;
+  r.li = un.li + ki.layer;
+  r.e = ki.layer * a.n + ki.b;
   r.s = a.seq_ids ? a.seq_ids[ki.b] : ki.b;
   r.t0 = r.t1 = 0;
   uint32_t len = 0;
@@ -390,7 +398,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const uint32_t it_begin = blockIdx.x < n_ranges ? min(a.ranges[blockIdx.x], n_items) : n_items;
   const uint32_t it_end = blockIdx.x < n_ranges ? min(a.ranges[blockIdx.x + 1], n_items) : n_items;
   const uint32_t cnt = it_end > it_begin ? it_end - it_begin : 0u;
-  const uint32_t n_units = cnt * a.n_layers_call;
+  const uint32_t n_units = cnt * a.unit_layers;
   if (blockIdx.x == 0 && threadIdx.x == 0 && n_ranges > gridDim.x) atomicOr(a.status, KVCU_STATUS_BAD_PLAN);
   if (threadIdx.x == 0) *reinterpret_cast<volatile uint32_t*>(smem + OFF_CUR_ITEM) = 0u;
   tc_fence_before();
@@ -427,9 +435,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
       };
       for (uint32_t u = 0; u < n_units && live; ++u) {
-        const Unit un = unit_of(u, it_begin, cnt);
-        const Item im = load_item(a, un.it);
-        const uint64_t layer = (uint64_t)a.layer + un.li;
+        const Item im = load_item(a, unit_of(u, it_begin, cnt));
+        const uint64_t layer = (uint64_t)a.layer + im.li;
         for (uint32_t k = 0; k < im.ntiles && live; ++k) {
           const uint32_t s = g & 1u;
           const uint32_t tt0 = im.tok0 + k * TILE;
@@ -440,10 +447,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             prefetch_tile(im, layer, k + 1);
           } else {
             for (uint32_t u2 = u + 1; u2 < n_units && u2 < u + 4; ++u2) {
-              const Unit un2 = unit_of(u2, it_begin, cnt);
-              const Item im2 = load_item(a, un2.it);
+              const Item im2 = load_item(a, unit_of(u2, it_begin, cnt));
               if (im2.ntiles) {
-                prefetch_tile(im2, (uint64_t)a.layer + un2.li, 0);
+                prefetch_tile(im2, (uint64_t)a.layer + im2.li, 0);
                 break;
               }
             }
@@ -498,7 +504,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     uint32_t g = 0, item_no = 0;
     bool ok = true;
     for (uint32_t u = 0; u < n_units && ok; ++u) {
-      const Item im = load_item(a, unit_of(u, it_begin, cnt).it);
+      const Item im = load_item(a, unit_of(u, it_begin, cnt));
       if (im.ntiles == 0) continue;
       if (!mbar_wait_warp(bar(B_Q_FULL), item_no & 1u, abort_flag, a.status)) break;
       tc_fence_after();
@@ -551,7 +557,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     bool ok = true;
     const uint64_t ones_desc = smem_desc(sbase + OFF_ONES, 0, 0, LAYOUT_NONE);
     for (uint32_t u = 0; u < n_units && ok; ++u) {
-      const Item im = load_item(a, unit_of(u, it_begin, cnt).it);
+      const Item im = load_item(a, unit_of(u, it_begin, cnt));
       if (im.ntiles == 0) continue;
       for (uint32_t k = 0; k < im.ntiles && ok; ++k, ++g) {
         if (k == 0 && item_ord > 0) {
@@ -620,10 +626,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         __nanosleep(256);
       }
       if (!go) break;
-      const Unit un = unit_of(nx, it_begin, cnt);
-      const Item im = load_item(a, un.it);
+      const Item im = load_item(a, unit_of(nx, it_begin, cnt));
       if (im.ntiles == 0) continue;
-      const uint8_t* qb = reinterpret_cast<const uint8_t*>(a.q + un.li * a.q_lstride + (uint64_t)im.b * H * W);
+      const uint8_t* qb = reinterpret_cast<const uint8_t*>(a.q + im.li * a.q_lstride + (uint64_t)im.b * H * W);
       for (uint32_t off = lane * 128u; off < H * (uint32_t)W * 4u; off += 32u * 128u) prefetch_l2_keep(qb + off);
     }
   }
@@ -654,8 +659,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     // query is staged as soon as this item's last P is out (its QK MMAs are all
     // done then), so the next item's first QK overlaps this item's drain.
     uint32_t staged_u = 0xFFFFFFFFu;
-    auto stage_q = [&](const Unit& su, const Item& si) -> bool {
-      const float* qb = a.q + su.li * a.q_lstride + (uint64_t)si.b * H * W;
+    auto stage_q = [&](const Item& si) -> bool {
+      const float* qb = a.q + si.li * a.q_lstride + (uint64_t)si.b * H * W;
       for (uint32_t hl = ew & 3u; hl < (uint32_t)HH; hl += 4) {
         const uint32_t h = h0 + hl;
         float amax = 0.f;
@@ -701,28 +706,28 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     for (uint32_t u = 0; u < n_units && ok; ++u) {
       if (ew == 0 && lane == 0) *cur_item = u;
       const Unit un = unit_of(u, it_begin, cnt);
-      const Item im = load_item(a, un.it);
-      const bool single = a.seq_count[im.b] == 1;
-      // this unit's layer: its output, partial slot (item index) and lse
-      float* const out_l = a.out + un.li * a.out_lstride;
+      const Item im = load_item(a, un);
+      const bool single = a.seq_count[im.e] == 1;
+      // this unit's partial slot (item index); its output rows and lse, those
+      // of entry b in layer offset im.li, are addressed where they are written
+      // (a pointer formed here would stay live across the item and spill)
       const uint64_t pit = un.li * a.part_lstride + un.it;
-      float* const lse_l = a.lse ? a.lse + un.li * a.lse_lstride : nullptr;
       if (im.ntiles == 0) {
         // empty item: zeros, or an empty partial
         for (uint32_t i = ew * 32 + lane; i < H * (uint32_t)R; i += 32 * EPI_WARPS) {
           const uint32_t h = i / R, c = i % R;
-          if (single) out_l[((uint64_t)im.b * H + h) * R + c] = 0.f;
+          if (single) a.out[im.li * a.out_lstride + ((uint64_t)im.b * H + h) * R + c] = 0.f;
           else a.part_o[(pit * a.ws_heads + h) * R + c] = 0.f;
         }
         if (!single && ew == 0 && lane < H) {
           a.part_ml[(pit * a.ws_heads + lane) * 2 + 0] = -INFINITY;
           a.part_ml[(pit * a.ws_heads + lane) * 2 + 1] = 0.f;
         }
-        if (single && lse_l && ew == 0 && lane < H) lse_l[(uint64_t)im.b * H + lane] = -INFINITY;
+        if (single && a.lse && ew == 0 && lane < H) a.lse[im.li * a.lse_lstride + (uint64_t)im.b * H + lane] = -INFINITY;
         continue;
       }
       if (staged_u != u) {
-        if (!stage_q(un, im)) {
+        if (!stage_q(im)) {
           ok = false;
           break;
         }
@@ -930,10 +935,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       }
       if (!ok) break;
       for (uint32_t u2 = u + 1; u2 < n_units; ++u2) {
-        const Unit un2 = unit_of(u2, it_begin, cnt);
-        const Item im2 = load_item(a, un2.it);
+        const Item im2 = load_item(a, unit_of(u2, it_begin, cnt));
         if (im2.ntiles == 0) continue;
-        if (!stage_q(un2, im2)) ok = false;
+        if (!stage_q(im2)) ok = false;
         staged_u = u2;
         break;
       }
@@ -964,7 +968,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const uint32_t hg = h0 + h;
             if (hg >= H) continue;
             const float v = __uint_as_float(o[h]);
-            if (single) out_l[((uint64_t)im.b * H + hg) * R + c] = ltot[h] > 0.f ? v / ltot[h] : 0.f;
+            if (single) a.out[im.li * a.out_lstride + ((uint64_t)im.b * H + hg) * R + c] = ltot[h] > 0.f ? v / ltot[h] : 0.f;
             else a.part_o[(pit * a.ws_heads + hg) * R + c] = v;
           }
         }
@@ -979,7 +983,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           a.part_ml[(pit * a.ws_heads + h0 + lane) * 2 + 0] = mh * 0.69314718055994531f;
           a.part_ml[(pit * a.ws_heads + h0 + lane) * 2 + 1] = lh;
         }
-        if (single && lse_l && q4 == 0 && lane < HH && h0 + lane < H) {
+        if (single && a.lse && q4 == 0 && lane < HH && h0 + lane < H) {
           float lh = 0.f, mh = 0.f;
 #pragma unroll
           for (int h = 0; h < HH; ++h)
@@ -988,7 +992,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
               mh = mref[h];
             }
           // mref is in log2 units of the scaled score, l = sum 2^(s - mref)
-          lse_l[(uint64_t)im.b * H + h0 + lane] = lh > 0.f ? (mh + log2f(lh)) * 0.69314718055994531f : -INFINITY;
+          a.lse[im.li * a.lse_lstride + (uint64_t)im.b * H + h0 + lane] = lh > 0.f ? (mh + log2f(lh)) * 0.69314718055994531f : -INFINITY;
         }
         tc_fence_before();
         __syncwarp();
@@ -1005,7 +1009,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     uint32_t g = 0;
     bool ok = true;
     for (uint32_t u = 0; u < n_units && ok; ++u) {
-      const Item im = load_item(a, unit_of(u, it_begin, cnt).it);
+      const Item im = load_item(a, unit_of(u, it_begin, cnt));
       for (uint32_t k = 0; k < im.ntiles && ok; ++k, ++g) {
         const uint32_t s = g & 1u;
         const uint32_t tt0 = im.tok0 + k * TILE;
@@ -1223,6 +1227,7 @@ int kvcu_launch_decode_tc(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint
   a.ws_heads = ws->max_heads;
   a.lse = lse;
   a.n_layers_call = n_layers_call;
+  a.unit_layers = ws->plan_layers > 1 ? 1u : n_layers_call;  // a layered plan already lists every layer
   a.q_lstride = q_lstride;
   a.out_lstride = out_lstride;
   a.part_lstride = ws->max_items;

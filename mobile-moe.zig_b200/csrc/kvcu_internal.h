@@ -24,22 +24,29 @@ struct kvcu_pool {
   uint64_t rows() const { return (uint64_t)n_layers * num_blocks * block_size; }
 };
 
-// Split-KV work item: batch entry b, tokens [start, end).
+// Split-KV work item: batch entry b, tokens [start, end), of layer offset
+// `layer` (always 0 in a one-layer plan; in a layered plan, the offset from the
+// decode call's first layer).
 struct kvcu_item {
-  uint32_t b, start, end, pad;
+  uint32_t b, start, end, layer;
 };
 
 struct kvcu_decode_ws {
   int device;
   uint32_t max_batch, max_heads, max_items, max_ranges;
   uint32_t max_layers;       // layers one multi-layer decode may cover (partials per layer)
-  kvcu_item* items;          // [max_items]
+  kvcu_item* items;          // [max_layers * max_items]
   uint32_t* meta;            // [0] n_items, [1] CTA ranges G
   uint32_t* ranges;          // [max_ranges + 1] first item of each CTA range
-  uint32_t* seq_first;       // [max_batch] first item of entry b
-  uint32_t* seq_count;       // [max_batch] items of entry b
+  uint32_t* seq_first;       // [max_layers * max_batch] first item of plan entry e
+  uint32_t* seq_count;       // [max_layers * max_batch] items of plan entry e
   float* part_o;             // [max_layers][max_items][max_heads][512]
   float* part_ml;            // [max_layers][max_items][max_heads][2] (m, l)
+  // Layers the last plan balances as one list (plan entry e = layer * n + b,
+  // n the batch): 1 for a one-layer plan, which a multi-layer decode repeats
+  // for every layer; L > 1 for kvcu_decode_plan_layers, valid only for a
+  // multi-layer decode of exactly L layers.
+  uint32_t plan_layers;
   const uint32_t* entry_lens;  // per-entry lengths of the last plan (device; nullptr: whole sequences)
   uint64_t wait_limit;         // clocks a bounded device wait may take (0: the default, ~2^31)
   uint32_t withhold_plus1;     // test hook: 0, or 1 + the tile whose first slice the producer withholds
@@ -125,7 +132,11 @@ int kvcu_launch_plan(kvcu_decode_ws* ws, const kvcu_pool* p, uint32_t n, const u
                      uint32_t n_seqs, const uint32_t* lens, cudaStream_t st, const uint32_t* entry_lens = nullptr);
 int kvcu_launch_plan_target(kvcu_decode_ws* ws, const kvcu_pool* p, uint32_t n,
                             const uint32_t* seq_ids, uint32_t n_seqs, const uint32_t* lens,
-                            uint32_t target, cudaStream_t st, const uint32_t* entry_lens = nullptr);
+                            uint32_t target, cudaStream_t st, const uint32_t* entry_lens = nullptr,
+                            uint32_t n_layers = 1);
+// Whether a multi-layer decode of this batch runs as one tensor-core launch,
+// the only form a layered plan (n_layers > 1) serves.
+bool kvcu_decode_layers_fused(const kvcu_decode_ws* ws, const kvcu_pool* p, uint32_t n, uint32_t n_heads);
 // ---- checkpoint bytes through a caller-owned device staging buffer (kvcu_api.cu) ----
 int kvcu_pool_read_checkpoint_staged(kvcu_pool* p, uint64_t offset, uint64_t nbytes, void* host_dst,
                                      cudaStream_t st, uint8_t* staging, uint64_t staging_bytes);
@@ -158,8 +169,10 @@ int kvcu_noalloc_prepare(int device);
 // ---- tensor-core decode (kvcu_decode_tc.cu) ----
 bool kvcu_decode_tc_supported(const kvcu_pool* p, uint32_t n_heads);
 // Layers [layer, layer + n_layers_call) with one plan: q / out / lse of layer
-// layer+i at + i * its stride (floats); partials of layer i at item index
-// i * ws->max_items + item (ws->max_layers >= n_layers_call).
+// layer+i at + i * its stride (floats).  With a one-layer plan the partials of
+// layer i sit at item index i * ws->max_items + item (ws->max_layers >=
+// n_layers_call); a layered plan of n_layers_call layers numbers its items
+// across all layers, and each item's partials sit at its own index.
 int kvcu_launch_decode_tc(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint32_t n_layers_call, uint32_t n,
                           const uint32_t* seq_ids, uint32_t n_seqs, const uint32_t* toff,
                           const uint32_t* tables, const uint32_t* lens, const float* q, uint64_t q_lstride,
@@ -173,7 +186,7 @@ int kvcu_launch_decode(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint32_
                        uint32_t n_heads, float scale, float* out, float* lse, cudaStream_t st);
 // Several layers with one plan (strides in floats between consecutive layers'
 // q, out and lse); one decode launch and one combine launch on the tensor-core
-// path, a launch pair per layer on the CUDA-core path.
+// path, a launch pair per layer on the CUDA-core path (one-layer plans only).
 int kvcu_launch_decode_layers(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint32_t n_layers_call,
                               uint32_t n, const uint32_t* seq_ids, uint32_t n_seqs,
                               const uint32_t* table_offsets, const uint32_t* tables, const uint32_t* lens,

@@ -76,6 +76,7 @@ _SIGS = {
     "kvcu_decode_ws_destroy": (_i32, [_vp]),
     "kvcu_decode_plan": (_i32, [_vp, _vp, _u32, _vp, _u32, _vp, _vp]),
     "kvcu_decode_plan_causal": (_i32, [_vp, _vp, _u32, _vp, _u32, _vp, _vp, _vp]),
+    "kvcu_decode_plan_layers": (_i32, [_vp, _vp, _u32, _vp, _u32, _vp, _u32, _vp]),
     "kvcu_mla_decode": (_i32, [_vp, _vp, _u32, _u32, _vp, _u32, _vp, _vp, _vp, _vp, _u32, _f32, _vp, _vp]),
     "kvcu_mla_decode_lse": (_i32, [_vp, _vp, _u32, _u32, _vp, _u32, _vp, _vp, _vp, _vp, _u32, _f32, _vp, _vp,
                                    _vp]),
@@ -344,6 +345,12 @@ class DecodeWorkspace:
         n = n if n is not None else (seq_ids.numel() if seq_ids is not None else lens.numel())
         check(lib().kvcu_decode_plan(self._h, pool.handle, n, _dptr(seq_ids), lens.numel(), _dptr(lens),
                                      _stream(stream)), "kvcu_decode_plan")
+
+    def plan_layers(self, pool: DevicePool, lens, n_layers, seq_ids=None, n=None, stream=None):
+        """One plan for a decode_layers call of n_layers layers (all (layer, entry) pairs balanced as one list)."""
+        n = n if n is not None else (seq_ids.numel() if seq_ids is not None else lens.numel())
+        check(lib().kvcu_decode_plan_layers(self._h, pool.handle, n, _dptr(seq_ids), lens.numel(), _dptr(lens),
+                                            n_layers, _stream(stream)), "kvcu_decode_plan_layers")
 
     def decode(self, pool: DevicePool, layer, q, table_offsets, tables, lens, scale, out,
                seq_ids=None, stream=None):

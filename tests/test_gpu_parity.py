@@ -378,6 +378,35 @@ def test_decode_tensor_core_vs_cuda_core_same_data(kv, oracle):
     assert rel_err_rows(a, b) <= REL_TOL
 
 
+def test_decode_layers_layered_plan_against_the_oracle(kv, oracle, torch_mod):
+    """The multi-layer call of the kvcache mirror balances all (layer, entry)
+    pairs of the call as one list (a layered plan); every layer's output must
+    still match the oracle."""
+    torch = torch_mod
+    lens = [0, 1, 200, 1500, 4100, 9000, 130, 64]
+    nl, H, bs = 3, 20, 64
+    nb = sum((L + bs - 1) // bs for L in lens) + 3
+    c, o, _ = _multi_seq_cache(kv, oracle, lens, bs, nb, 91, True, 0.01, nl)
+    offs, tabs = [0], []
+    for s in range(len(lens)):
+        tabs.extend(c.seq_block_table(s))
+        offs.append(len(tabs))
+    offs, tabs = np.array(offs, np.uint32), np.array(tabs, np.uint32)
+    q = np.random.default_rng(92).standard_normal((nl, len(lens), H, W)).astype(np.float32)
+    ids = np.arange(len(lens), dtype=np.uint32)
+    q_dev = torch.from_numpy(q).cuda()
+    out_dev = torch.full((nl, len(lens), H, R), float("nan"), device="cuda")
+    c.mlaDecodeLayers_dev(0, ids, q_dev, SCALE, out_dev)
+    torch.cuda.synchronize()
+    got = out_dev.cpu().numpy()
+    assert c.pool().status() == 0
+    for layer in range(nl):
+        want = o.attention_batch(layer, offs, tabs, np.array(lens, np.uint32), q[layer], SCALE, n_threads=8)
+        err = rel_err_rows(got[layer], want)
+        assert err <= REL_TOL, (layer, err)
+        assert np.all(got[layer][0] == 0)  # the empty entry
+
+
 def test_decode_lazy_rescale_when_scores_jump(kv, oracle):
     """Scores that double from one 128-token tile to the next (a sawtooth of 4
     tiles, gains 1, 2, 4, 8) inside items of several tiles: the tensor-core
