@@ -911,7 +911,7 @@ def run_ours(args, rank, world, local_rank):
                           "work issued layer by layer"),
             "per_layer": per_layer,
             "roofline": {"kernel": (f"multi-layer decode call ({layers_per_launch} layers: k_decode_tc + k_combine, "
-                                    "k_decode_tc ~99.6% of the device time)"),
+                                    "k_decode_tc ~99.8% of the device time)"),
                          "layers_per_launch": layers_per_launch,
                          "bound": "hbm", "achieved": dec_gbs, "peak": peak, "unit": "GB/s",
                          "frac": dec_gbs / peak, "peak_source": peak_kind,
