@@ -116,6 +116,10 @@ __global__ void __launch_bounds__(NTHR, 1) k_head_gemm_tc(GemmArgs g) {
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + L::OFF_TMEM);
+  // programmatic launch: the set-up above overlaps the previous kernel's tail;
+  // A, B and the merge operands are read only after this wait
+  kvcu_pdl_wait();
+  kvcu_pdl_trigger();  // the next kernel may start its own set-up
   // kind::tf32: D f32 (bit 4), A and B TF32 (format 2 at bits 7 and 10), both
   // K-major, N >> 3 at bit 17, M >> 4 at bit 24
   constexpr uint32_t IDESC = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(NT >> 3) << 17) |
@@ -276,8 +280,8 @@ int launch(const GemmArgs& g, uint32_t heads, cudaStream_t st) {
                                nullptr);
   if (rc) return rc;
   const dim3 grid(g.N / NT, (g.M + TM - 1) / TM, heads);
-  k_head_gemm_tc<NT, TRANS_B><<<grid, NTHR, Layout<NT>::ALLOC, st>>>(g);
-  return kvcu_check_cuda(cudaGetLastError(), "head_gemm_tc launch");
+  return kvcu_check_cuda(kvcu_launch_pdl(k_head_gemm_tc<NT, TRANS_B>, grid, dim3(NTHR), Layout<NT>::ALLOC, st, g),
+                         "head_gemm_tc launch");
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }

@@ -46,6 +46,8 @@ __global__ void __launch_bounds__(ROWS_THREADS)
                const float* __restrict__ norm_w, float eps, float rope_base, float* __restrict__ q_abs,
                float* __restrict__ rows) {
   __shared__ float red[ROWS_THREADS / 32];
+  kvcu_pdl_wait();     // launched programmatically: the previous kernel may still be finishing
+  kvcu_pdl_trigger();  // the k_b product may start its set-up
   const uint32_t b = blockIdx.x, tid = threadIdx.x;
   const float* x = kv_a + (uint64_t)b * (R + P);
   float* row = rows + (uint64_t)b * (R + P);
@@ -210,6 +212,8 @@ __global__ void __launch_bounds__(MERGE_THREADS)
                   const float* __restrict__ rows, const float* __restrict__ lse, float scale,
                   float* __restrict__ w) {
   extern __shared__ float msh[];  // [R] latent of the newest token, then [P] its k_pe
+  kvcu_pdl_wait();     // launched programmatically after the decode's combine
+  kvcu_pdl_trigger();  // the v_b product may start its set-up
   float* cs = msh;
   float* kpe = msh + R;
   const uint32_t b = blockIdx.x, tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
@@ -260,6 +264,8 @@ __global__ void __launch_bounds__(MERGE_THREADS)
 __global__ void __launch_bounds__(MERGE_THREADS)
     k_mla_merge_apply(uint32_t H, uint32_t R, uint32_t P, const float* __restrict__ rows, const float* __restrict__ w,
                       float* __restrict__ latent) {
+  kvcu_pdl_wait();  // launched programmatically after the weights kernel
+  kvcu_pdl_trigger();
   const uint32_t b = blockIdx.x / H, h = blockIdx.x % H;
   const float* row = rows + (uint64_t)b * (R + P);
   const float* wr = w + ((uint64_t)b * H + h) * 3;
@@ -358,9 +364,9 @@ extern "C" int kvcu_mla_prepare(kvcu_pool* pool, uint32_t n, uint32_t n_heads, u
   if (d.rc) return d.rc;
   const uint32_t R = pool->kv_rank, P = pool->rope_dim;
   const cudaStream_t st = (cudaStream_t)stream;
-  k_mla_rows<<<n, ROWS_THREADS, 0, st>>>(n_heads, qk_nope, R, P, q, kv_a, positions, norm_w, eps, rope_base,
-                                         q_abs, rows);
-  int rc = kvcu_check_cuda(cudaGetLastError(), "mla rows launch");
+  int rc = kvcu_check_cuda(kvcu_launch_pdl(k_mla_rows, dim3(n), dim3(ROWS_THREADS), 0, st, n_heads, qk_nope, R, P,
+                                           q, kv_a, positions, norm_w, eps, rope_base, q_abs, rows),
+                           "mla rows launch");
   if (rc) return rc;
   // q_abs[b][h][0:R] = q_nope[b][h] (n x qk_nope) x k_b_h (qk_nope x R)
   return launch_head_gemm<false>(n_heads, n, R, qk_nope, q, n_heads * (qk_nope + P), qk_nope + P, k_b, R,
@@ -407,16 +413,17 @@ int kvcu_mla_finish_fused(kvcu_pool* pool, uint32_t n, uint32_t n_heads, uint32_
   const uint32_t R = pool->kv_rank, P = pool->rope_dim;
   if ((uint64_t)(R + P) * sizeof(float) > 48u * 1024u)  // the weights kernel's shared latent and k_pe
     return kvcu_mla_finish(pool, n, n_heads, v_dim, q_abs, rows, latent, lse, scale, v_b, attn, st);
-  k_mla_merge_w<<<n, MERGE_THREADS, (R + P) * sizeof(float), st>>>(n_heads, R, P, pool->quantized ? 1 : 0, q_abs,
-                                                                    rows, lse, scale, w);
-  int rc = kvcu_check_cuda(cudaGetLastError(), "mla merge launch");
+  int rc = kvcu_check_cuda(kvcu_launch_pdl(k_mla_merge_w, dim3(n), dim3(MERGE_THREADS), (R + P) * sizeof(float), st,
+                                           n_heads, R, P, pool->quantized ? 1 : 0, q_abs, rows, lse, scale, w),
+                           "mla merge launch");
   if (rc) return rc;
   const kvcu_gemm_merge mrg{rows, R + P, w};
   rc = kvcu_launch_head_gemm_tc(true, n_heads, n, v_dim, R, latent, n_heads * R, R, v_b, R, (uint64_t)v_dim * R,
                                 attn, n_heads * v_dim, v_dim, pool->status, st, &mrg);
   if (rc != KVCU_ERR_UNSUPPORTED) return rc;
-  k_mla_merge_apply<<<n * n_heads, MERGE_THREADS, 0, st>>>(n_heads, R, P, rows, w, latent);
-  rc = kvcu_check_cuda(cudaGetLastError(), "mla merge launch");
+  rc = kvcu_check_cuda(kvcu_launch_pdl(k_mla_merge_apply, dim3(n * n_heads), dim3(MERGE_THREADS), 0, st, n_heads, R,
+                                       P, rows, w, latent),
+                       "mla merge launch");
   if (rc) return rc;
   return launch_head_gemm_cc<true>(n_heads, n, v_dim, R, latent, n_heads * R, R, v_b, R, (uint64_t)v_dim * R, attn,
                                    n_heads * v_dim, v_dim, st);
