@@ -200,7 +200,9 @@ int kvcu_decode_plan(kvcu_decode_ws* ws, const kvcu_pool* pool, uint32_t n, cons
  * the next kvcu_decode_plan drops it. */
 int kvcu_decode_plan_causal(kvcu_decode_ws* ws, const kvcu_pool* pool, uint32_t n, const uint32_t* seq_ids,
                             uint32_t n_seqs, const uint32_t* lens, const uint32_t* entry_lens, void* stream);
-/* Run decode for one layer with the last plan of `ws`. */
+/* Run decode for one layer with the last plan of `ws`.  The batch must be the
+ * one planned (the plan's items index seq_ids, q and out): an n other than the
+ * plan's returns KVCU_ERR_INVALID_ARG, as does a decode before any plan. */
 int kvcu_mla_decode(kvcu_decode_ws* ws, kvcu_pool* pool, uint32_t layer, uint32_t n,
                     const uint32_t* seq_ids, uint32_t n_seqs, const uint32_t* table_offsets,
                     const uint32_t* tables, const uint32_t* lens, const float* q,

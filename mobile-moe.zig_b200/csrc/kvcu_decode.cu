@@ -648,6 +648,7 @@ int kvcu_launch_plan_target(kvcu_decode_ws* ws, const kvcu_pool* p, uint32_t n,
   // after a failed launch the device holds an older plan of unknown shape: no
   // decode may use it until a plan succeeds
   ws->plan_layers = rc ? 0xFFFFFFFFu : n_layers;
+  ws->plan_n = rc ? 0xFFFFFFFFu : n;
   return rc;
 }
 
@@ -663,6 +664,10 @@ int kvcu_launch_decode(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, uint32_
   if (ws->plan_layers > 1) {
     kvcu_set_error("mla_decode: the workspace's plan covers %u layers as one list; a one-layer decode "
                    "needs kvcu_decode_plan", ws->plan_layers);
+    return KVCU_ERR_INVALID_ARG;
+  }
+  if (n && n != ws->plan_n) {
+    kvcu_set_error("mla_decode: batch of %u entries, the workspace's last plan covers %u", n, ws->plan_n);
     return KVCU_ERR_INVALID_ARG;
   }
   const bool tc_ok = kvcu_decode_tc_supported(p, n_heads) && n_heads <= ws->max_heads &&
@@ -745,6 +750,10 @@ int kvcu_launch_decode_layers(kvcu_decode_ws* ws, kvcu_pool* p, uint32_t layer, 
                               uint64_t out_lstride, float* lse, uint64_t lse_lstride, cudaStream_t st) {
   if (n_layers_call > ws->max_layers) {
     kvcu_set_error("mla_decode: %u layers in one call, the workspace holds %u", n_layers_call, ws->max_layers);
+    return KVCU_ERR_INVALID_ARG;
+  }
+  if (n && n != ws->plan_n) {
+    kvcu_set_error("mla_decode: batch of %u entries, the workspace's last plan covers %u", n, ws->plan_n);
     return KVCU_ERR_INVALID_ARG;
   }
   const bool fused = kvcu_decode_layers_fused(ws, p, n, n_heads);

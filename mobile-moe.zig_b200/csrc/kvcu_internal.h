@@ -47,6 +47,9 @@ struct kvcu_decode_ws {
   // for every layer; L > 1 for kvcu_decode_plan_layers, valid only for a
   // multi-layer decode of exactly L layers.
   uint32_t plan_layers;
+  // Entries per layer of the last plan: a decode must cover the same batch,
+  // since the plan's items index its seq_ids, q and out (~0 after a failed plan).
+  uint32_t plan_n;
   const uint32_t* entry_lens;  // per-entry lengths of the last plan (device; nullptr: whole sequences)
   uint64_t wait_limit;         // clocks a bounded device wait may take (0: the default, ~2^31)
   uint32_t withhold_plus1;     // test hook: 0, or 1 + the tile whose first slice the producer withholds

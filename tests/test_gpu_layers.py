@@ -136,6 +136,29 @@ def test_layered_plan_is_refused_on_the_cuda_core_path(kv):
     pool.close()
 
 
+def test_decode_refuses_a_batch_other_than_the_planned_one(kv):
+    import torch
+
+    lens = [100, 200, 300]
+    pool, toff, ttab = _pool(kv, torch, lens, 16, True, 2, 77)
+    lens_dev = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    ws = kv.DecodeWorkspace(0, 3, 8, max_layers=2)
+    q = torch.zeros((2, 3, 8, W), device="cuda")
+    out = torch.zeros((2, 3, 8, 512), device="cuda")
+    with pytest.raises(kv.KVCudaError):  # no plan yet
+        ws.decode(pool, 0, q[0], toff, ttab, lens_dev, SCALE, out[0])
+    ws.plan(pool, lens_dev)
+    with pytest.raises(kv.KVCudaError):  # two entries against a plan of three
+        ws.decode(pool, 0, q[0, :2].contiguous(), toff, ttab, lens_dev, SCALE, out[0, :2].contiguous())
+    with pytest.raises(kv.KVCudaError):
+        ws.decode_layers(pool, 0, q[:, :2].contiguous(), toff, ttab, lens_dev, SCALE, out[:, :2].contiguous())
+    ws.decode_layers(pool, 0, q, toff, ttab, lens_dev, SCALE, out)  # the planned batch
+    torch.cuda.synchronize()
+    assert pool.status() == 0
+    ws.close()
+    pool.close()
+
+
 def test_decode_layers_needs_a_workspace_with_room_for_the_layers(kv):
     import torch
 
